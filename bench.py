@@ -1,0 +1,350 @@
+#!/usr/bin/env python3
+"""Benchmark of the routed-expert NVFP4 slice (BASELINE.json metric: MoE-layer
+decode µs for 6 rows, and NVFP4 weight GB/s against the measured HBM peak).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one MoE layer over one batch: the routed-expert slice of every rank's
+column shard (N ranks split the 2304 intermediate columns contiguously), then the
+fixed-order FP32 combine of the per-rank BF16 partials on rank 0. Weights are
+seeded synthetic NVFP4 (BASELINE config 1/2 shapes: 384 experts, hidden 5120,
+intermediate 2304), resident in HBM; each step routes a different seeded draw
+over several resident layers, so the ~680 MB of expert weights a step reads
+exceeds the 126 MB L2.
+
+--impl reference times the reference's dequantize-and-matmul path restated on
+the host cores (the oracle), on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "qmesh-afd-tp3_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+HIDDEN = 5120
+INTER = 2304
+N_EXPERTS = 384
+TOPK = 6
+EXPERT_BYTES = 2 * INTER * (HIDDEN // 2 + HIDDEN // 16) + HIDDEN * (INTER // 2 + INTER // 16)  # 19,906,560
+METRIC = "MoE-layer decode µs (6 rows) & NVFP4 weight GB/s vs HBM peak, 1/2/4/8 GPU"
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.f = open(self.path, "w")
+            q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.is_file():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        busy = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(n_draws: int, rows: int, seed: int, n_experts: int):
+    """Seeded routing (softmax top-6 of N(0,1) logits) and FP8 activations per draw."""
+    from qmesh_b200.synth import make_activation, routing
+    gen = torch.Generator().manual_seed(seed)
+    draws = []
+    for _ in range(n_draws):
+        logits = torch.randn(rows, n_experts, generator=gen)
+        ids, tw = routing(logits, TOPK)
+        q, inv = make_activation(rows, gen)
+        draws.append((q, inv, ids, tw))
+    return draws
+
+
+def run_ours(args) -> dict | None:
+    import torch.distributed as dist
+    from qmesh_b200 import build
+    from qmesh_b200.arena import Arena
+    from qmesh_b200.combine import combine_ordered
+    from qmesh_b200.expert_slice import alloc_workspace, launch
+    build.build()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+    rows = args.rows
+    width = INTER // world
+    a0, a1 = rank * width, (rank + 1) * width
+    layers = args.layers
+    ar = Arena(dev, layers, N_EXPERTS, a0, a1)
+    ar.check_memory()
+    for li in range(layers):
+        ar.fill_synthetic(li, seed=1000 + li)
+    torch.cuda.synchronize()
+    draws = make_inputs(args.draws, rows, seed=1, n_experts=N_EXPERTS)
+    dq = [(q.to(dev), inv.to(dev), ids.to(dev), tw.to(dev)) for q, inv, ids, tw in draws]
+    uniq = [len(set(ids.flatten().tolist())) for _, _, ids, _ in draws]
+    ws = alloc_workspace(rows, TOPK, a0, a1, dev)
+    part = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
+    gathered = [torch.empty_like(part) for _ in range(world)] if world > 1 else None
+    out = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
+    views = [ar.view(li) for li in range(layers)]
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i: int) -> None:
+        q, inv, ids, tw = dq[i % len(dq)]
+        launch(views[i % layers], q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=stream.cuda_stream)
+        if world > 1:
+            dist.all_gather(gathered, part)
+            if rank == 0:
+                combine_ordered(gathered, out=out)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    us_layer = ms * 1e3 / args.steps
+
+    # ---- end to end through the public call with host buffers ----
+    from qmesh_b200.expert_slice import expert_slice
+    host = [(q.pin_memory(), inv.pin_memory(), ids.pin_memory(), tw.pin_memory()) for q, inv, ids, tw in draws]
+    dev_in = [torch.empty_like(t, device=dev) for t in host[0]]
+    out_h = torch.empty(rows, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host[0])
+    d2h = out_h.numel() * out_h.element_size()
+
+    def e2e_step(i: int) -> None:
+        src = host[i % len(host)]
+        for d, s in zip(dev_in, src):
+            d.copy_(s, non_blocking=True)
+        launch(views[i % layers], dev_in[0], dev_in[2], dev_in[3], part, a0, a1, ws, x_scale=dev_in[1],
+               stream=stream.cuda_stream)
+        if world > 1:
+            dist.all_gather(gathered, part)
+            if rank == 0:
+                combine_ordered(gathered, out=out)
+                out_h.copy_(out, non_blocking=True)
+        else:
+            out_h.copy_(part, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    us_e2e = ms_e2e * 1e3 / args.steps
+
+    # ---- kernel-only timing of the slice call (roofline) ----
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i, (a, b) in enumerate(evs):
+        q, inv, ids, tw = dq[i % len(dq)]
+        a.record(stream)
+        launch(views[i % layers], q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=stream.cuda_stream)
+        b.record(stream)
+    torch.cuda.synchronize()
+    k_us = [a.elapsed_time(b) * 1e3 for a, b in evs]
+    k_mean = sum(k_us) / len(k_us)
+    mean_u = sum(uniq[i % len(uniq)] for i in range(args.steps)) / args.steps
+    alg_bytes = mean_u * EXPERT_BYTES / world + rows * HIDDEN * 1 + rows * HIDDEN * 2
+    gbs = alg_bytes / (k_mean * 1e-6) / 1e9
+    peak, peak_kind = peaks()
+    res = None
+    if rank == 0:
+        clocks = clk.summary()
+        res = {
+            "metric": METRIC,
+            "value": round(us_layer, 3),
+            "unit": "us/layer",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(us_layer / 1e3, 6),
+            "higher_is_better": False,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "nvfp4-w/fp8-x/fp32-acc",
+            "data": "synthetic (seeded NVFP4 weights from N(0,0.02); FP8 activations from N(0,1))",
+            "config": {"workload": "config1-decode" if world == 1 else "config2-column-split",
+                       "experts": N_EXPERTS, "hidden": HIDDEN, "intermediate": INTER, "rows": rows,
+                       "topk": TOPK, "columns_per_rank": width, "resident_layers": layers,
+                       "routing_draws": args.draws, "mean_unique_experts": round(mean_u, 2),
+                       "l2": "inputs larger than L2: ~%.0f MB of expert weights per step" % (mean_u * EXPERT_BYTES / 1e6),
+                       "parallelism": f"column-split tp{world}"},
+            "tokens_per_s": round(rows / (us_layer * 1e-6), 1),
+            "weight_gbs": round(gbs, 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                         "kernel_us": round(k_mean, 3), "alg_bytes_per_launch": int(alg_bytes)},
+            "e2e": {"value": round(us_e2e, 3), "unit": "us/layer", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * 2 + (args.steps if world > 1 else 0),
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu:
+            res["cpu_baseline"] = cpu_baseline(draws, ar, rows, a0, a1, args.cpu_layers)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res
+
+
+def cpu_baseline(draws, ar, rows, a0, a1, n_layers: int) -> dict:
+    """The reference torch dequant-and-matmul path restated on the host cores."""
+    from oracle import moe
+    n = moe.cpu_threads()
+    times = []
+    for i in range(n_layers):
+        q, inv, ids, tw = draws[i % len(draws)]
+        experts = sorted(set(ids.flatten().tolist()))
+        pack = ar.expert_pack(i % ar.layers, experts)
+        local = torch.tensor([experts.index(e) for e in ids.flatten().tolist()], dtype=torch.int32).view_as(ids)
+        from oracle import nvfp4 as oq
+        x = oq.fp8_ingest(q, inv)
+        t0 = time.perf_counter()
+        moe.slice_w4a16(x, local, tw, pack, 0, a1 - a0)
+        times.append(time.perf_counter() - t0)
+    us = sum(times) / len(times) * 1e6
+    return {"value": round(us, 1), "unit": "us/layer", "cores": n, "kind": "port",
+            "sample": f"{n_layers} layer calls of the config-1 workload ({rows} rows, full columns)"}
+
+
+def run_reference(args) -> dict | None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    from oracle import moe, nvfp4 as oq
+    n = moe.cpu_threads()
+    gen = torch.Generator().manual_seed(1)
+    rows = args.rows
+    # one resident CPU layer of the routed experts only (the rest are never read)
+    draws = make_inputs(max(args.steps + args.warmup, 1), rows, seed=1, n_experts=N_EXPERTS)
+    times = []
+    for i in range(args.warmup + args.steps):
+        q, inv, ids, tw = draws[i]
+        experts = sorted(set(ids.flatten().tolist()))
+        layer = moe.make_layer(len(experts), gen)
+        local = torch.tensor([experts.index(e) for e in ids.flatten().tolist()], dtype=torch.int32).view_as(ids)
+        x = oq.fp8_ingest(q, inv)
+        t0 = time.perf_counter()
+        moe.slice_w4a16(x, local, tw, layer, 0, INTER)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(dt)
+    us = sum(times) / len(times) * 1e6
+    return {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/layer",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(us / 1e3, 3), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp32 (W4A16 dequant)", "data": "synthetic",
+            "config": {"workload": "config1-decode", "experts": N_EXPERTS, "rows": rows, "topk": TOPK,
+                       "intermediate": INTER},
+            "cpu_baseline": {"value": round(us, 1), "unit": "us/layer", "cores": n, "kind": "port",
+                             "sample": f"{args.steps} layer calls, routed experts only"},
+            "e2e": {"value": round(us, 1), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--rows", type=int, default=6)
+    ap.add_argument("--layers", type=int, default=2)
+    ap.add_argument("--draws", type=int, default=16)
+    ap.add_argument("--cpu-layers", type=int, default=3)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    res = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,122 @@
+/* qmesh_b200 -- C ABI of the B200 routed-expert NVFP4 slice.
+ *
+ * One shared library, libqmesh_b200.so, built for sm_100a. Every entry point
+ * takes plain pointers and sizes, launches on the caller's stream, allocates
+ * nothing, never synchronises the host and never exits the process: it returns
+ * a status code (QX_OK on success). Device-side problems found while running
+ * (bad expert ids, a wait that ran out of time) are recorded in the status
+ * words of the caller's workspace; qx_status_read decodes them.
+ *
+ * Reference interfaces these replace (paths inside QMesh AFD-TP3):
+ *   qx_slice_decode    gx/kernels/ext_variant.cu:11-24  run(out, x, ids, tw,
+ *                      w13, s13, g13, w2, s2, g2, act, swiglu_limit, has_limit)
+ *                      -> decode_moe<5120,896,864> (fp4_decode_moe_swz.cu:390-402),
+ *                      reached through gx/gx_decode_swz.py:163-178 body().
+ *   qx_combine_ordered native/qmesh_afd_seam.cu:310-484 seam_combine(_vec)_kernel,
+ *                      launched by Seam.collect (native/qmesh_afd_seam_py.inc:69-106).
+ */
+#ifndef QMESH_B200_H
+#define QMESH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+enum {
+  QX_OK = 0,
+  QX_ERR_ARG = 1,        /* null pointer or inconsistent argument */
+  QX_ERR_SHAPE = 2,      /* size outside what the kernel supports */
+  QX_ERR_ALIGN = 3,      /* pointer or stride not aligned as required */
+  QX_ERR_WORKSPACE = 4,  /* workspace smaller than qx_slice_workspace_bytes */
+  QX_ERR_LAUNCH = 5,     /* the CUDA launch itself failed */
+  QX_ERR_DEVICE = 6      /* no usable sm_100 device */
+};
+
+/* Device status bits written into the workspace by the kernels. */
+enum {
+  QX_DEV_BAD_ID = 1,       /* an id outside {-1} U [0, E): that slot was skipped */
+  QX_DEV_TIMEOUT = 2,      /* a bounded device wait ran out; the output is invalid */
+  QX_DEV_OVERFLOW = 4      /* more routed pairs than the workspace was sized for */
+};
+
+/* Activation formats. */
+enum {
+  QX_X_E4M3 = 0,   /* e4m3 [rows, hidden] + one FP32 dequant scale per row (inv) */
+  QX_X_E4M3_POST = 1, /* e4m3 [rows, hidden] + one FP32 dequant scale for all rows */
+  QX_X_BF16 = 2    /* bf16 [rows, hidden] (the reference body's input) */
+};
+
+/* Geometry of the build's NVFP4 arena (one MoE layer on one GPU).
+ *
+ * The arena holds intermediate columns [a0, a1) of every expert. Codes and
+ * scales are stored in tiles so that any 32-column-aligned column range of
+ * one expert streams as contiguous bulk copies (see qx_arena_bytes). */
+typedef struct {
+  const uint8_t* w13;      /* gate/up tiles, qx_arena_w13_bytes(E, a1-a0) bytes */
+  const uint8_t* w2;       /* down tiles,    qx_arena_w2_bytes(E, a1-a0) bytes */
+  const float*   g13;      /* [E] w13 weight_scale_2 (w1 and w3 share it) */
+  const float*   g2;       /* [E] w2 weight_scale_2 */
+  int32_t        n_experts;
+  int32_t        a0, a1;   /* arena column range, multiples of 32 */
+} QxArena;
+
+/* One call of the routed-expert slice over columns [c0, c1). */
+typedef struct {
+  const void*  x;          /* activations, format x_fmt, row stride x_stride bytes */
+  const float* x_scale;    /* QX_X_E4M3: [rows]; QX_X_E4M3_POST: [1]; else unused */
+  int64_t      x_stride;   /* bytes between rows of x (>= hidden * element size) */
+  int32_t      x_fmt;
+  const void*  ids;        /* int32 or int64 [rows, topk]; -1 = padding slot */
+  int32_t      ids_int64;
+  const float* tw;         /* FP32 [rows, topk] routing weights */
+  int32_t      rows;       /* 1 .. QX_MAX_ROWS */
+  int32_t      topk;       /* 1 .. QX_MAX_TOPK */
+  int32_t      c0, c1;     /* column range, 32-aligned, inside [a0, a1) */
+  float        swiglu_limit;
+  int32_t      has_limit;
+  uint16_t*    out;        /* BF16 [rows, hidden] partial, row stride out_stride elements */
+  int64_t      out_stride;
+  void*        workspace;  /* qx_slice_workspace_bytes(rows, topk, c0, c1) bytes, 256-aligned */
+  size_t       workspace_bytes;
+} QxSliceArgs;
+
+#define QX_HIDDEN 5120
+#define QX_MAX_ROWS 64
+#define QX_MAX_TOPK 8
+
+/* Arena sizes in bytes for E experts and `width` = a1 - a0 columns. */
+size_t qx_arena_w13_bytes(int32_t n_experts, int32_t width);
+size_t qx_arena_w2_bytes(int32_t n_experts, int32_t width);
+
+/* Workspace bytes one qx_slice_decode call needs. */
+size_t qx_slice_workspace_bytes(int32_t rows, int32_t topk, int32_t c0, int32_t c1);
+
+/* Routed-expert NVFP4 SwiGLU slice (decode, rows <= QX_MAX_ROWS).
+ * Replaces gx/kernels/ext_variant.cu:11-24 run(). Two launches on `stream`
+ * (a routing/activation prologue and the persistent weight-streaming kernel);
+ * capture-safe. */
+int qx_slice_decode(const QxArena* arena, const QxSliceArgs* args, void* stream);
+
+/* Fixed-order combine: out = bf16(fp32(parts[0]) + ... + fp32(parts[n-1])), in
+ * that order, one rounding (out_f32: keep FP32). parts[i] are BF16 [rows, hidden]
+ * rows of stride part_stride elements; they may live on peer GPUs (P2P-mapped
+ * pointers). Replaces native/qmesh_afd_seam.cu:310-484. */
+int qx_combine_ordered(const uint16_t* const* parts, int32_t n_parts, int64_t part_stride,
+                       void* out, int64_t out_stride, int32_t out_f32, int32_t rows,
+                       void* stream);
+
+/* Read the device status words of a workspace (host copy, synchronous on
+ * `stream`): bit set of QX_DEV_*. */
+int qx_status_read(const void* workspace, uint32_t* status, void* stream);
+
+/* Library version string. */
+const char* qx_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QMESH_B200_H */

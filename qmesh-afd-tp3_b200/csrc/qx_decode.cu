@@ -1,0 +1,965 @@
+// Routed-expert NVFP4 SwiGLU slice for decode rows (<= 64) on B200 (sm_100a).
+//
+// Replaces the reference's two-launch v7 body (gx/kernels/fp4_decode_moe_swz.cu
+// stage1_kernel :187-301, stage2_kernel :309-386, decode_moe :390-402) with:
+//
+//   qx_prep_kernel    one CTA per activation row: e4m3 (or bf16) -> the
+//                     reference's bf16 activation (gx/gx_ingest.py:151-154),
+//                     held as f16 scaled by an exact power of two; plus one
+//                     routing CTA that deduplicates experts over all rows and
+//                     builds the work list (pairs grouped by expert).
+//   qx_decode_kernel  persistent, one CTA per SM, warp-specialised: a producer
+//                     warp streams each unique expert's weight tiles once with
+//                     bulk async copies (TMA engine) into a 6-slot shared-memory
+//                     ring; 16 consumer warps dequantise in registers and run
+//                     the dot products for every row routed to that expert.
+//                     Work items come from one atomic queue: first the gate/up
+//                     items (expert, 32-column block), then the down items
+//                     (expert, 256-row output tile). A down item waits (bounded)
+//                     for its expert's gate/up items through per-group counters,
+//                     so the two phases overlap instead of meeting at a grid
+//                     barrier. The warp that completes an output tile last sums
+//                     the per-slot partials in slot order and rounds to BF16 once.
+//
+// Numerics (identical in meaning to the reference's decode path):
+//   x      = bf16(float(e4m3) * inv)                       gx_ingest.py:151-154
+//   w      = e2m1(code) * e4m3(block scale)                fp4_decode_moe_swz.cu:82-96
+//   g, u   = g13[e] * sum_k x_k w_k (FP32 accumulation)    :287-297
+//   act    = (min(g,L) / (1 + exp(-min(g,L)))) * clamp(u,-L,L)   :295-299
+//   y_j    = (g2[e_j] * tw_j) * sum_c act_c w2_c           :356-385
+//   out    = bf16(y_0 + y_1 + ... + y_{k-1})  slot order, one rounding
+// The gate/up dot runs on f16 operands with FP32 accumulation: x is held as
+// x * 2^p in f16 (exact, since a bf16 row decoded from e4m3 spans < 2^18 and p
+// puts its maximum in [2^14, 2^15)), e2m1 values are exact in f16, and every
+// f16 x f16 product is exact in FP32. The down dot widens the e2m1 codes to
+// FP32 and keeps the FP32 activation, as the reference does.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdlib.h>
+
+#include "qmesh_b200.h"
+#include "qx_ptx.cuh"
+
+namespace qx {
+
+constexpr int HID = QX_HIDDEN;            // 5120
+constexpr int KC = 512;                   // gate/up K chunk per stage (elements)
+constexpr int NKC = HID / KC;             // 10 stages per gate/up item
+constexpr int TC = 32;                    // intermediate columns per block
+constexpr int P1_ROWS = 2 * TC;           // 32 gate rows then 32 up rows
+constexpr int P1_CODE = P1_ROWS * KC / 2; // 16384 code bytes per stage
+constexpr int P1_SC = P1_ROWS * KC / 16;  // 2048 scale bytes per stage
+constexpr int P1_STAGE = P1_CODE + P1_SC; // 18432
+constexpr int P1_TILE = NKC * P1_STAGE;   // 184320 bytes per (expert, column block)
+constexpr int TK = 256;                   // down-projection output rows per item
+constexpr int NKT = HID / TK;             // 20
+constexpr int P2_CB_CODE = TK * 16;       // 4096 code bytes per (row tile, column block)
+constexpr int P2_CB_SC = TK * 2;          // 512 scale bytes
+constexpr int P2_CB = P2_CB_CODE + P2_CB_SC;
+constexpr int CB_PER_STAGE = 4;           // column blocks per down stage
+constexpr int PG = 8;                     // routed pairs per group (one item serves a group)
+constexpr int NS = 6;                     // ring slots
+constexpr int SLOT_W = 18432;             // weight bytes per slot
+constexpr int SLOT_A = PG * 1024;         // activation bytes per slot
+constexpr int SLOT = SLOT_W + SLOT_A;     // 26624
+constexpr int NCW = 16;                   // consumer warps
+constexpr int NTHR = (NCW + 1) * 32;      // + one producer warp
+constexpr int MAXP = QX_MAX_ROWS * QX_MAX_TOPK;
+constexpr int MAXE = 4096;
+
+static_assert(CB_PER_STAGE * P2_CB == SLOT_W, "down stage must fill the weight slot");
+static_assert(P1_STAGE == SLOT_W, "gate/up stage must fill the weight slot");
+
+struct Ctl {
+  uint32_t work;      // next work item
+  uint32_t status;    // QX_DEV_* bits
+  uint32_t n_unique;
+  uint32_t n_groups;
+  uint32_t n1, n2;    // gate/up items, down items
+  uint32_t pad[10];
+  uint32_t cnt2[NKT]; // warps finished per output tile
+  uint32_t pad2[64 - 16 - NKT];
+};
+static_assert(sizeof(Ctl) == 256, "ctl block is 256 bytes");
+
+struct Uniq {        // one unique routed expert
+  int32_t expert, pair_off, pair_cnt, ng;
+  int32_t group_off, item1_off, item2_off, pad;
+};
+
+struct Params {
+  const void* x;
+  const float* x_scale;
+  int64_t x_stride;
+  int x_fmt;
+  const void* ids;
+  int ids64;
+  const float* tw;
+  int rows, topk, P;
+  int cbo, n_cb, n_cb_arena, W;
+  const uint8_t* w13;
+  const uint8_t* w2;
+  const float* g13;
+  const float* g2;
+  int E;
+  float limit;
+  int has_limit;
+  __nv_bfloat16* out;
+  int64_t out_stride;
+  Ctl* ctl;
+  uint32_t* cnt1;
+  Uniq* uniq;
+  int32_t* pairlist;
+  int32_t* pexp;
+  float* xscale;
+  __half* x16;
+  float* act;
+  float* y;
+  uint64_t timeout_ns;
+  uint32_t dep_extra;  // test hook: extra arrivals a down item waits for (0 in service)
+};
+
+struct Meta {        // one ring slot's contents, written by the producer
+  int32_t kind;      // 0 end, 1 gate/up stage, 2 down stage
+  int32_t stage, nstages;
+  int32_t expert, group, np, pair_base;
+  int32_t blk;       // column block (gate/up, relative to c0) or output tile (down)
+  int32_t nc;        // column blocks in this down stage
+  int32_t pad[7];
+};
+
+// ------------------------------------------------------------------ workspace
+struct WsLayout {
+  size_t ctl, cnt1, uniq, pairlist, pexp, xscale, x16, act, y, total;
+};
+
+__host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+__host__ inline WsLayout ws_layout(int rows, int topk, int W) {
+  WsLayout L;
+  const size_t P = (size_t)rows * topk;
+  size_t o = 0;
+  L.ctl = o;      o = align256(o + sizeof(Ctl));
+  L.cnt1 = o;     o = align256(o + MAXP * sizeof(uint32_t));
+  L.uniq = o;     o = align256(o + (MAXP + 1) * sizeof(Uniq));
+  L.pairlist = o; o = align256(o + MAXP * sizeof(int32_t));
+  L.pexp = o;     o = align256(o + MAXP * sizeof(int32_t));
+  L.xscale = o;   o = align256(o + (size_t)rows * sizeof(float));
+  L.x16 = o;      o = align256(o + (size_t)rows * HID * sizeof(__half));
+  L.act = o;      o = align256(o + P * (size_t)W * sizeof(float));
+  L.y = o;        o = align256(o + P * (size_t)HID * sizeof(float));
+  L.total = o;
+  return L;
+}
+
+// ------------------------------------------------------------------ prologue
+// In-place exclusive scan of v[0..n) (n <= 512) by a 256-thread block; returns
+// the total. All threads must call it.
+__device__ int block_scan_excl(int* v, int n, int* warp_tot) {
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int i0 = 2 * t, i1 = 2 * t + 1;
+  const int a = i0 < n ? v[i0] : 0;
+  const int b = i1 < n ? v[i1] : 0;
+  int s = a + b, inc = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += u;
+  }
+  if (lane == 31) warp_tot[w] = inc;
+  __syncthreads();
+  if (w == 0) {
+    int x = lane < 8 ? warp_tot[lane] : 0, xi = x;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, xi, o);
+      if (lane >= o) xi += u;
+    }
+    if (lane < 8) warp_tot[lane] = xi - x;  // exclusive warp offsets
+    if (lane == 7) warp_tot[8] = xi;        // total
+  }
+  __syncthreads();
+  const int base = warp_tot[w] + inc - s;
+  if (i0 < n) v[i0] = base;
+  if (i1 < n) v[i1] = base + a;
+  const int total = warp_tot[8];
+  __syncthreads();
+  return total;
+}
+
+__device__ void route(const Params& p) {
+  __shared__ uint32_t bits[MAXE / 32];
+  __shared__ int wpref[MAXE / 32];
+  __shared__ int cntu[MAXP], offu[MAXP], ngu[MAXP], gofu[MAXP], i1u[MAXP], i2u[MAXP];
+  __shared__ int pu[MAXP], ppos[MAXP];
+  __shared__ int wt[9];
+  const int t = threadIdx.x;
+  const int nw = (p.E + 31) / 32;
+  for (int i = t; i < MAXE / 32; i += blockDim.x) bits[i] = 0;
+  for (int i = t; i < MAXP; i += blockDim.x) cntu[i] = 0;
+  for (int i = t; i < MAXP; i += blockDim.x) p.cnt1[i] = 0;
+  uint32_t* c = reinterpret_cast<uint32_t*>(p.ctl);
+  for (int i = t; i < (int)(sizeof(Ctl) / 4); i += blockDim.x) c[i] = 0;
+  __syncthreads();
+  for (int q = t; q < p.P; q += blockDim.x) {
+    const long long id = p.ids64 ? reinterpret_cast<const long long*>(p.ids)[q]
+                                 : (long long)reinterpret_cast<const int*>(p.ids)[q];
+    int e = -1;
+    if (id >= 0 && id < p.E) {
+      e = (int)id;
+      atomicOr(&bits[e >> 5], 1u << (e & 31));
+    } else if (id != -1) {
+      atomicOr(&p.ctl->status, (uint32_t)QX_DEV_BAD_ID);
+    }
+    p.pexp[q] = e;
+  }
+  __syncthreads();
+  for (int i = t; i < nw; i += blockDim.x) wpref[i] = __popc(bits[i]);
+  __syncthreads();
+  // nw <= 128 words: the 512-element scan covers it
+  const int U = block_scan_excl(wpref, nw, wt);
+  for (int i = t; i < nw; i += blockDim.x) {
+    uint32_t w = bits[i];
+    int k = wpref[i];
+    while (w) {
+      const int b = __ffs(w) - 1;
+      p.uniq[k].expert = i * 32 + b;
+      ++k;
+      w &= w - 1;
+    }
+  }
+  for (int q = t; q < p.P; q += blockDim.x) {
+    const int e = p.pexp[q];
+    if (e >= 0) {
+      const int u = wpref[e >> 5] + __popc(bits[e >> 5] & ((1u << (e & 31)) - 1u));
+      pu[q] = u;
+      ppos[q] = atomicAdd(&cntu[u], 1);
+    }
+  }
+  __syncthreads();
+  for (int u = t; u < U; u += blockDim.x) {
+    offu[u] = cntu[u];
+    ngu[u] = (cntu[u] + PG - 1) / PG;
+    gofu[u] = ngu[u];
+    i1u[u] = ngu[u] * p.n_cb;
+    i2u[u] = ngu[u] * NKT;
+  }
+  __syncthreads();
+  block_scan_excl(offu, U, wt);
+  const int G = block_scan_excl(gofu, U, wt);
+  const int n1 = block_scan_excl(i1u, U, wt);
+  const int n2 = block_scan_excl(i2u, U, wt);
+  for (int q = t; q < p.P; q += blockDim.x) {
+    if (p.pexp[q] >= 0) p.pairlist[offu[pu[q]] + ppos[q]] = q;
+  }
+  for (int u = t; u < U; u += blockDim.x) {
+    Uniq& d = p.uniq[u];
+    d.pair_off = offu[u];
+    d.pair_cnt = cntu[u];
+    d.ng = ngu[u];
+    d.group_off = gofu[u];
+    d.item1_off = i1u[u];
+    d.item2_off = i2u[u];
+  }
+  if (t == 0) {
+    Uniq& s = p.uniq[U];
+    s.expert = -1; s.pair_off = 0; s.pair_cnt = 0; s.ng = 0;
+    s.group_off = G; s.item1_off = n1; s.item2_off = n2;
+    p.ctl->n_unique = U;
+    p.ctl->n_groups = G;
+    p.ctl->n1 = n1;
+    p.ctl->n2 = n2;
+  }
+}
+
+// x row -> bf16 value (reference ingest) -> f16 * 2^p, stored in the chunk
+// layout the gate/up consumers read: chunk kc (512 elements), 16-byte unit
+// (v, q) of element 32v + 8q at unit v*4 + (q ^ ((v >> 1) & 3)), which spreads
+// the 16 lanes of a half-warp over all shared-memory bank groups.
+__device__ void convert_row(const Params& p, int r) {
+  __shared__ float red[8];
+  const int t = threadIdx.x;
+  constexpr int UNITS = HID / 8;  // 640
+  float v[3][8];
+  float amax = 0.f;
+  float inv = 1.f;
+  if (p.x_fmt == QX_X_E4M3) inv = p.x_scale[r];
+  else if (p.x_fmt == QX_X_E4M3_POST) inv = p.x_scale[0];
+  const uint8_t* xr = reinterpret_cast<const uint8_t*>(p.x) + (size_t)r * p.x_stride;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int u = t + 256 * j;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[j][e] = 0.f;
+    if (u < UNITS) {
+      if (p.x_fmt == QX_X_BF16) {
+        const uint4 w = *reinterpret_cast<const uint4*>(xr + (size_t)u * 16);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          v[j][2 * k] = __uint_as_float(ww[k] << 16);
+          v[j][2 * k + 1] = __uint_as_float(ww[k] & 0xffff0000u);
+        }
+      } else {
+        const uint2 w = *reinterpret_cast<const uint2*>(xr + (size_t)u * 8);
+        const uint32_t ww[2] = {w.x, w.y};
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t f2 = e4m3x2_to_f16x2(ww[k] >> (16 * h));
+            const float a = __fmul_rn(f16lo_to_f32(f2), inv);
+            const float b = __fmul_rn(f16hi_to_f32(f2), inv);
+            v[j][4 * k + 2 * h] = __bfloat162float(__float2bfloat16_rn(a));
+            v[j][4 * k + 2 * h + 1] = __bfloat162float(__float2bfloat16_rn(b));
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[j][e]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((t & 31) == 0) red[t >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) amax = fmaxf(amax, red[i]);
+  int pw = 0;
+  if (amax > 0.f && amax < INFINITY) {
+    int ex;
+    frexpf(amax, &ex);  // amax = m * 2^ex, m in [0.5, 1)
+    pw = 15 - ex;       // amax * 2^pw in [2^14, 2^15)
+    pw = max(-120, min(120, pw));
+  }
+  const float sc = ldexpf(1.f, pw);
+  if (t == 0) p.xscale[r] = ldexpf(1.f, -pw);
+  __half* dst = p.x16 + (size_t)r * HID;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int u = t + 256 * j;
+    if (u < UNITS) {
+      const int kc = u >> 6, ui = u & 63, vv = ui >> 2, q = ui & 3;
+      const int pos = vv * 4 + (q ^ ((vv >> 1) & 3));
+      __align__(16) __half h[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(v[j][e] * sc);
+      *reinterpret_cast<uint4*>(dst + kc * KC + pos * 8) = *reinterpret_cast<const uint4*>(h);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) qx_prep_kernel(Params p) {
+  pdl_launch_dependents();
+  if ((int)blockIdx.x < p.rows) convert_row(p, blockIdx.x);
+  else route(p);
+}
+
+// ------------------------------------------------------------------ main kernel
+__device__ __forceinline__ const void* to_global(const void* p) {
+  size_t g;
+  asm("cvta.to.global.u64 %0, %1;" : "=l"(g) : "l"(p));
+  return reinterpret_cast<const void*>(g);
+}
+
+// Unique-expert index u with item_off[u] <= item < item_off[u+1].
+__device__ __forceinline__ int find_unique(const Uniq* uq, int U, int item, bool phase1) {
+  int lo = 0, hi = U;  // invariant: off(lo) <= item < off(hi)
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    const int off = phase1 ? uq[mid].item1_off : uq[mid].item2_off;
+    if (off <= item) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+__device__ void producer(const Params& p, uint8_t* smem, uint64_t* full, uint64_t* empty, Meta* meta,
+                         uint64_t deadline) {
+  volatile uint32_t* status = &p.ctl->status;
+  const uint32_t n1 = p.ctl->n1, n2 = p.ctl->n2, U = p.ctl->n_unique;
+  const uint32_t total = n1 + n2;
+  const int n_st2 = (p.n_cb + CB_PER_STAGE - 1) / CB_PER_STAGE;
+  int gs = 0;
+  bool ok = true;
+  Meta m{};
+  int nst = 0, st = 0;
+  int np = 0, pbase = 0, expert = 0, group = 0, blk = 0, kind = 0;
+  for (;;) {
+    if (st == nst) {  // claim the next item
+      const uint32_t item = atomicAdd(&p.ctl->work, 1u);
+      if (item >= total) {
+        kind = 0;
+      } else if (item < n1) {
+        const int u = find_unique(p.uniq, U, item, true);
+        const Uniq d = p.uniq[u];
+        const int local = item - d.item1_off;
+        const int pg = local % d.ng;
+        blk = local / d.ng;
+        kind = 1;
+        nst = NKC;
+        expert = d.expert;
+        group = d.group_off + pg;
+        pbase = d.pair_off + pg * PG;
+        np = min(PG, d.pair_cnt - pg * PG);
+      } else {
+        const int it2 = item - n1;
+        const int u = find_unique(p.uniq, U, it2, false);
+        const Uniq d = p.uniq[u];
+        const int local = it2 - d.item2_off;
+        const int pg = local % d.ng;
+        blk = local / d.ng;
+        kind = 2;
+        nst = n_st2;
+        expert = d.expert;
+        group = d.group_off + pg;
+        pbase = d.pair_off + pg * PG;
+        np = min(PG, d.pair_cnt - pg * PG);
+        // the group's activations must be complete: every gate/up item of the
+        // group increments cnt1 once per consumer warp
+        const uint32_t need = (uint32_t)p.n_cb * NCW + p.dep_extra;
+        uint32_t spins = 0;
+        while (ld_acquire_gpu(&p.cnt1[group]) < need) {
+          if ((++spins & 63u) == 0u) {
+            if (*status & QX_DEV_TIMEOUT) break;
+            if (globaltimer_ns() > deadline) {
+              atomicOr(const_cast<uint32_t*>(status), (uint32_t)QX_DEV_TIMEOUT);
+              break;
+            }
+          }
+          __nanosleep(128);
+        }
+        fence_proxy_async_global();
+      }
+      st = 0;
+    }
+    const int s = gs % NS;
+    if (gs >= NS) {
+      if (!mbar_wait_bounded(&empty[s], ((gs / NS) - 1) & 1, status, QX_DEV_TIMEOUT, deadline)) {
+        ok = false;
+        break;
+      }
+    }
+    m.kind = kind;
+    m.stage = st;
+    m.nstages = nst;
+    m.expert = expert;
+    m.group = group;
+    m.np = np;
+    m.pair_base = pbase;
+    m.blk = blk;
+    m.nc = 0;
+    uint8_t* slot = smem + (size_t)s * SLOT;
+    if (kind == 0) {
+      meta[s] = m;
+      mbar_arrive(&full[s]);
+      ++gs;
+      break;
+    }
+    if (kind == 1) {
+      const uint8_t* src = p.w13 + ((size_t)expert * p.n_cb_arena + (p.cbo + blk)) * P1_TILE + (size_t)st * P1_STAGE;
+      meta[s] = m;
+      mbar_arrive_expect_tx(&full[s], P1_STAGE + np * 1024);
+      bulk_g2s(slot, to_global(src), P1_STAGE, &full[s]);
+      for (int i = 0; i < np; ++i) {
+        const int q = p.pairlist[pbase + i];
+        const int row = q / p.topk;
+        const __half* xs = p.x16 + (size_t)row * HID + st * KC;
+        bulk_g2s(slot + SLOT_W + i * 1024, to_global(xs), 1024, &full[s]);
+      }
+    } else {
+      const int cb0 = st * CB_PER_STAGE;
+      const int nc = min(CB_PER_STAGE, p.n_cb - cb0);
+      m.nc = nc;
+      const uint8_t* base = p.w2 + ((size_t)expert * NKT + blk) * ((size_t)p.n_cb_arena * P2_CB);
+      const uint8_t* csrc = base + (size_t)(p.cbo + cb0) * P2_CB_CODE;
+      const uint8_t* ssrc = base + (size_t)p.n_cb_arena * P2_CB_CODE + (size_t)(p.cbo + cb0) * P2_CB_SC;
+      meta[s] = m;
+      mbar_arrive_expect_tx(&full[s], nc * P2_CB + np * nc * 128);
+      bulk_g2s(slot, to_global(csrc), nc * P2_CB_CODE, &full[s]);
+      bulk_g2s(slot + CB_PER_STAGE * P2_CB_CODE, to_global(ssrc), nc * P2_CB_SC, &full[s]);
+      for (int i = 0; i < np; ++i) {
+        const int q = p.pairlist[pbase + i];
+        const float* a = p.act + (size_t)q * p.W + cb0 * TC;
+        bulk_g2s(slot + SLOT_W + i * 512, to_global(a), nc * 128, &full[s]);
+      }
+    }
+    ++gs;
+    ++st;
+  }
+  if (!ok) {
+    // Drain: every copy this CTA issued must land before the CTA exits.
+    const int first = gs > NS ? gs - NS : 0;
+    for (int g = first; g < gs; ++g) {
+      const uint64_t d2 = globaltimer_ns() + 100000000ull;
+      while (!mbar_try_wait(&full[g % NS], (g / NS) & 1)) {
+        if (globaltimer_ns() > d2) break;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void decode16(const uint4 c, uint32_t (&h)[16]) {
+  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+#pragma unroll
+    for (int b = 0; b < 4; ++b) h[4 * q + b] = e2m1x2_to_f16x2((w[q] >> (8 * b)) & 0xffu);
+  }
+}
+
+__device__ __forceinline__ void scales2(uint32_t two, float& s0, float& s1) {
+  const uint32_t h = e4m3x2_to_f16x2(two);
+  s0 = f16lo_to_f32(h);
+  s1 = f16hi_to_f32(h);
+}
+
+__device__ void final_reduce(const Params& p, int kt, int lane) {
+  const int n = p.rows * TK;
+  for (int idx = lane; idx < n; idx += 32) {
+    const int row = idx / TK, c = idx - row * TK;
+    float s = 0.f;
+    for (int j = 0; j < p.topk; ++j) {
+      const int q = row * p.topk + j;
+      if (p.pexp[q] >= 0) s += __ldcg(p.y + (size_t)q * HID + kt * TK + c);
+    }
+    p.out[(size_t)row * p.out_stride + kt * TK + c] = __float2bfloat16_rn(s);
+  }
+}
+
+__device__ void consumer(const Params& p, const uint8_t* smem, uint64_t* full, uint64_t* empty, const Meta* meta,
+                         uint64_t deadline) {
+  volatile uint32_t* status = &p.ctl->status;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = threadIdx.x;
+  float acc_a[PG], acc_b[PG];
+#pragma unroll
+  for (int i = 0; i < PG; ++i) acc_a[i] = acc_b[i] = 0.f;
+  for (int gs = 0;; ++gs) {
+    const int s = gs % NS;
+    if (!mbar_wait_bounded(&full[s], (gs / NS) & 1, status, QX_DEV_TIMEOUT, deadline)) return;
+    const Meta m = meta[s];
+    if (m.kind == 0) return;
+    const uint8_t* slot = smem + (size_t)s * SLOT;
+    if (m.stage == 0) {
+#pragma unroll
+      for (int i = 0; i < PG; ++i) acc_a[i] = acc_b[i] = 0.f;
+    }
+    if (m.kind == 1) {
+      // gate/up: lane half (lane>>4) picks the gate row, v = lane&15 the 32-element vector
+      const int v = lane & 15;
+      const int gr = 2 * warp + (lane >> 4);
+      const uint4 cg = *reinterpret_cast<const uint4*>(slot + gr * 256 + v * 16);
+      const uint4 cu = *reinterpret_cast<const uint4*>(slot + (gr + TC) * 256 + v * 16);
+      const uint32_t sgw = *reinterpret_cast<const uint16_t*>(slot + P1_CODE + gr * 32 + v * 2);
+      const uint32_t suw = *reinterpret_cast<const uint16_t*>(slot + P1_CODE + (gr + TC) * 32 + v * 2);
+      float sg0, sg1, su0, su1;
+      scales2(sgw, sg0, sg1);
+      scales2(suw, su0, su1);
+      uint32_t hg[16], hu[16];
+      decode16(cg, hg);
+      decode16(cu, hu);
+      const int sw = (v >> 1) & 3;
+#pragma unroll
+      for (int i = 0; i < PG; ++i) {
+        if (i < m.np) {
+          const uint4* xq = reinterpret_cast<const uint4*>(slot + SLOT_W + i * 1024) + v * 4;
+          const uint4 x0 = xq[0 ^ sw], x1 = xq[1 ^ sw], x2 = xq[2 ^ sw], x3 = xq[3 ^ sw];
+          float g0 = 0.f, g1 = 0.f, u0 = 0.f, u1 = 0.f;
+          g0 = fma2_f16_f32(hg[0], x0.x, g0);  u0 = fma2_f16_f32(hu[0], x0.x, u0);
+          g0 = fma2_f16_f32(hg[1], x0.y, g0);  u0 = fma2_f16_f32(hu[1], x0.y, u0);
+          g0 = fma2_f16_f32(hg[2], x0.z, g0);  u0 = fma2_f16_f32(hu[2], x0.z, u0);
+          g0 = fma2_f16_f32(hg[3], x0.w, g0);  u0 = fma2_f16_f32(hu[3], x0.w, u0);
+          g0 = fma2_f16_f32(hg[4], x1.x, g0);  u0 = fma2_f16_f32(hu[4], x1.x, u0);
+          g0 = fma2_f16_f32(hg[5], x1.y, g0);  u0 = fma2_f16_f32(hu[5], x1.y, u0);
+          g0 = fma2_f16_f32(hg[6], x1.z, g0);  u0 = fma2_f16_f32(hu[6], x1.z, u0);
+          g0 = fma2_f16_f32(hg[7], x1.w, g0);  u0 = fma2_f16_f32(hu[7], x1.w, u0);
+          g1 = fma2_f16_f32(hg[8], x2.x, g1);  u1 = fma2_f16_f32(hu[8], x2.x, u1);
+          g1 = fma2_f16_f32(hg[9], x2.y, g1);  u1 = fma2_f16_f32(hu[9], x2.y, u1);
+          g1 = fma2_f16_f32(hg[10], x2.z, g1); u1 = fma2_f16_f32(hu[10], x2.z, u1);
+          g1 = fma2_f16_f32(hg[11], x2.w, g1); u1 = fma2_f16_f32(hu[11], x2.w, u1);
+          g1 = fma2_f16_f32(hg[12], x3.x, g1); u1 = fma2_f16_f32(hu[12], x3.x, u1);
+          g1 = fma2_f16_f32(hg[13], x3.y, g1); u1 = fma2_f16_f32(hu[13], x3.y, u1);
+          g1 = fma2_f16_f32(hg[14], x3.z, g1); u1 = fma2_f16_f32(hu[14], x3.z, u1);
+          g1 = fma2_f16_f32(hg[15], x3.w, g1); u1 = fma2_f16_f32(hu[15], x3.w, u1);
+          acc_a[i] = fmaf(g1, sg1, fmaf(g0, sg0, acc_a[i]));
+          acc_b[i] = fmaf(u1, su1, fmaf(u0, su0, acc_b[i]));
+        }
+      }
+    } else {
+      // down: thread -> output row r = t/2, column blocks {2h, 2h+1} of the stage
+      const int r = t >> 1, h = t & 1;
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = 2 * h + jj;
+        if (j < m.nc) {
+          const uint4 c = *reinterpret_cast<const uint4*>(slot + j * P2_CB_CODE + r * 16);
+          const uint32_t sw2 = *reinterpret_cast<const uint16_t*>(slot + CB_PER_STAGE * P2_CB_CODE + j * P2_CB_SC + r * 2);
+          float s0, s1;
+          scales2(sw2, s0, s1);
+          uint32_t hw[16];
+          decode16(c, hw);
+          float wf[32];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            wf[2 * k] = f16lo_to_f32(hw[k]);
+            wf[2 * k + 1] = f16hi_to_f32(hw[k]);
+          }
+#pragma unroll
+          for (int i = 0; i < PG; ++i) {
+            if (i < m.np) {
+              const float4* a = reinterpret_cast<const float4*>(slot + SLOT_W + i * 512 + j * 128);
+              float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+#pragma unroll
+              for (int k = 0; k < 2; ++k) {
+                const float4 a0 = a[2 * k], a1 = a[2 * k + 1];
+                b0 = fmaf(wf[8 * k + 0], a0.x, b0);
+                b1 = fmaf(wf[8 * k + 1], a0.y, b1);
+                b0 = fmaf(wf[8 * k + 2], a0.z, b0);
+                b1 = fmaf(wf[8 * k + 3], a0.w, b1);
+                b0 = fmaf(wf[8 * k + 4], a1.x, b0);
+                b1 = fmaf(wf[8 * k + 5], a1.y, b1);
+                b0 = fmaf(wf[8 * k + 6], a1.z, b0);
+                b1 = fmaf(wf[8 * k + 7], a1.w, b1);
+              }
+#pragma unroll
+              for (int k = 2; k < 4; ++k) {
+                const float4 a0 = a[2 * k], a1 = a[2 * k + 1];
+                b2 = fmaf(wf[8 * k + 0], a0.x, b2);
+                b3 = fmaf(wf[8 * k + 1], a0.y, b3);
+                b2 = fmaf(wf[8 * k + 2], a0.z, b2);
+                b3 = fmaf(wf[8 * k + 3], a0.w, b3);
+                b2 = fmaf(wf[8 * k + 4], a1.x, b2);
+                b3 = fmaf(wf[8 * k + 5], a1.y, b3);
+                b2 = fmaf(wf[8 * k + 6], a1.z, b2);
+                b3 = fmaf(wf[8 * k + 7], a1.w, b3);
+              }
+              acc_a[i] = fmaf(b2 + b3, s1, fmaf(b0 + b1, s0, acc_a[i]));
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (m.stage != m.nstages - 1) continue;
+    // ---- item epilogue (registers + global memory only) ----
+    if (m.kind == 1) {
+      const int v = lane & 15;
+      const int gr = 2 * warp + (lane >> 4);
+      const float g13 = p.g13[m.expert];
+#pragma unroll
+      for (int i = 0; i < PG; ++i) {
+        if (i < m.np) {
+          float g = acc_a[i], u = acc_b[i];
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) {
+            g += __shfl_xor_sync(0xffffffffu, g, o);
+            u += __shfl_xor_sync(0xffffffffu, u, o);
+          }
+          if (v == 0) {
+            const int q = p.pairlist[m.pair_base + i];
+            const float xs = p.xscale[q / p.topk];
+            float gg = (g * xs) * g13, uu = (u * xs) * g13;
+            if (p.has_limit) {
+              gg = fminf(gg, p.limit);
+              uu = fminf(fmaxf(uu, -p.limit), p.limit);
+            }
+            p.act[(size_t)q * p.W + m.blk * TC + gr] = (gg / (1.f + expf(-gg))) * uu;
+          }
+        }
+      }
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) atomicAdd(&p.cnt1[m.group], 1u);
+    } else {
+      const int r = t >> 1, h = t & 1;
+      const float g2 = p.g2[m.expert];
+#pragma unroll
+      for (int i = 0; i < PG; ++i) {
+        if (i < m.np) {
+          const float a = acc_a[i] + __shfl_xor_sync(0xffffffffu, acc_a[i], 1);
+          if (h == 0) {
+            const int q = p.pairlist[m.pair_base + i];
+            const float gw = g2 * p.tw[q];
+            p.y[(size_t)q * HID + m.blk * TK + r] = a * gw;
+          }
+        }
+      }
+      __threadfence();
+      __syncwarp();
+      uint32_t last = 0;
+      if (lane == 0) {
+        const uint32_t old = atomicAdd(&p.ctl->cnt2[m.blk], 1u);
+        last = (old == p.ctl->n_groups * NCW - 1u) ? 1u : 0u;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence();
+        final_reduce(p, m.blk, lane);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(NTHR, 1) qx_decode_kernel(Params p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * SLOT);
+  uint64_t* empty = full + NS;
+  Meta* meta = reinterpret_cast<Meta*>(empty + NS);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NCW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_wait();  // the prologue's routing tables and activations are complete
+  const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+  if (p.ctl->n_groups == 0) {  // every slot was padding: the partial is zero
+    if (blockIdx.x == 0) {
+      for (int i = threadIdx.x; i < p.rows * HID; i += blockDim.x) {
+        const int row = i / HID, c = i - row * HID;
+        p.out[(size_t)row * p.out_stride + c] = __float2bfloat16_rn(0.f);
+      }
+    }
+    return;
+  }
+  const int warp = threadIdx.x >> 5;
+  if (warp == NCW) {
+    if ((threadIdx.x & 31) == 0) producer(p, smem, full, empty, meta, deadline);
+    return;
+  }
+  consumer(p, smem, full, empty, meta, deadline);
+}
+
+constexpr size_t SMEM_BYTES = (size_t)NS * SLOT + 2 * NS * sizeof(uint64_t) + NS * sizeof(Meta);
+
+// ------------------------------------------------------------------ combine
+struct CombineParams {
+  const uint16_t* parts[16];
+  int n_parts;
+  int64_t part_stride;
+  void* out;
+  int64_t out_stride;
+  int out_f32;
+  int rows;
+};
+
+// Fixed-order FP32 sum of BF16 partials, 8 elements per thread (16-byte loads).
+__global__ void __launch_bounds__(256) qx_combine_kernel(CombineParams c) {
+  const int chunks = HID / 8;
+  const int n = c.rows * chunks;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int row = i / chunks, col = (i - row * chunks) * 8;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int k = 0; k < c.n_parts; ++k) {
+      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(c.parts[k] + (size_t)row * c.part_stride + col));
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[2 * e] += __uint_as_float(w[e] << 16);
+        acc[2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+      }
+    }
+    if (c.out_f32) {
+      float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(c.out) + (size_t)row * c.out_stride + col);
+      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+        w[e] = *reinterpret_cast<const uint32_t*>(&b);
+      }
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(c.out) + (size_t)row * c.out_stride + col) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+static int device_sms(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  static int cached[64] = {0};
+  static bool attr_set[64] = {false};
+  if (dev < 0 || dev >= 64) return -1;
+  if (cached[dev] == 0) {
+    int major = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return -1;
+    if (major != 10) return -1;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    cached[dev] = sms;
+  }
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(qx_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) !=
+        cudaSuccess)
+      return -1;
+    attr_set[dev] = true;
+  }
+  *dev_out = dev;
+  return cached[dev];
+}
+
+// Bound on every device-side wait, QX_TIMEOUT_MS (default 1000 ms), read per launch.
+static uint64_t timeout_ns() {
+  const char* e = getenv("QX_TIMEOUT_MS");
+  long ms = e ? atol(e) : 1000;
+  if (ms < 10) ms = 10;
+  return (uint64_t)ms * 1000000ull;
+}
+
+// Test hook QX_TEST_DEP_EXTRA=n: every down item waits for n arrivals that never
+// come, so the bounded dependency wait runs out and QX_DEV_TIMEOUT is recorded.
+static uint32_t dep_extra() {
+  const char* e = getenv("QX_TEST_DEP_EXTRA");
+  return e ? (uint32_t)atol(e) : 0u;
+}
+
+}  // namespace qx
+
+using namespace qx;
+
+extern "C" {
+
+size_t qx_arena_w13_bytes(int32_t n_experts, int32_t width) {
+  if (n_experts <= 0 || width <= 0 || width % TC) return 0;
+  return (size_t)n_experts * (width / TC) * P1_TILE;
+}
+
+size_t qx_arena_w2_bytes(int32_t n_experts, int32_t width) {
+  if (n_experts <= 0 || width <= 0 || width % TC) return 0;
+  return (size_t)n_experts * NKT * (size_t)(width / TC) * P2_CB;
+}
+
+size_t qx_slice_workspace_bytes(int32_t rows, int32_t topk, int32_t c0, int32_t c1) {
+  if (rows <= 0 || rows > QX_MAX_ROWS || topk <= 0 || topk > QX_MAX_TOPK || c1 <= c0) return 0;
+  return ws_layout(rows, topk, c1 - c0).total;
+}
+
+int qx_slice_decode(const QxArena* arena, const QxSliceArgs* a, void* stream) {
+  if (!arena || !a) return QX_ERR_ARG;
+  if (!a->x || !a->ids || !a->tw || !a->out || !a->workspace || !arena->w13 || !arena->w2 || !arena->g13 ||
+      !arena->g2)
+    return QX_ERR_ARG;
+  if ((a->x_fmt == QX_X_E4M3 || a->x_fmt == QX_X_E4M3_POST) && !a->x_scale) return QX_ERR_ARG;
+  if (a->x_fmt < QX_X_E4M3 || a->x_fmt > QX_X_BF16) return QX_ERR_ARG;
+  if (a->rows < 1 || a->rows > QX_MAX_ROWS || a->topk < 1 || a->topk > QX_MAX_TOPK) return QX_ERR_SHAPE;
+  if (arena->n_experts < 1 || arena->n_experts > MAXE) return QX_ERR_SHAPE;
+  if (arena->a0 % TC || arena->a1 % TC || arena->a1 <= arena->a0) return QX_ERR_SHAPE;
+  if (a->c0 % TC || a->c1 % TC || a->c0 < arena->a0 || a->c1 > arena->a1 || a->c1 <= a->c0) return QX_ERR_SHAPE;
+  const int esz = a->x_fmt == QX_X_BF16 ? 2 : 1;
+  if (a->x_stride < (int64_t)HID * esz || a->out_stride < HID) return QX_ERR_SHAPE;
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(a->x);
+  if ((xa & 15u) || (a->x_stride & 15) || (reinterpret_cast<uintptr_t>(a->workspace) & 255u) ||
+      (reinterpret_cast<uintptr_t>(arena->w13) & 15u) || (reinterpret_cast<uintptr_t>(arena->w2) & 15u))
+    return QX_ERR_ALIGN;
+  const int W = a->c1 - a->c0;
+  const WsLayout L = ws_layout(a->rows, a->topk, W);
+  if (a->workspace_bytes < L.total) return QX_ERR_WORKSPACE;
+  int dev = 0;
+  const int sms = device_sms(&dev);
+  if (sms <= 0) return QX_ERR_DEVICE;
+
+  Params p;
+  p.x = a->x;
+  p.x_scale = a->x_scale;
+  p.x_stride = a->x_stride;
+  p.x_fmt = a->x_fmt;
+  p.ids = a->ids;
+  p.ids64 = a->ids_int64 ? 1 : 0;
+  p.tw = a->tw;
+  p.rows = a->rows;
+  p.topk = a->topk;
+  p.P = a->rows * a->topk;
+  p.cbo = (a->c0 - arena->a0) / TC;
+  p.n_cb = W / TC;
+  p.n_cb_arena = (arena->a1 - arena->a0) / TC;
+  p.W = W;
+  p.w13 = arena->w13;
+  p.w2 = arena->w2;
+  p.g13 = arena->g13;
+  p.g2 = arena->g2;
+  p.E = arena->n_experts;
+  p.limit = a->swiglu_limit;
+  p.has_limit = a->has_limit ? 1 : 0;
+  p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
+  p.out_stride = a->out_stride;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
+  p.ctl = reinterpret_cast<Ctl*>(ws + L.ctl);
+  p.cnt1 = reinterpret_cast<uint32_t*>(ws + L.cnt1);
+  p.uniq = reinterpret_cast<Uniq*>(ws + L.uniq);
+  p.pairlist = reinterpret_cast<int32_t*>(ws + L.pairlist);
+  p.pexp = reinterpret_cast<int32_t*>(ws + L.pexp);
+  p.xscale = reinterpret_cast<float*>(ws + L.xscale);
+  p.x16 = reinterpret_cast<__half*>(ws + L.x16);
+  p.act = reinterpret_cast<float*>(ws + L.act);
+  p.y = reinterpret_cast<float*>(ws + L.y);
+  p.timeout_ns = timeout_ns();
+  p.dep_extra = dep_extra();
+
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  qx_prep_kernel<<<a->rows + 1, 256, 0, st>>>(p);
+  if (cudaGetLastError() != cudaSuccess) return QX_ERR_LAUNCH;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms, 1, 1);
+  cfg.blockDim = dim3(NTHR, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, qx_decode_kernel, p) != cudaSuccess) return QX_ERR_LAUNCH;
+  return QX_OK;
+}
+
+int qx_combine_ordered(const uint16_t* const* parts, int32_t n_parts, int64_t part_stride, void* out,
+                       int64_t out_stride, int32_t out_f32, int32_t rows, void* stream) {
+  if (!parts || !out || n_parts < 1 || n_parts > 16 || rows < 1) return QX_ERR_ARG;
+  if (part_stride < HID || out_stride < HID || (part_stride & 7) || (out_stride & (out_f32 ? 3 : 7)))
+    return QX_ERR_SHAPE;
+  CombineParams c;
+  for (int i = 0; i < n_parts; ++i) {
+    if (!parts[i] || (reinterpret_cast<uintptr_t>(parts[i]) & 15u)) return QX_ERR_ALIGN;
+    c.parts[i] = parts[i];
+  }
+  if (reinterpret_cast<uintptr_t>(out) & 15u) return QX_ERR_ALIGN;
+  c.n_parts = n_parts;
+  c.part_stride = part_stride;
+  c.out = out;
+  c.out_stride = out_stride;
+  c.out_f32 = out_f32 ? 1 : 0;
+  c.rows = rows;
+  int dev = 0;
+  const int sms = device_sms(&dev);
+  if (sms <= 0) return QX_ERR_DEVICE;
+  const int n = rows * (HID / 8);
+  int blocks = (n + 255) / 256;
+  if (blocks > 4 * sms) blocks = 4 * sms;
+  qx_combine_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(c);
+  return cudaGetLastError() == cudaSuccess ? QX_OK : QX_ERR_LAUNCH;
+}
+
+int qx_status_read(const void* workspace, uint32_t* status, void* stream) {
+  if (!workspace || !status) return QX_ERR_ARG;
+  const Ctl* ctl = reinterpret_cast<const Ctl*>(workspace);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(status, &ctl->status, sizeof(uint32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return QX_ERR_LAUNCH;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return QX_ERR_LAUNCH;
+  return QX_OK;
+}
+
+const char* qx_version(void) { return "qmesh_b200 0.1 sm_100a"; }
+
+}  // extern "C"

@@ -1,0 +1,137 @@
+"""The routed-expert slice call: the drop-in for the reference's decode body.
+
+Two forms over the same C entry point (qx_slice_decode):
+
+* ``expert_slice(layer, x, ids, tw, c0=, c1=, x_scale=)`` -- the north-star form:
+  FP8 e4m3 activations [rows, 5120] with an FP32 dequant scale per row (or one
+  per post), top-k ids and weights, a column range [c0, c1); returns the BF16
+  [rows, 5120] partial.
+* ``make_body(arena, swiglu_limit)`` -> ``body(li, r, x, ids, tw, out, ws13, ws2, a1g)``
+  with the signature, argument meaning and errors of gx/gx_decode_swz.py:148-179
+  (x is the ingested BF16 activation; out is written in place).
+
+Everything is launched on the current torch stream, allocates nothing once the
+workspace exists, and never synchronises the host, so both forms can be captured
+in a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .arena import Arena
+
+SWIGLU_LIMIT = 10.0
+
+
+def workspace_bytes(rows: int, topk: int, c0: int, c1: int) -> int:
+    n = _lib.load().qx_slice_workspace_bytes(rows, topk, c0, c1)
+    if n == 0:
+        raise ValueError(f"no workspace for rows={rows} topk={topk} columns [{c0}, {c1})")
+    return n
+
+
+def alloc_workspace(rows: int, topk: int, c0: int, c1: int, device) -> torch.Tensor:
+    """Workspace for calls of up to `rows` rows over `c1 - c0` columns."""
+    return torch.empty(workspace_bytes(rows, topk, c0, c1), dtype=torch.uint8, device=device)
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr() if t is not None else 0)
+
+
+def launch(view: _lib.QxArena, x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, out: torch.Tensor,
+           c0: int, c1: int, workspace: torch.Tensor, x_scale: torch.Tensor | None = None,
+           swiglu_limit: float = SWIGLU_LIMIT, has_limit: bool = True, stream=None) -> None:
+    """Validate and launch one slice call (no allocation, no host sync)."""
+    lib = _lib.load()
+    rows = x.shape[0]
+    if x.dtype == torch.bfloat16:
+        fmt = _lib.QX_X_BF16
+        esz = 2
+    elif x.dtype in (torch.float8_e4m3fn, torch.uint8):
+        if x_scale is None:
+            raise TypeError("FP8 activations need x_scale (per row [rows] or per post [1])")
+        if x_scale.dtype != torch.float32:
+            raise TypeError(f"x_scale must be float32, got {x_scale.dtype}")
+        fmt = _lib.QX_X_E4M3 if x_scale.numel() == rows else _lib.QX_X_E4M3_POST
+        if x_scale.numel() not in (1, rows):
+            raise ValueError(f"x_scale has {x_scale.numel()} values for {rows} rows")
+        esz = 1
+    else:
+        raise TypeError(f"x must be bf16 or e4m3, got {x.dtype}")
+    if ids.dtype not in (torch.int32, torch.int64) or tw.dtype != torch.float32 or out.dtype != torch.bfloat16:
+        raise TypeError(f"ids/tw/out must be int32|int64/f32/bf16, got {ids.dtype}/{tw.dtype}/{out.dtype}")
+    if ids.shape != tw.shape or ids.shape[0] != rows or out.shape[0] < rows:
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)} ids {tuple(ids.shape)} tw {tuple(tw.shape)} "
+                         f"out {tuple(out.shape)}")
+    if x.shape[1] != _lib.HIDDEN or out.shape[1] != _lib.HIDDEN:
+        raise ValueError(f"hidden size must be {_lib.HIDDEN}")
+    if not (ids.is_contiguous() and tw.is_contiguous()) or x.stride(1) != 1 or out.stride(1) != 1:
+        raise ValueError("ids/tw must be contiguous and x/out rows unit-stride")
+    args = _lib.QxSliceArgs(
+        _ptr(x), _ptr(x_scale), x.stride(0) * esz, fmt,
+        _ptr(ids), 1 if ids.dtype == torch.int64 else 0, _ptr(tw),
+        rows, ids.shape[1], c0, c1, float(swiglu_limit), 1 if has_limit else 0,
+        _ptr(out), out.stride(0), _ptr(workspace), workspace.numel())
+    if stream is None:
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+    rc = lib.qx_slice_decode(ctypes.byref(view), ctypes.byref(args), ctypes.c_void_p(stream))
+    _lib.check(rc, "qx_slice_decode")
+
+
+def expert_slice(arena: Arena, li: int, x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor,
+                 c0: int | None = None, c1: int | None = None, x_scale: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                 swiglu_limit: float = SWIGLU_LIMIT) -> torch.Tensor:
+    """BF16 [rows, 5120] partial of the routed experts over columns [c0, c1)."""
+    c0 = arena.a0 if c0 is None else c0
+    c1 = arena.a1 if c1 is None else c1
+    rows = x.shape[0]
+    if out is None:
+        out = torch.empty(rows, _lib.HIDDEN, dtype=torch.bfloat16, device=x.device)
+    if workspace is None:
+        workspace = alloc_workspace(rows, ids.shape[1], c0, c1, x.device)
+    launch(arena.view(li), x, ids, tw, out, c0, c1, workspace, x_scale=x_scale,
+           swiglu_limit=max(swiglu_limit, 0.0), has_limit=swiglu_limit > 0)
+    return out
+
+
+def device_status(workspace: torch.Tensor) -> int:
+    """QX_DEV_* bits the last call on this workspace recorded (synchronises)."""
+    st = ctypes.c_uint32(0)
+    stream = torch.cuda.current_stream(workspace.device).cuda_stream
+    _lib.check(_lib.load().qx_status_read(_ptr(workspace), ctypes.byref(st), ctypes.c_void_p(stream)),
+               "qx_status_read")
+    return int(st.value)
+
+
+def make_body(arena: Arena, swiglu_limit: float, max_rows: int = 16, topk: int = 6):
+    """``body(li, r, x, ids, tw, out, ws13, ws2, a1g)`` over the arena's own tensors.
+
+    Mirrors gx/gx_decode_swz.py:148-179: x bf16 [r, 5120] (ingested), ids int32,
+    tw f32, out bf16, all [r, ...]; ws13/ws2/a1g are accepted for signature
+    compatibility. The kernel's scratch is this body's own workspace, sized once
+    here for `max_rows`, so replays allocate nothing.
+    """
+    _lib.load()
+    has_limit = bool(swiglu_limit > 0)
+    limit = float(max(swiglu_limit, 0.0))
+    ws = alloc_workspace(max_rows, topk, arena.a0, arena.a1, arena.dev)
+
+    def body(li: int, r: int, x, ids, tw, out, ws13=None, ws2=None, a1g=None) -> None:
+        if not arena.loaded(li):
+            raise RuntimeError(f"layer {li} is not loaded in the arena")
+        if (ids.dtype is not torch.int32 or tw.dtype is not torch.float32
+                or x.dtype is not torch.bfloat16 or out.dtype is not torch.bfloat16):
+            raise TypeError(
+                f"decode body: ids/tw/x/out must be int32/f32/bf16/bf16, "
+                f"got {ids.dtype}/{tw.dtype}/{x.dtype}/{out.dtype}")
+        if not 1 <= r <= max_rows:
+            raise ValueError(f"row count {r} outside 1..{max_rows}")
+        launch(arena.view(li), x[:r], ids[:r], tw[:r], out[:r], arena.a0, arena.a1, ws,
+               swiglu_limit=limit, has_limit=has_limit)
+    return body

@@ -1,0 +1,63 @@
+"""Shared test helpers: the parity tolerance and small synthetic layers."""
+
+from __future__ import annotations
+
+import functools
+
+import torch
+
+from oracle import moe, nvfp4 as q4
+
+# BF16 partial and combined output within relative-L2 5e-3
+# and max-abs 2 BF16 ulp per element of the reference value.
+REL_L2 = 5e-3
+MAX_ULP = 2.0
+
+
+def bf16_ulp(v: torch.Tensor) -> torch.Tensor:
+    """Spacing of BF16 numbers at |v| (normal range; 2^-133 below it)."""
+    a = v.abs().float().clamp_min(2.0 ** -126)
+    return torch.pow(2.0, torch.floor(torch.log2(a)) - 7.0)
+
+
+def parity(out: torch.Tensor, ref: torch.Tensor) -> dict:
+    out = out.float().cpu()
+    ref = ref.float().cpu()
+    err = (out - ref).abs()
+    rel = (err.norm() / ref.norm().clamp_min(1e-30)).item()
+    ulps = (err / bf16_ulp(ref)).max().item()
+    return {"rel_l2": rel, "max_ulp": ulps, "max_abs": err.max().item(), "exact": float((err == 0).float().mean())}
+
+
+def assert_parity(out, ref, what=""):
+    p = parity(out, ref)
+    assert p["rel_l2"] <= REL_L2 and p["max_ulp"] <= MAX_ULP, f"{what} {p}"
+    return p
+
+
+def small_layer(seed: int, n_experts: int, inter: int = 2304):
+    gen = torch.Generator().manual_seed(seed)
+    return moe.make_layer(n_experts, gen, inter=inter)
+
+
+@functools.lru_cache(maxsize=2)
+def config0_cached(seed: int = 0):
+    return moe.config0(seed)
+
+
+def activations(rows: int, seed: int):
+    gen = torch.Generator().manual_seed(seed)
+    return moe.make_activation(rows, gen)
+
+
+def random_routing(rows: int, n_experts: int, seed: int, topk: int = 6):
+    gen = torch.Generator().manual_seed(seed)
+    return moe.routing(torch.randn(rows, n_experts, generator=gen), topk)
+
+
+def oracle_out(x_used, ids, tw, layer, c0, c1, limit=10.0, has_limit=True):
+    return moe.slice_w4a16(x_used, ids, tw, layer, c0, c1, limit=limit, has_limit=has_limit)
+
+
+def ingest(q, inv):
+    return q4.fp8_ingest(q, inv)

@@ -1,0 +1,259 @@
+"""GPU parity of the decode slice (through the C ABI) against the CPU oracle."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import helpers as H
+from oracle import moe, nvfp4 as oq
+
+pytestmark = pytest.mark.gpu
+
+
+def _arena(dev, layer, a0=0, a1=None, n_layers=1, li=0, src_a0=0):
+    from qmesh_b200.arena import Arena
+    inter = layer["c13"].shape[1] // 2
+    a1 = inter if a1 is None else a1
+    ar = Arena(dev, n_layers, layer["c13"].shape[0], a0, a1)
+    ar.load_layer(li, layer, src_a0=src_a0)
+    return ar
+
+
+def _run(ar, q, inv, ids, tw, c0=None, c1=None, ws=None, **kw):
+    from qmesh_b200.expert_slice import expert_slice
+    dev = ar.dev
+    out = expert_slice(ar, 0, q.to(dev), ids.to(dev), tw.to(dev), c0=c0, c1=c1,
+                       x_scale=None if inv is None else inv.to(dev), workspace=ws, **kw)
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.fixture(scope="module")
+def small(cuda_ready):
+    layer = H.small_layer(21, 16, inter=512)
+    return layer, _arena(cuda_ready, layer)
+
+
+def test_config0_parity(cuda_ready):
+    """8 experts, hidden 5120, intermediate 2304, rows=1, top-6."""
+    c = H.config0_cached(0)
+    ar = _arena(cuda_ready, c)
+    out = _run(ar, c["q"], c["inv"], c["ids"], c["tw"])
+    ref = H.oracle_out(H.ingest(c["q"], c["inv"]), c["ids"], c["tw"], c, 0, 2304)
+    p = H.assert_parity(out, ref, "config0")
+    print("config0", p)
+
+
+@pytest.mark.parametrize("rows,seed", [(1, 1), (6, 2), (16, 3), (20, 4)])
+def test_rows_and_dedup(small, rows, seed):
+    layer, ar = small
+    ids, tw = H.random_routing(rows, 16, seed)
+    _, q, inv = H.activations(rows, seed)
+    out = _run(ar, q, inv, ids, tw)
+    ref = H.oracle_out(H.ingest(q, inv), ids, tw, layer, 0, 512)
+    H.assert_parity(out, ref, f"rows={rows}")
+
+
+def test_hot_expert_spans_groups(small):
+    """One expert routed from 20 rows: three pair groups share one weight stream."""
+    layer, ar = small
+    rows = 20
+    ids, tw = H.random_routing(rows, 16, 5)
+    ids[:, 0] = 3
+    ids[:, 1] = torch.where(ids[:, 1] == 3, 4, ids[:, 1])
+    for j in range(2, 6):
+        ids[:, j] = torch.where(ids[:, j] == 3, (ids[:, j] + 5) % 16, ids[:, j])
+    _, q, inv = H.activations(rows, 5)
+    out = _run(ar, q, inv, ids, tw)
+    ref = H.oracle_out(H.ingest(q, inv), ids, tw, layer, 0, 512)
+    H.assert_parity(out, ref, "hot expert")
+
+
+def test_padding_and_corrupt_ids(small):
+    from qmesh_b200 import _lib
+    from qmesh_b200.expert_slice import alloc_workspace, device_status
+    layer, ar = small
+    rows = 4
+    ids, tw = H.random_routing(rows, 16, 9)
+    ids[1, 2] = -1
+    ids[2, :] = -1
+    _, q, inv = H.activations(rows, 9)
+    ws = alloc_workspace(rows, 6, 0, 512, ar.dev)
+    out = _run(ar, q, inv, ids, tw, ws=ws)
+    assert device_status(ws) == 0
+    keep = ids >= 0
+    tw0 = torch.where(keep, tw, torch.zeros_like(tw))
+    ids0 = torch.where(keep, ids, torch.zeros_like(ids))
+    ref = H.oracle_out(H.ingest(q, inv), ids0, tw0, layer, 0, 512)
+    H.assert_parity(out, ref, "padding")
+    assert (out[2].float() == 0).all()
+    ids[0, 1] = 999
+    out = _run(ar, q, inv, ids, tw, ws=ws)
+    assert device_status(ws) & _lib.QX_DEV_BAD_ID
+    keep = ids >= 0
+    keep[0, 1] = False
+    ref = H.oracle_out(H.ingest(q, inv), torch.where(keep, ids, 0), torch.where(keep, tw, 0.0), layer, 0, 512)
+    H.assert_parity(out, ref, "corrupt id skipped")
+
+
+def test_all_padding_gives_zero(small):
+    layer, ar = small
+    ids = torch.full((3, 6), -1, dtype=torch.int32)
+    tw = torch.zeros(3, 6)
+    _, q, inv = H.activations(3, 1)
+    out = _run(ar, q, inv, ids, tw)
+    assert (out.float() == 0).all()
+
+
+def test_input_forms_agree(small):
+    """bf16 x (reference body input), per-post scale, int64 ids: same partial."""
+    layer, ar = small
+    rows = 5
+    ids, tw = H.random_routing(rows, 16, 12)
+    _, q, inv = H.activations(rows, 12)
+    base = _run(ar, q, inv, ids, tw)
+    xb = H.ingest(q, inv).to(torch.bfloat16)
+    bf = _run(ar, xb, None, ids, tw)
+    assert torch.equal(base, bf)
+    i64 = _run(ar, q, inv, ids.to(torch.int64), tw)
+    assert torch.equal(base, i64)
+    post = torch.full((1,), float(inv[0]))
+    qp, _ = oq.fp8_quant_rows(H.ingest(q, inv))
+    a = _run(ar, q, post, ids, tw)
+    ref = H.oracle_out(H.ingest(q, post.expand(rows)), ids, tw, layer, 0, 512)
+    H.assert_parity(a, ref, "per-post scale")
+
+
+def test_column_ranges_and_ordered_combine(small):
+    from qmesh_b200.combine import combine_ordered
+    layer, ar = small
+    rows = 6
+    ids, tw = H.random_routing(rows, 16, 14)
+    _, q, inv = H.activations(rows, 14)
+    x = H.ingest(q, inv)
+    parts = []
+    for a, b in moe.shard_ranges(512, 4):
+        out = _run(ar, q, inv, ids, tw, c0=a, c1=b)
+        H.assert_parity(out, H.oracle_out(x, ids, tw, layer, a, b), f"shard [{a},{b})")
+        parts.append(out)
+    comb = combine_ordered(parts)
+    torch.cuda.synchronize()
+    want = moe.combine_ordered([p.float().cpu() for p in parts])
+    assert torch.equal(comb.float().cpu(), want)
+    H.assert_parity(comb, H.oracle_out(x, ids, tw, layer, 0, 512), "combined")
+
+
+def test_rank_arena_equals_full_arena_slice(small, cuda_ready):
+    layer, ar = small
+    rank = _arena(cuda_ready, layer, a0=128, a1=384)
+    rows = 6
+    ids, tw = H.random_routing(rows, 16, 15)
+    _, q, inv = H.activations(rows, 15)
+    a = _run(ar, q, inv, ids, tw, c0=128, c1=384)
+    b = _run(rank, q, inv, ids, tw)
+    assert torch.equal(a, b)
+
+
+def test_deterministic(small):
+    layer, ar = small
+    ids, tw = H.random_routing(6, 16, 16)
+    _, q, inv = H.activations(6, 16)
+    a = _run(ar, q, inv, ids, tw)
+    for _ in range(3):
+        assert torch.equal(a, _run(ar, q, inv, ids, tw))
+
+
+def test_body_interface_and_graph_capture(small):
+    """make_body mirrors gx_decode_swz.make_body; replay of a captured graph."""
+    from qmesh_b200.expert_slice import make_body
+    layer, ar = small
+    dev = ar.dev
+    body = make_body(ar, 10.0)
+    r = 6
+    ids, tw = H.random_routing(r, 16, 17)
+    _, q, inv = H.activations(r, 17)
+    x = H.ingest(q, inv).to(torch.bfloat16).to(dev)
+    ids, tw = ids.to(dev), tw.to(dev)
+    out = torch.zeros(r, 5120, dtype=torch.bfloat16, device=dev)
+    body(0, r, x, ids, tw, out, None, None, None)
+    torch.cuda.synchronize()
+    eager = out.clone()
+    with pytest.raises(TypeError):
+        body(0, r, x.float(), ids, tw, out, None, None, None)
+    with pytest.raises(RuntimeError):
+        body(5, r, x, ids, tw, out, None, None, None)
+    with pytest.raises(ValueError):
+        body(0, 17, x, ids, tw, out, None, None, None)
+    out.zero_()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        body(0, r, x, ids, tw, out, None, None, None)  # warm
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            body(0, r, x, ids, tw, out, None, None, None)
+    out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+
+
+def test_bounded_wait_reports_timeout_and_context_survives(small, monkeypatch):
+    """A dependency that never completes: the bounded wait runs out, the kernel
+    returns, QX_DEV_TIMEOUT is recorded, and the next call is correct."""
+    from qmesh_b200 import _lib
+    from qmesh_b200.expert_slice import alloc_workspace, device_status
+    layer, ar = small
+    ids, tw = H.random_routing(2, 16, 18)
+    _, q, inv = H.activations(2, 18)
+    ws = alloc_workspace(2, 6, 0, 512, ar.dev)
+    monkeypatch.setenv("QX_TEST_DEP_EXTRA", "1")
+    monkeypatch.setenv("QX_TIMEOUT_MS", "50")
+    _run(ar, q, inv, ids, tw, ws=ws)
+    assert device_status(ws) & _lib.QX_DEV_TIMEOUT
+    monkeypatch.delenv("QX_TEST_DEP_EXTRA")
+    monkeypatch.delenv("QX_TIMEOUT_MS")
+    out = _run(ar, q, inv, ids, tw, ws=ws)
+    assert device_status(ws) == 0
+    H.assert_parity(out, H.oracle_out(H.ingest(q, inv), ids, tw, layer, 0, 512), "after timeout")
+
+
+def _full_layer_case(dev, seed, rows, n_experts=384, bias=None, a0=0, a1=2304):
+    from qmesh_b200.arena import Arena
+    ar = Arena(dev, 1, n_experts, a0, a1)
+    ar.fill_synthetic(0, seed)
+    gen = torch.Generator().manual_seed(seed)
+    logits = torch.randn(rows, n_experts, generator=gen)
+    if bias is not None:
+        logits = logits + bias
+    ids, tw = moe.routing(logits)
+    _, q, inv = moe.make_activation(rows, gen)
+    return ar, ids, tw, q, inv
+
+
+def _check_full(ar, ids, tw, q, inv, c0, c1):
+    out = _run(ar, q, inv, ids, tw, c0=c0, c1=c1)
+    experts = sorted(set(ids.flatten().tolist()))
+    pack = ar.expert_pack(0, experts)
+    local = torch.tensor([experts.index(e) for e in ids.flatten().tolist()], dtype=torch.int32).view_as(ids)
+    ref = H.oracle_out(H.ingest(q, inv), local, tw, pack, c0 - ar.a0, c1 - ar.a0)
+    return H.assert_parity(out, ref, f"full layer rows={ids.shape[0]}"), len(experts)
+
+
+def test_config1_full_layer(cuda_ready):
+    """384 experts, rows=6, full columns, seed 1."""
+    ar, ids, tw, q, inv = _full_layer_case(cuda_ready, 1, 6)
+    p, u = _check_full(ar, ids, tw, q, inv, 0, 2304)
+    print("config1", p, "unique experts", u)
+
+
+def test_config3_zipf_rows48_shard(cuda_ready):
+    """BASELINE config 3 shape on one rank of the 8-way split: rows=48, Zipf bias."""
+    gen = torch.Generator().manual_seed(3)
+    bias = moe.zipf_bias(384, 1.1, gen)
+    ar, ids, tw, q, inv = _full_layer_case(cuda_ready, 3, 48, bias=bias, a0=2016, a1=2304)
+    p, u = _check_full(ar, ids, tw, q, inv, 2016, 2304)
+    print("config3 shard", p, "unique experts", u)
