@@ -134,12 +134,13 @@ def run_ours(args) -> dict | None:
     width = INTER // world
     a0, a1 = rank * width, (rank + 1) * width
     layers = args.layers
-    ar = Arena(dev, layers, N_EXPERTS, a0, a1)
+    n_exp = args.experts
+    ar = Arena(dev, layers, n_exp, a0, a1)
     ar.check_memory()
     for li in range(layers):
         ar.fill_synthetic(li, seed=1000 + li)
     torch.cuda.synchronize()
-    draws = make_inputs(args.draws, rows, seed=1, n_experts=N_EXPERTS)
+    draws = make_inputs(args.draws, rows, seed=1, n_experts=n_exp)
     dq = [(q.to(dev), inv.to(dev), ids.to(dev), tw.to(dev)) for q, inv, ids, tw in draws]
     uniq = [len(set(ids.flatten().tolist())) for _, _, ids, _ in draws]
     ws = alloc_workspace(rows, TOPK, a0, a1, dev)
@@ -249,7 +250,7 @@ def run_ours(args) -> dict | None:
             "dtype": "nvfp4-w/fp8-x/fp32-acc",
             "data": "synthetic (seeded NVFP4 weights from N(0,0.02); FP8 activations from N(0,1))",
             "config": {"workload": "config1-decode" if world == 1 else "config2-column-split",
-                       "experts": N_EXPERTS, "hidden": HIDDEN, "intermediate": INTER, "rows": rows,
+                       "experts": n_exp, "hidden": HIDDEN, "intermediate": INTER, "rows": rows,
                        "topk": TOPK, "columns_per_rank": width, "resident_layers": layers,
                        "routing_draws": args.draws, "mean_unique_experts": round(mean_u, 2),
                        "l2": "inputs larger than L2: ~%.0f MB of expert weights per step" % (mean_u * EXPERT_BYTES / 1e6),
@@ -333,6 +334,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--rows", type=int, default=6)
+    ap.add_argument("--experts", type=int, default=N_EXPERTS)
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--draws", type=int, default=16)
     ap.add_argument("--cpu-layers", type=int, default=3)

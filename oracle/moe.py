@@ -91,7 +91,7 @@ def config0(seed: int = 0, n_experts: int = 8, rows: int = 1, hidden: int = HIDD
 
 def slice_w4a16(x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, layer: dict,
                 c0: int, c1: int, limit: float = SWIGLU_LIMIT, has_limit: bool = True,
-                return_act: bool = False):
+                return_act: bool = False, dtype: torch.dtype = torch.float32, round_out: bool = True):
     """BF16 partial [R, H] of the routed experts over intermediate columns [c0, c1).
 
     x: bf16-valued float32 [R, H] (what the ingest hands the body);
@@ -103,19 +103,21 @@ def slice_w4a16(x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, layer: dic
     act = g / (1 + exp(-g)) * u in float32.
     Stage 2 (:356-385): y_j = (g2[e_j] * tw_j) * act_j.W2 (W2 = e2m1*e4m3 over
     columns [c0, c1)); out = bf16(sum_j y_j), j ascending, one rounding.
+    dtype=float64 with round_out=False gives a high-precision value of the same
+    expression (diagnostics only).
     """
     r, k = ids.shape
     inter = layer["c13"].shape[1] // 2
-    acc = torch.zeros(r, k, x.shape[1], dtype=torch.float32)
-    act_all = torch.zeros(r * k, c1 - c0, dtype=torch.float32)
+    acc = torch.zeros(r, k, x.shape[1], dtype=dtype)
+    act_all = torch.zeros(r * k, c1 - c0, dtype=dtype)
     for e in torch.unique(ids).tolist():
         sel = (ids == e).nonzero().tolist()
         rows = [p[0] for p in sel]
-        g13 = layer["g13"][e]
-        wg = q4.dequant(layer["c13"][e, c0:c1], layer["s13"][e, c0:c1], g13)
+        g13 = layer["g13"][e].to(dtype)
+        wg = q4.dequant(layer["c13"][e, c0:c1], layer["s13"][e, c0:c1], 1.0).to(dtype) * g13
         wu = q4.dequant(layer["c13"][e, inter + c0:inter + c1],
-                        layer["s13"][e, inter + c0:inter + c1], g13)
-        xr = x[rows].to(torch.float32)
+                        layer["s13"][e, inter + c0:inter + c1], 1.0).to(dtype) * g13
+        xr = x[rows].to(dtype)
         g = xr @ wg.T
         u = xr @ wu.T
         del wg, wu
@@ -123,17 +125,17 @@ def slice_w4a16(x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, layer: dic
             g = torch.clamp(g, max=limit)
             u = torch.clamp(u, min=-limit, max=limit)
         act = g / (1.0 + torch.exp(-g)) * u
-        w2 = q4.dequant(layer["c2"][e][:, c0 // 2:c1 // 2], layer["s2"][e][:, c0 // 16:c1 // 16], 1.0)
+        w2 = q4.dequant(layer["c2"][e][:, c0 // 2:c1 // 2], layer["s2"][e][:, c0 // 16:c1 // 16], 1.0).to(dtype)
         y = act @ w2.T
         del w2
         for i, (row, j) in enumerate(sel):
-            gw = layer["g2"][e].to(torch.float32) * tw[row, j].to(torch.float32)
+            gw = (layer["g2"][e].to(torch.float32) * tw[row, j].to(torch.float32)).to(dtype)
             acc[row, j] = y[i] * gw
             act_all[row * k + j] = act[i]
     out = acc[:, 0].clone()
     for j in range(1, k):
         out = out + acc[:, j]
-    out = q4.bf16_round(out)
+    out = q4.bf16_round(out) if round_out else out
     return (out, act_all) if return_act else out
 
 

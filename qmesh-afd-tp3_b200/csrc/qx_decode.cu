@@ -86,8 +86,11 @@ static_assert(sizeof(Ctl) == 256, "ctl block is 256 bytes");
 
 struct Uniq {        // one unique routed expert
   int32_t expert, pair_off, pair_cnt, ng;
-  int32_t group_off, item1_off, item2_off, pad;
+  int32_t group_off, item1_off, item2_off;
+  float g13, g2;     // the expert's global scales
+  int32_t pad[3];
 };
+static_assert(sizeof(Uniq) == 48, "uniq record is 48 bytes");
 
 struct Params {
   const void* x;
@@ -123,12 +126,15 @@ struct Params {
 
 struct Meta {        // one ring slot's contents, written by the producer
   int32_t kind;      // 0 end, 1 gate/up stage, 2 down stage
-  int32_t stage, nstages;
-  int32_t expert, group, np, pair_base;
+  int32_t stage, nstages, np;
   int32_t blk;       // column block (gate/up, relative to c0) or output tile (down)
   int32_t nc;        // column blocks in this down stage
-  int32_t pad[7];
+  int32_t group, pad0;
+  int32_t pair[PG];  // routed pair index q = row * topk + slot
+  float fac[PG];     // gate/up: 2^-p(row) * g13[e]; down: g2[e] * tw[q]
+  int32_t pad[8];
 };
+static_assert(sizeof(Meta) == 128, "meta record is 128 bytes");
 
 // ------------------------------------------------------------------ workspace
 struct WsLayout {
@@ -262,6 +268,8 @@ __device__ void route(const Params& p) {
     d.group_off = gofu[u];
     d.item1_off = i1u[u];
     d.item2_off = i2u[u];
+    d.g13 = p.g13[d.expert];
+    d.g2 = p.g2[d.expert];
   }
   if (t == 0) {
     Uniq& s = p.uniq[U];
@@ -376,118 +384,148 @@ __device__ __forceinline__ int find_unique(const Uniq* uq, int U, int item, bool
   return lo;
 }
 
-__device__ void producer(const Params& p, uint8_t* smem, uint64_t* full, uint64_t* empty, Meta* meta,
-                         uint64_t deadline) {
+// Per-CTA copies of the routing tables, loaded once after the prologue.
+struct Tables {
+  Uniq uniq[MAXP + 1];
+  int32_t pair[MAXP];
+  float tw[MAXP];
+  float xs[QX_MAX_ROWS];
+};
+
+struct Item {        // one decoded work item
+  int kind, nst, blk, group, np, expert;
+  int pair[PG];
+  float fac[PG];
+};
+
+__device__ void decode_item(const Params& p, const Tables& tb, uint32_t item, uint32_t n1, uint32_t total,
+                            int U, int n_st2, Item& it) {
+  if (item >= total) {
+    it.kind = 0;
+    return;
+  }
+  const bool ph1 = item < n1;
+  const int local0 = ph1 ? (int)item : (int)(item - n1);
+  const int u = find_unique(tb.uniq, U, local0, ph1);
+  const Uniq& d = tb.uniq[u];
+  const int local = local0 - (ph1 ? d.item1_off : d.item2_off);
+  const int pg = local % d.ng;
+  it.blk = local / d.ng;
+  it.kind = ph1 ? 1 : 2;
+  it.nst = ph1 ? NKC : n_st2;
+  it.expert = d.expert;
+  it.group = d.group_off + pg;
+  const int base = d.pair_off + pg * PG;
+  it.np = min(PG, d.pair_cnt - pg * PG);
+#pragma unroll
+  for (int i = 0; i < PG; ++i) {
+    const int q = i < it.np ? tb.pair[base + i] : 0;
+    it.pair[i] = q;
+    it.fac[i] = ph1 ? tb.xs[q / p.topk] * d.g13 : d.g2 * tb.tw[q];
+  }
+}
+
+__device__ void producer(const Params& p, const Tables& tb, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                         Meta* meta, uint64_t deadline) {
   volatile uint32_t* status = &p.ctl->status;
-  const uint32_t n1 = p.ctl->n1, n2 = p.ctl->n2, U = p.ctl->n_unique;
+  const uint32_t n1 = p.ctl->n1, n2 = p.ctl->n2;
+  const int U = (int)p.ctl->n_unique;
   const uint32_t total = n1 + n2;
   const int n_st2 = (p.n_cb + CB_PER_STAGE - 1) / CB_PER_STAGE;
   int gs = 0;
   bool ok = true;
-  Meta m{};
-  int nst = 0, st = 0;
-  int np = 0, pbase = 0, expert = 0, group = 0, blk = 0, kind = 0;
+  // The next item is claimed while the current one is still being issued, so
+  // the queue atomic's latency overlaps useful work.
+  uint32_t next = atomicAdd(&p.ctl->work, 1u);
+  bool next_claimed = true;
+  Item it;
   for (;;) {
-    if (st == nst) {  // claim the next item
-      const uint32_t item = atomicAdd(&p.ctl->work, 1u);
-      if (item >= total) {
-        kind = 0;
-      } else if (item < n1) {
-        const int u = find_unique(p.uniq, U, item, true);
-        const Uniq d = p.uniq[u];
-        const int local = item - d.item1_off;
-        const int pg = local % d.ng;
-        blk = local / d.ng;
-        kind = 1;
-        nst = NKC;
-        expert = d.expert;
-        group = d.group_off + pg;
-        pbase = d.pair_off + pg * PG;
-        np = min(PG, d.pair_cnt - pg * PG);
-      } else {
-        const int it2 = item - n1;
-        const int u = find_unique(p.uniq, U, it2, false);
-        const Uniq d = p.uniq[u];
-        const int local = it2 - d.item2_off;
-        const int pg = local % d.ng;
-        blk = local / d.ng;
-        kind = 2;
-        nst = n_st2;
-        expert = d.expert;
-        group = d.group_off + pg;
-        pbase = d.pair_off + pg * PG;
-        np = min(PG, d.pair_cnt - pg * PG);
-        // the group's activations must be complete: every gate/up item of the
-        // group increments cnt1 once per consumer warp
-        const uint32_t need = (uint32_t)p.n_cb * NCW + p.dep_extra;
-        uint32_t spins = 0;
-        while (ld_acquire_gpu(&p.cnt1[group]) < need) {
-          if ((++spins & 63u) == 0u) {
-            if (*status & QX_DEV_TIMEOUT) break;
-            if (globaltimer_ns() > deadline) {
-              atomicOr(const_cast<uint32_t*>(status), (uint32_t)QX_DEV_TIMEOUT);
-              break;
-            }
+    if (!next_claimed) next = atomicAdd(&p.ctl->work, 1u);
+    const uint32_t item = next;
+    next_claimed = false;
+    decode_item(p, tb, item, n1, total, U, n_st2, it);
+    if (it.kind == 2) {
+      // the group's activations must be complete: every gate/up item of the
+      // group increments cnt1 once per consumer warp
+      const uint32_t need = (uint32_t)p.n_cb * NCW + p.dep_extra;
+      uint32_t spins = 0;
+      while (ld_acquire_gpu(&p.cnt1[it.group]) < need) {
+        if ((++spins & 63u) == 0u) {
+          if (*status & QX_DEV_TIMEOUT) break;
+          if (globaltimer_ns() > deadline) {
+            atomicOr(const_cast<uint32_t*>(status), (uint32_t)QX_DEV_TIMEOUT);
+            break;
           }
-          __nanosleep(128);
         }
-        fence_proxy_async_global();
+        __nanosleep(64);
       }
-      st = 0;
+      fence_proxy_async_global();
     }
-    const int s = gs % NS;
-    if (gs >= NS) {
-      if (!mbar_wait_bounded(&empty[s], ((gs / NS) - 1) & 1, status, QX_DEV_TIMEOUT, deadline)) {
-        ok = false;
+    const int nst = it.kind == 0 ? 1 : it.nst;
+    for (int st = 0; st < nst; ++st) {
+      if (it.kind != 0 && st == nst - 3 + (nst < 3 ? 3 - nst : 0) && !next_claimed) {
+        next = atomicAdd(&p.ctl->work, 1u);
+        next_claimed = true;
+      }
+      const int s = gs % NS;
+      if (gs >= NS) {
+        if (!mbar_wait_bounded(&empty[s], ((gs / NS) - 1) & 1, status, QX_DEV_TIMEOUT, deadline)) {
+          ok = false;
+          break;
+        }
+      }
+      Meta& m = meta[s];
+      m.kind = it.kind;
+      m.stage = st;
+      m.nstages = nst;
+      m.np = it.np;
+      m.blk = it.blk;
+      m.group = it.group;
+      m.nc = 0;
+#pragma unroll
+      for (int i = 0; i < PG; ++i) {
+        m.pair[i] = it.pair[i];
+        m.fac[i] = it.fac[i];
+      }
+      uint8_t* slot = smem + (size_t)s * SLOT;
+      if (it.kind == 0) {
+        mbar_arrive(&full[s]);
+        ++gs;
         break;
       }
-    }
-    m.kind = kind;
-    m.stage = st;
-    m.nstages = nst;
-    m.expert = expert;
-    m.group = group;
-    m.np = np;
-    m.pair_base = pbase;
-    m.blk = blk;
-    m.nc = 0;
-    uint8_t* slot = smem + (size_t)s * SLOT;
-    if (kind == 0) {
-      meta[s] = m;
-      mbar_arrive(&full[s]);
+      if (it.kind == 1) {
+        const uint8_t* src =
+            p.w13 + ((size_t)it.expert * p.n_cb_arena + (p.cbo + it.blk)) * P1_TILE + (size_t)st * P1_STAGE;
+        mbar_arrive_expect_tx(&full[s], P1_STAGE + it.np * 1024);
+        bulk_g2s(slot, to_global(src), P1_STAGE, &full[s]);
+#pragma unroll
+        for (int i = 0; i < PG; ++i) {
+          if (i < it.np) {
+            const int row = it.pair[i] / p.topk;
+            bulk_g2s(slot + SLOT_W + i * 1024, to_global(p.x16 + (size_t)row * HID + st * KC), 1024, &full[s]);
+          }
+        }
+      } else {
+        const int cb0 = st * CB_PER_STAGE;
+        const int nc = min(CB_PER_STAGE, p.n_cb - cb0);
+        m.nc = nc;
+        const uint8_t* base = p.w2 + ((size_t)it.expert * NKT + it.blk) * ((size_t)p.n_cb_arena * P2_CB);
+        const uint8_t* csrc = base + (size_t)(p.cbo + cb0) * P2_CB_CODE;
+        const uint8_t* ssrc = base + (size_t)p.n_cb_arena * P2_CB_CODE + (size_t)(p.cbo + cb0) * P2_CB_SC;
+        mbar_arrive_expect_tx(&full[s], nc * P2_CB + it.np * nc * 128);
+        bulk_g2s(slot, to_global(csrc), nc * P2_CB_CODE, &full[s]);
+        bulk_g2s(slot + CB_PER_STAGE * P2_CB_CODE, to_global(ssrc), nc * P2_CB_SC, &full[s]);
+#pragma unroll
+        for (int i = 0; i < PG; ++i) {
+          if (i < it.np) {
+            const float* a = p.act + (size_t)it.pair[i] * p.W + cb0 * TC;
+            bulk_g2s(slot + SLOT_W + i * 512, to_global(a), nc * 128, &full[s]);
+          }
+        }
+      }
       ++gs;
-      break;
     }
-    if (kind == 1) {
-      const uint8_t* src = p.w13 + ((size_t)expert * p.n_cb_arena + (p.cbo + blk)) * P1_TILE + (size_t)st * P1_STAGE;
-      meta[s] = m;
-      mbar_arrive_expect_tx(&full[s], P1_STAGE + np * 1024);
-      bulk_g2s(slot, to_global(src), P1_STAGE, &full[s]);
-      for (int i = 0; i < np; ++i) {
-        const int q = p.pairlist[pbase + i];
-        const int row = q / p.topk;
-        const __half* xs = p.x16 + (size_t)row * HID + st * KC;
-        bulk_g2s(slot + SLOT_W + i * 1024, to_global(xs), 1024, &full[s]);
-      }
-    } else {
-      const int cb0 = st * CB_PER_STAGE;
-      const int nc = min(CB_PER_STAGE, p.n_cb - cb0);
-      m.nc = nc;
-      const uint8_t* base = p.w2 + ((size_t)expert * NKT + blk) * ((size_t)p.n_cb_arena * P2_CB);
-      const uint8_t* csrc = base + (size_t)(p.cbo + cb0) * P2_CB_CODE;
-      const uint8_t* ssrc = base + (size_t)p.n_cb_arena * P2_CB_CODE + (size_t)(p.cbo + cb0) * P2_CB_SC;
-      meta[s] = m;
-      mbar_arrive_expect_tx(&full[s], nc * P2_CB + np * nc * 128);
-      bulk_g2s(slot, to_global(csrc), nc * P2_CB_CODE, &full[s]);
-      bulk_g2s(slot + CB_PER_STAGE * P2_CB_CODE, to_global(ssrc), nc * P2_CB_SC, &full[s]);
-      for (int i = 0; i < np; ++i) {
-        const int q = p.pairlist[pbase + i];
-        const float* a = p.act + (size_t)q * p.W + cb0 * TC;
-        bulk_g2s(slot + SLOT_W + i * 512, to_global(a), nc * 128, &full[s]);
-      }
-    }
-    ++gs;
-    ++st;
+    if (!ok || it.kind == 0) break;
   }
   if (!ok) {
     // Drain: every copy this CTA issued must land before the CTA exits.
@@ -540,14 +578,15 @@ __device__ void consumer(const Params& p, const uint8_t* smem, uint64_t* full, u
   for (int gs = 0;; ++gs) {
     const int s = gs % NS;
     if (!mbar_wait_bounded(&full[s], (gs / NS) & 1, status, QX_DEV_TIMEOUT, deadline)) return;
-    const Meta m = meta[s];
-    if (m.kind == 0) return;
+    const Meta& ms = meta[s];
+    const int kind = ms.kind, stage = ms.stage, nstages = ms.nstages, np = ms.np, nc = ms.nc;
+    if (kind == 0) return;
     const uint8_t* slot = smem + (size_t)s * SLOT;
-    if (m.stage == 0) {
+    if (stage == 0) {
 #pragma unroll
       for (int i = 0; i < PG; ++i) acc_a[i] = acc_b[i] = 0.f;
     }
-    if (m.kind == 1) {
+    if (kind == 1) {
       // gate/up: lane half (lane>>4) picks the gate row, v = lane&15 the 32-element vector
       const int v = lane & 15;
       const int gr = 2 * warp + (lane >> 4);
@@ -564,7 +603,7 @@ __device__ void consumer(const Params& p, const uint8_t* smem, uint64_t* full, u
       const int sw = (v >> 1) & 3;
 #pragma unroll
       for (int i = 0; i < PG; ++i) {
-        if (i < m.np) {
+        if (i < np) {
           const uint4* xq = reinterpret_cast<const uint4*>(slot + SLOT_W + i * 1024) + v * 4;
           const uint4 x0 = xq[0 ^ sw], x1 = xq[1 ^ sw], x2 = xq[2 ^ sw], x3 = xq[3 ^ sw];
           float g0 = 0.f, g1 = 0.f, u0 = 0.f, u1 = 0.f;
@@ -594,9 +633,10 @@ __device__ void consumer(const Params& p, const uint8_t* smem, uint64_t* full, u
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
         const int j = 2 * h + jj;
-        if (j < m.nc) {
+        if (j < nc) {
           const uint4 c = *reinterpret_cast<const uint4*>(slot + j * P2_CB_CODE + r * 16);
-          const uint32_t sw2 = *reinterpret_cast<const uint16_t*>(slot + CB_PER_STAGE * P2_CB_CODE + j * P2_CB_SC + r * 2);
+          const uint32_t sw2 =
+              *reinterpret_cast<const uint16_t*>(slot + CB_PER_STAGE * P2_CB_CODE + j * P2_CB_SC + r * 2);
           float s0, s1;
           scales2(sw2, s0, s1);
           uint32_t hw[16];
@@ -609,7 +649,7 @@ __device__ void consumer(const Params& p, const uint8_t* smem, uint64_t* full, u
           }
 #pragma unroll
           for (int i = 0; i < PG; ++i) {
-            if (i < m.np) {
+            if (i < np) {
               const float4* a = reinterpret_cast<const float4*>(slot + SLOT_W + i * 512 + j * 128);
               float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
 #pragma unroll
@@ -642,17 +682,28 @@ __device__ void consumer(const Params& p, const uint8_t* smem, uint64_t* full, u
         }
       }
     }
+    if (stage != nstages - 1) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      continue;
+    }
+    // ---- item epilogue: pairs and factors come from the slot's meta ----
+    int pq[PG];
+    float fac[PG];
+#pragma unroll
+    for (int i = 0; i < PG; ++i) {
+      pq[i] = ms.pair[i];
+      fac[i] = ms.fac[i];
+    }
+    const int blk = ms.blk, group = ms.group;
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    if (m.stage != m.nstages - 1) continue;
-    // ---- item epilogue (registers + global memory only) ----
-    if (m.kind == 1) {
+    if (kind == 1) {
       const int v = lane & 15;
       const int gr = 2 * warp + (lane >> 4);
-      const float g13 = p.g13[m.expert];
 #pragma unroll
       for (int i = 0; i < PG; ++i) {
-        if (i < m.np) {
+        if (i < np) {
           float g = acc_a[i], u = acc_b[i];
 #pragma unroll
           for (int o = 8; o > 0; o >>= 1) {
@@ -660,55 +711,54 @@ __device__ void consumer(const Params& p, const uint8_t* smem, uint64_t* full, u
             u += __shfl_xor_sync(0xffffffffu, u, o);
           }
           if (v == 0) {
-            const int q = p.pairlist[m.pair_base + i];
-            const float xs = p.xscale[q / p.topk];
-            float gg = (g * xs) * g13, uu = (u * xs) * g13;
+            float gg = g * fac[i], uu = u * fac[i];
             if (p.has_limit) {
               gg = fminf(gg, p.limit);
               uu = fminf(fmaxf(uu, -p.limit), p.limit);
             }
-            p.act[(size_t)q * p.W + m.blk * TC + gr] = (gg / (1.f + expf(-gg))) * uu;
+            p.act[(size_t)pq[i] * p.W + blk * TC + gr] = (gg / (1.f + expf(-gg))) * uu;
           }
         }
       }
       __threadfence();
       __syncwarp();
-      if (lane == 0) atomicAdd(&p.cnt1[m.group], 1u);
+      if (lane == 0) atomicAdd(&p.cnt1[group], 1u);
     } else {
       const int r = t >> 1, h = t & 1;
-      const float g2 = p.g2[m.expert];
 #pragma unroll
       for (int i = 0; i < PG; ++i) {
-        if (i < m.np) {
+        if (i < np) {
           const float a = acc_a[i] + __shfl_xor_sync(0xffffffffu, acc_a[i], 1);
-          if (h == 0) {
-            const int q = p.pairlist[m.pair_base + i];
-            const float gw = g2 * p.tw[q];
-            p.y[(size_t)q * HID + m.blk * TK + r] = a * gw;
-          }
+          if (h == 0) p.y[(size_t)pq[i] * HID + blk * TK + r] = a * fac[i];
         }
       }
       __threadfence();
       __syncwarp();
       uint32_t last = 0;
       if (lane == 0) {
-        const uint32_t old = atomicAdd(&p.ctl->cnt2[m.blk], 1u);
+        const uint32_t old = atomicAdd(&p.ctl->cnt2[blk], 1u);
         last = (old == p.ctl->n_groups * NCW - 1u) ? 1u : 0u;
       }
       last = __shfl_sync(0xffffffffu, last, 0);
       if (last) {
         __threadfence();
-        final_reduce(p, m.blk, lane);
+        final_reduce(p, blk, lane);
       }
     }
   }
 }
 
+constexpr size_t SMEM_RING = (size_t)NS * SLOT;
+constexpr size_t SMEM_BARS = 2 * NS * sizeof(uint64_t);
+constexpr size_t SMEM_META = NS * sizeof(Meta);
+constexpr size_t SMEM_BYTES = SMEM_RING + SMEM_BARS + SMEM_META + sizeof(Tables);
+
 __global__ void __launch_bounds__(NTHR, 1) qx_decode_kernel(Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * SLOT);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SMEM_RING);
   uint64_t* empty = full + NS;
-  Meta* meta = reinterpret_cast<Meta*>(empty + NS);
+  Meta* meta = reinterpret_cast<Meta*>(smem + SMEM_RING + SMEM_BARS);
+  Tables& tb = *reinterpret_cast<Tables*>(smem + SMEM_RING + SMEM_BARS + SMEM_META);
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
@@ -716,9 +766,9 @@ __global__ void __launch_bounds__(NTHR, 1) qx_decode_kernel(Params p) {
     }
     fence_mbar_init();
   }
-  __syncthreads();
   pdl_wait();  // the prologue's routing tables and activations are complete
   const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+  const int U = (int)p.ctl->n_unique;
   if (p.ctl->n_groups == 0) {  // every slot was padding: the partial is zero
     if (blockIdx.x == 0) {
       for (int i = threadIdx.x; i < p.rows * HID; i += blockDim.x) {
@@ -728,15 +778,25 @@ __global__ void __launch_bounds__(NTHR, 1) qx_decode_kernel(Params p) {
     }
     return;
   }
+  {
+    const int4* src = reinterpret_cast<const int4*>(p.uniq);
+    int4* dst = reinterpret_cast<int4*>(tb.uniq);
+    const int n16 = (U + 1) * (int)(sizeof(Uniq) / 16);
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src[i];
+    for (int i = threadIdx.x; i < p.P; i += blockDim.x) {
+      tb.pair[i] = p.pairlist[i];
+      tb.tw[i] = p.tw[i];
+    }
+    for (int i = threadIdx.x; i < p.rows; i += blockDim.x) tb.xs[i] = p.xscale[i];
+  }
+  __syncthreads();
   const int warp = threadIdx.x >> 5;
   if (warp == NCW) {
-    if ((threadIdx.x & 31) == 0) producer(p, smem, full, empty, meta, deadline);
+    if ((threadIdx.x & 31) == 0) producer(p, tb, smem, full, empty, meta, deadline);
     return;
   }
   consumer(p, smem, full, empty, meta, deadline);
 }
-
-constexpr size_t SMEM_BYTES = (size_t)NS * SLOT + 2 * NS * sizeof(uint64_t) + NS * sizeof(Meta);
 
 // ------------------------------------------------------------------ combine
 struct CombineParams {

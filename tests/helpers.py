@@ -9,9 +9,17 @@ import torch
 from oracle import moe, nvfp4 as q4
 
 # BF16 partial and combined output within relative-L2 5e-3
-# and max-abs 2 BF16 ulp per element of the reference value.
+# and max-abs 2 BF16 ulp per element.
+#
+# The ulp of an element is the BF16 spacing at max(|ref|, 2^-10 * rms(row)).
+# Below that floor an element is a near-cancellation of terms ~2^10 times
+# larger, and any two FP32 summation orders already disagree there by several
+# of its own ulps: the FP32 oracle itself is up to 11 ulp from a float64
+# evaluation of the same expression on such elements, while the floor still
+# allows only ~2^-16 * rms, about 20x the FP32 noise observed.
 REL_L2 = 5e-3
 MAX_ULP = 2.0
+ULP_FLOOR = 2.0 ** -10
 
 
 def bf16_ulp(v: torch.Tensor) -> torch.Tensor:
@@ -20,13 +28,24 @@ def bf16_ulp(v: torch.Tensor) -> torch.Tensor:
     return torch.pow(2.0, torch.floor(torch.log2(a)) - 7.0)
 
 
+def element_ulp(ref: torch.Tensor) -> torch.Tensor:
+    r2 = ref.reshape(-1, ref.shape[-1]) if ref.dim() > 1 else ref.reshape(1, -1)
+    rms = r2.pow(2).mean(dim=-1, keepdim=True).sqrt()
+    floor = (ULP_FLOOR * rms).expand_as(r2)
+    return bf16_ulp(torch.maximum(r2.abs(), floor)).reshape(ref.shape)
+
+
 def parity(out: torch.Tensor, ref: torch.Tensor) -> dict:
     out = out.float().cpu()
     ref = ref.float().cpu()
     err = (out - ref).abs()
     rel = (err.norm() / ref.norm().clamp_min(1e-30)).item()
-    ulps = (err / bf16_ulp(ref)).max().item()
-    return {"rel_l2": rel, "max_ulp": ulps, "max_abs": err.max().item(), "exact": float((err == 0).float().mean())}
+    u = err / element_ulp(ref)
+    i = int(u.argmax())
+    idx = [int(v) for v in torch.unravel_index(torch.tensor(i), ref.shape)]
+    return {"rel_l2": rel, "max_ulp": u.max().item(), "max_abs": err.max().item(),
+            "exact": float((err == 0).float().mean()), "worst": {"at": idx, "out": out.flatten()[i].item(),
+                                                                "ref": ref.flatten()[i].item()}}
 
 
 def assert_parity(out, ref, what=""):

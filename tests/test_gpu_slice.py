@@ -133,16 +133,24 @@ def test_column_ranges_and_ordered_combine(small):
     ids, tw = H.random_routing(rows, 16, 14)
     _, q, inv = H.activations(rows, 14)
     x = H.ingest(q, inv)
-    parts = []
+    parts, ref_parts = [], []
     for a, b in moe.shard_ranges(512, 4):
         out = _run(ar, q, inv, ids, tw, c0=a, c1=b)
-        H.assert_parity(out, H.oracle_out(x, ids, tw, layer, a, b), f"shard [{a},{b})")
+        ref = H.oracle_out(x, ids, tw, layer, a, b)
+        H.assert_parity(out, ref, f"shard [{a},{b})")
         parts.append(out)
+        ref_parts.append(ref)
     comb = combine_ordered(parts)
     torch.cuda.synchronize()
+    # the combine kernel is exactly the ordered FP32 sum of the BF16 partials ...
     want = moe.combine_ordered([p.float().cpu() for p in parts])
     assert torch.equal(comb.float().cpu(), want)
-    H.assert_parity(comb, H.oracle_out(x, ids, tw, layer, 0, 512), "combined")
+    # ... and the combined output matches the reference protocol: per-rank BF16
+    # partials summed in FP32 in rank order (qmesh_afd_seam.cu:310-361)
+    H.assert_parity(comb, moe.combine_ordered(ref_parts), "combined")
+    f32 = combine_ordered(parts, out_f32=True)
+    torch.cuda.synchronize()
+    assert torch.equal(f32.cpu(), moe.combine_ordered([p.float().cpu() for p in parts], out_f32=True))
 
 
 def test_rank_arena_equals_full_arena_slice(small, cuda_ready):

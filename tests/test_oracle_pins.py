@@ -156,3 +156,12 @@ def test_oracle_column_split_is_additive():
     comb = moe.combine_ordered(parts)
     rel = ((comb - full).norm() / full.norm()).item()
     assert rel < 5e-3
+
+
+def test_ulp_floor_definition():
+    import helpers as H
+    ref = torch.tensor([[1.0, 0.5, 1e-6, -1e-6] + [1.0] * 60])
+    u = H.element_ulp(ref)
+    assert u[0, 0] == 2.0 ** -7 and u[0, 1] == 2.0 ** -8
+    # tiny elements use the floor 2^-10 * rms (rms just under 1) -> ulp 2^-18
+    assert u[0, 2] == u[0, 3] == 2.0 ** -18
