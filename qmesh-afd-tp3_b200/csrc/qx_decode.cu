@@ -5,21 +5,27 @@
 //
 //   qx_prep_kernel    one CTA per activation row: e4m3 (or bf16) -> the
 //                     reference's bf16 activation (gx/gx_ingest.py:151-154),
-//                     held as f16 scaled by an exact power of two; plus one
-//                     routing CTA that deduplicates experts over all rows and
-//                     builds the work list (pairs grouped by expert).
+//                     held as f16 scaled by an exact power of two in MMA
+//                     fragment order; plus one routing CTA that deduplicates
+//                     experts over all rows and builds the work list.
 //   qx_decode_kernel  persistent, one CTA per SM, warp-specialised: a producer
 //                     warp streams each unique expert's weight tiles once with
 //                     bulk async copies (TMA engine) into a 6-slot shared-memory
-//                     ring; 16 consumer warps dequantise in registers and run
-//                     the dot products for every row routed to that expert.
+//                     ring; 16 consumer warps dequantise each NVFP4 weight once
+//                     in registers (e2m1 x e4m3 block scale, exact in f16) and
+//                     feed it to register-sourced tensor-core MMAs
+//                     (m16n8k16, f16 in, f32 accumulate) against every row
+//                     routed to that expert (up to 8 per MMA).
 //                     Work items come from one atomic queue: first the gate/up
 //                     items (expert, 32-column block), then the down items
-//                     (expert, 256-row output tile). A down item waits (bounded)
-//                     for its expert's gate/up items through per-group counters,
-//                     so the two phases overlap instead of meeting at a grid
-//                     barrier. The warp that completes an output tile last sums
-//                     the per-slot partials in slot order and rounds to BF16 once.
+//                     (expert, 256-row output tile, <= 1152-column sub-range). A
+//                     down item waits (bounded) for its expert's gate/up items
+//                     through per-group counters, so the two phases overlap
+//                     instead of meeting at a grid barrier.
+//   qx_finalize_kernel  sums the per-slot down-projection partials of every row
+//                     in slot order and rounds to BF16 once; launched with
+//                     programmatic dependent launch so it is resident before the
+//                     weight-streaming kernel finishes.
 //
 // Numerics (identical in meaning to the reference's decode path):
 //   x      = bf16(float(e4m3) * inv)                       gx_ingest.py:151-154
@@ -28,11 +34,12 @@
 //   act    = (min(g,L) / (1 + exp(-min(g,L)))) * clamp(u,-L,L)   :295-299
 //   y_j    = (g2[e_j] * tw_j) * sum_c act_c w2_c           :356-385
 //   out    = bf16(y_0 + y_1 + ... + y_{k-1})  slot order, one rounding
-// The gate/up dot runs on f16 operands with FP32 accumulation: x is held as
-// x * 2^p in f16 (exact, since a bf16 row decoded from e4m3 spans < 2^18 and p
-// puts its maximum in [2^14, 2^15)), e2m1 values are exact in f16, and every
-// f16 x f16 product is exact in FP32. The down dot widens the e2m1 codes to
-// FP32 and keeps the FP32 activation, as the reference does.
+// Exactness of the f16 operands: e2m1 * e4m3 has at most 6 significant bits and
+// lies in [2^-10, 2688], so w is exact in f16; x is held as x * 2^p with the
+// row maximum in [2^14, 2^15), exact because a bf16 row decoded from e4m3 spans
+// less than 2^18; f16 x f16 products are exact in the FP32 accumulator. The
+// down projection's FP32 activation enters as two f16 terms (hi + lo, 22
+// significant bits) scaled by a power of two chosen from the SwiGLU clamp.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -45,12 +52,11 @@
 namespace qx {
 
 constexpr int HID = QX_HIDDEN;            // 5120
-constexpr int KC = 512;                   // gate/up K chunk per stage (elements)
-constexpr int NKC = HID / KC;             // 10 stages per gate/up item
 constexpr int TC = 32;                    // intermediate columns per block
-constexpr int P1_ROWS = 2 * TC;           // 32 gate rows then 32 up rows
-constexpr int P1_CODE = P1_ROWS * KC / 2; // 16384 code bytes per stage
-constexpr int P1_SC = P1_ROWS * KC / 16;  // 2048 scale bytes per stage
+constexpr int KC = 512;                   // gate/up K per stage (elements)
+constexpr int NKC = HID / KC;             // 10 stages per gate/up item
+constexpr int P1_CODE = 2 * TC * KC / 2;  // 16384 code bytes per stage
+constexpr int P1_SC = 2 * TC * KC / 16;   // 2048 scale bytes per stage
 constexpr int P1_STAGE = P1_CODE + P1_SC; // 18432
 constexpr int P1_TILE = NKC * P1_STAGE;   // 184320 bytes per (expert, column block)
 constexpr int TK = 256;                   // down-projection output rows per item
@@ -59,11 +65,12 @@ constexpr int P2_CB_CODE = TK * 16;       // 4096 code bytes per (row tile, colu
 constexpr int P2_CB_SC = TK * 2;          // 512 scale bytes
 constexpr int P2_CB = P2_CB_CODE + P2_CB_SC;
 constexpr int CB_PER_STAGE = 4;           // column blocks per down stage
-constexpr int PG = 8;                     // routed pairs per group (one item serves a group)
+constexpr int SUB_CB = 36;                // column blocks per down item (1152 columns)
+constexpr int PG = 8;                     // routed pairs per group = MMA N
 constexpr int NS = 6;                     // ring slots
 constexpr int SLOT_W = 18432;             // weight bytes per slot
-constexpr int SLOT_A = PG * 1024;         // activation bytes per slot
-constexpr int SLOT = SLOT_W + SLOT_A;     // 26624
+constexpr int XPITCH = 1024 + 16;         // activation bytes per pair in a slot (+16: bank shift)
+constexpr int SLOT = SLOT_W + PG * XPITCH;
 constexpr int NCW = 16;                   // consumer warps
 constexpr int NTHR = (NCW + 1) * 32;      // + one producer warp
 constexpr int MAXP = QX_MAX_ROWS * QX_MAX_TOPK;
@@ -71,6 +78,7 @@ constexpr int MAXE = 4096;
 
 static_assert(CB_PER_STAGE * P2_CB == SLOT_W, "down stage must fill the weight slot");
 static_assert(P1_STAGE == SLOT_W, "gate/up stage must fill the weight slot");
+static_assert(SLOT % 16 == 0 && XPITCH % 16 == 0, "bulk copy destinations are 16-byte aligned");
 
 struct Ctl {
   uint32_t work;      // next work item
@@ -79,7 +87,7 @@ struct Ctl {
   uint32_t n_groups;
   uint32_t n1, n2;    // gate/up items, down items
   uint32_t pad[10];
-  uint32_t cnt2[NKT]; // warps finished per output tile
+  uint32_t cnt2[NKT]; // reserved
   uint32_t pad2[64 - 16 - NKT];
 };
 static_assert(sizeof(Ctl) == 256, "ctl block is 256 bytes");
@@ -101,7 +109,7 @@ struct Params {
   int ids64;
   const float* tw;
   int rows, topk, P;
-  int cbo, n_cb, n_cb_arena, W;
+  int cbo, n_cb, n_cb_arena, W, n_sub;
   const uint8_t* w13;
   const uint8_t* w2;
   const float* g13;
@@ -109,6 +117,7 @@ struct Params {
   int E;
   float limit;
   int has_limit;
+  float act_scale, act_unscale;  // power of two applied to the stored activation
   __nv_bfloat16* out;
   int64_t out_stride;
   Ctl* ctl;
@@ -117,24 +126,29 @@ struct Params {
   int32_t* pairlist;
   int32_t* pexp;
   float* xscale;
-  __half* x16;
-  float* act;
-  float* y;
+  uint8_t* x16;      // per row: f16 x * 2^p in MMA B-fragment order (10,240 B)
+  uint8_t* act;      // per pair: (hi, lo) f16 activation in B-fragment order (4 B/column)
+  float* y;          // [P][n_sub][HID]
   uint64_t timeout_ns;
   uint32_t dep_extra;  // test hook: extra arrivals a down item waits for (0 in service)
 };
 
-struct Meta {        // one ring slot's contents, written by the producer
-  int32_t kind;      // 0 end, 1 gate/up stage, 2 down stage
-  int32_t stage, nstages, np;
-  int32_t blk;       // column block (gate/up, relative to c0) or output tile (down)
-  int32_t nc;        // column blocks in this down stage
-  int32_t group, pad0;
+struct ItemMeta {    // one work item's description, written once by the producer
+  int32_t kind;      // 1 gate/up, 2 down
+  int32_t nstages, np;
+  int32_t blk;       // gate/up: column block (relative to c0); down: kt * n_sub + sub
+  int32_t group;
+  int32_t nc_last;   // down: column blocks in the last stage
+  int32_t pad0, pad1;
   int32_t pair[PG];  // routed pair index q = row * topk + slot
   float fac[PG];     // gate/up: 2^-p(row) * g13[e]; down: g2[e] * tw[q]
   int32_t pad[8];
 };
-static_assert(sizeof(Meta) == 128, "meta record is 128 bytes");
+static_assert(sizeof(ItemMeta) == 128, "item record is 128 bytes");
+// Item records in flight: the producer runs at most NS stages ahead of the
+// slowest consumer and every item has at least one stage, so NS + 2 entries
+// guarantee an entry is rewritten only after every consumer released it.
+constexpr int NI = NS + 2;
 
 // ------------------------------------------------------------------ workspace
 struct WsLayout {
@@ -143,9 +157,12 @@ struct WsLayout {
 
 __host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
+__host__ inline int n_sub_of(int n_cb) { return (n_cb + SUB_CB - 1) / SUB_CB; }
+
 __host__ inline WsLayout ws_layout(int rows, int topk, int W) {
   WsLayout L;
   const size_t P = (size_t)rows * topk;
+  const int nsub = n_sub_of(W / TC);
   size_t o = 0;
   L.ctl = o;      o = align256(o + sizeof(Ctl));
   L.cnt1 = o;     o = align256(o + MAXP * sizeof(uint32_t));
@@ -153,11 +170,22 @@ __host__ inline WsLayout ws_layout(int rows, int topk, int W) {
   L.pairlist = o; o = align256(o + MAXP * sizeof(int32_t));
   L.pexp = o;     o = align256(o + MAXP * sizeof(int32_t));
   L.xscale = o;   o = align256(o + (size_t)rows * sizeof(float));
-  L.x16 = o;      o = align256(o + (size_t)rows * HID * sizeof(__half));
-  L.act = o;      o = align256(o + P * (size_t)W * sizeof(float));
-  L.y = o;        o = align256(o + P * (size_t)HID * sizeof(float));
+  L.x16 = o;      o = align256(o + (size_t)rows * HID * 2);
+  L.act = o;      o = align256(o + P * (size_t)W * 4);
+  L.y = o;        o = align256(o + P * (size_t)nsub * HID * sizeof(float));
   L.total = o;
   return L;
+}
+
+// ------------------------------------------------------------------ fragment maps
+// Byte offset of the f16 pair (k, k+1), k even, inside a 512-element chunk of
+// B-fragment-ordered data: step i = k/16 holds, for thread-in-group t, the words
+// w0 = (2t, 2t+1) and w1 = (2t+8, 2t+9); two steps share one 16-byte unit per t:
+// unit (step pair sp, t) = [w0(2sp), w1(2sp), w0(2sp+1), w1(2sp+1)].
+__host__ __device__ __forceinline__ int frag_word_off(int k) {
+  const int i = k >> 4, e = k & 15;
+  const int t = (e & 7) >> 1, word = e >> 3;
+  return (i >> 1) * 64 + t * 16 + ((i & 1) * 2 + word) * 4;
 }
 
 // ------------------------------------------------------------------ prologue
@@ -224,7 +252,6 @@ __device__ void route(const Params& p) {
   __syncthreads();
   for (int i = t; i < nw; i += blockDim.x) wpref[i] = __popc(bits[i]);
   __syncthreads();
-  // nw <= 128 words: the 512-element scan covers it
   const int U = block_scan_excl(wpref, nw, wt);
   for (int i = t; i < nw; i += blockDim.x) {
     uint32_t w = bits[i];
@@ -250,7 +277,7 @@ __device__ void route(const Params& p) {
     ngu[u] = (cntu[u] + PG - 1) / PG;
     gofu[u] = ngu[u];
     i1u[u] = ngu[u] * p.n_cb;
-    i2u[u] = ngu[u] * NKT;
+    i2u[u] = ngu[u] * NKT * p.n_sub;
   }
   __syncthreads();
   block_scan_excl(offu, U, wt);
@@ -282,14 +309,11 @@ __device__ void route(const Params& p) {
   }
 }
 
-// x row -> bf16 value (reference ingest) -> f16 * 2^p, stored in the chunk
-// layout the gate/up consumers read: chunk kc (512 elements), 16-byte unit
-// (v, q) of element 32v + 8q at unit v*4 + (q ^ ((v >> 1) & 3)), which spreads
-// the 16 lanes of a half-warp over all shared-memory bank groups.
+// x row -> bf16 value (reference ingest) -> f16 * 2^p in B-fragment order.
 __device__ void convert_row(const Params& p, int r) {
   __shared__ float red[8];
   const int t = threadIdx.x;
-  constexpr int UNITS = HID / 8;  // 640
+  constexpr int UNITS = HID / 8;  // 640 units of 8 consecutive elements
   float v[3][8];
   float amax = 0.f;
   float inv = 1.f;
@@ -345,17 +369,18 @@ __device__ void convert_row(const Params& p, int r) {
   }
   const float sc = ldexpf(1.f, pw);
   if (t == 0) p.xscale[r] = ldexpf(1.f, -pw);
-  __half* dst = p.x16 + (size_t)r * HID;
+  uint8_t* dst = p.x16 + (size_t)r * HID * 2;
 #pragma unroll
   for (int j = 0; j < 3; ++j) {
     const int u = t + 256 * j;
     if (u < UNITS) {
-      const int kc = u >> 6, ui = u & 63, vv = ui >> 2, q = ui & 3;
-      const int pos = vv * 4 + (q ^ ((vv >> 1) & 3));
-      __align__(16) __half h[8];
+      const int k0 = u * 8;
+      uint8_t* chunk = dst + (k0 / KC) * (KC * 2);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(v[j][e] * sc);
-      *reinterpret_cast<uint4*>(dst + kc * KC + pos * 8) = *reinterpret_cast<const uint4*>(h);
+      for (int e = 0; e < 8; e += 2) {
+        const __half2 h = __floats2half2_rn(v[j][e] * sc, v[j][e + 1] * sc);
+        *reinterpret_cast<__half2*>(chunk + frag_word_off((k0 + e) % KC)) = h;
+      }
     }
   }
 }
@@ -375,7 +400,7 @@ __device__ __forceinline__ const void* to_global(const void* p) {
 
 // Unique-expert index u with item_off[u] <= item < item_off[u+1].
 __device__ __forceinline__ int find_unique(const Uniq* uq, int U, int item, bool phase1) {
-  int lo = 0, hi = U;  // invariant: off(lo) <= item < off(hi)
+  int lo = 0, hi = U;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     const int off = phase1 ? uq[mid].item1_off : uq[mid].item2_off;
@@ -393,13 +418,28 @@ struct Tables {
 };
 
 struct Item {        // one decoded work item
-  int kind, nst, blk, group, np, expert;
+  int kind, nst, blk, group, np, expert, cb_first, n_cbs;
   int pair[PG];
   float fac[PG];
 };
 
+// it.pair[i] / it.fac[i] for a lane-dependent i without indexing a register
+// array dynamically (which would move it to local memory).
+__device__ __forceinline__ int pick_pair(const Item& it, int i) {
+  int v = 0;
+#pragma unroll
+  for (int k = 0; k < PG; ++k) v = (k == i) ? it.pair[k] : v;
+  return v;
+}
+__device__ __forceinline__ float pick_fac(const Item& it, int i) {
+  float v = 0.f;
+#pragma unroll
+  for (int k = 0; k < PG; ++k) v = (k == i) ? it.fac[k] : v;
+  return v;
+}
+
 __device__ void decode_item(const Params& p, const Tables& tb, uint32_t item, uint32_t n1, uint32_t total,
-                            int U, int n_st2, Item& it) {
+                            int U, Item& it) {
   if (item >= total) {
     it.kind = 0;
     return;
@@ -412,7 +452,16 @@ __device__ void decode_item(const Params& p, const Tables& tb, uint32_t item, ui
   const int pg = local % d.ng;
   it.blk = local / d.ng;
   it.kind = ph1 ? 1 : 2;
-  it.nst = ph1 ? NKC : n_st2;
+  if (ph1) {
+    it.nst = NKC;
+    it.cb_first = it.blk;
+    it.n_cbs = 1;
+  } else {
+    const int sub = it.blk % p.n_sub;
+    it.cb_first = sub * SUB_CB;
+    it.n_cbs = min(SUB_CB, p.n_cb - it.cb_first);
+    it.nst = (it.n_cbs + CB_PER_STAGE - 1) / CB_PER_STAGE;
+  }
   it.expert = d.expert;
   it.group = d.group_off + pg;
   const int base = d.pair_off + pg * PG;
@@ -426,108 +475,134 @@ __device__ void decode_item(const Params& p, const Tables& tb, uint32_t item, ui
 }
 
 __device__ void producer(const Params& p, const Tables& tb, uint8_t* smem, uint64_t* full, uint64_t* empty,
-                         Meta* meta, uint64_t deadline) {
+                         ItemMeta* imeta, int32_t* smeta, uint64_t deadline) {
+  // The whole warp runs this loop in lockstep: lane 0 owns the queue, the
+  // barriers and the weight copies; lane i < np issues pair i's activation copy.
   volatile uint32_t* status = &p.ctl->status;
+  const int lane = threadIdx.x & 31;
   const uint32_t n1 = p.ctl->n1, n2 = p.ctl->n2;
   const int U = (int)p.ctl->n_unique;
   const uint32_t total = n1 + n2;
-  const int n_st2 = (p.n_cb + CB_PER_STAGE - 1) / CB_PER_STAGE;
-  int gs = 0;
+  int gs = 0, item_seq = 0;
   bool ok = true;
-  // The next item is claimed while the current one is still being issued, so
-  // the queue atomic's latency overlaps useful work.
-  uint32_t next = atomicAdd(&p.ctl->work, 1u);
+  uint32_t next = 0;
+  if (lane == 0) next = atomicAdd(&p.ctl->work, 1u);
+  next = __shfl_sync(0xffffffffu, next, 0);
   bool next_claimed = true;
   Item it;
   for (;;) {
-    if (!next_claimed) next = atomicAdd(&p.ctl->work, 1u);
+    if (!next_claimed) {
+      if (lane == 0) next = atomicAdd(&p.ctl->work, 1u);
+      next = __shfl_sync(0xffffffffu, next, 0);
+    }
     const uint32_t item = next;
     next_claimed = false;
-    decode_item(p, tb, item, n1, total, U, n_st2, it);
+    decode_item(p, tb, item, n1, total, U, it);
     if (it.kind == 2) {
       // the group's activations must be complete: every gate/up item of the
-      // group increments cnt1 once per consumer warp
-      const uint32_t need = (uint32_t)p.n_cb * NCW + p.dep_extra;
-      uint32_t spins = 0;
-      while (ld_acquire_gpu(&p.cnt1[it.group]) < need) {
-        if ((++spins & 63u) == 0u) {
-          if (*status & QX_DEV_TIMEOUT) break;
-          if (globaltimer_ns() > deadline) {
-            atomicOr(const_cast<uint32_t*>(status), (uint32_t)QX_DEV_TIMEOUT);
-            break;
+      // group increments cnt1 once per 16-row tile (4 per item)
+      if (lane == 0) {
+        const uint32_t need = (uint32_t)p.n_cb * 4 + p.dep_extra;
+        uint32_t spins = 0;
+        while (ld_acquire_gpu(&p.cnt1[it.group]) < need) {
+          if ((++spins & 63u) == 0u) {
+            if (*status & QX_DEV_TIMEOUT) break;
+            if (globaltimer_ns() > deadline) {
+              atomicOr(const_cast<uint32_t*>(status), (uint32_t)QX_DEV_TIMEOUT);
+              break;
+            }
           }
+          __nanosleep(64);
         }
-        __nanosleep(64);
       }
+      __syncwarp();
       fence_proxy_async_global();
     }
     const int nst = it.kind == 0 ? 1 : it.nst;
+    const int claim_at = nst > 3 ? nst - 3 : 0;
+    const int ri = item_seq % NI;
     for (int st = 0; st < nst; ++st) {
-      if (it.kind != 0 && st == nst - 3 + (nst < 3 ? 3 - nst : 0) && !next_claimed) {
-        next = atomicAdd(&p.ctl->work, 1u);
+      if (it.kind != 0 && st == claim_at && !next_claimed) {
+        if (lane == 0) next = atomicAdd(&p.ctl->work, 1u);
+        next = __shfl_sync(0xffffffffu, next, 0);
         next_claimed = true;
       }
       const int s = gs % NS;
       if (gs >= NS) {
-        if (!mbar_wait_bounded(&empty[s], ((gs / NS) - 1) & 1, status, QX_DEV_TIMEOUT, deadline)) {
+        int w_ok = 1;
+        if (lane == 0) w_ok = mbar_wait_bounded(&empty[s], ((gs / NS) - 1) & 1, status, QX_DEV_TIMEOUT, deadline);
+        if (!__shfl_sync(0xffffffffu, w_ok, 0)) {
           ok = false;
           break;
         }
       }
-      Meta& m = meta[s];
-      m.kind = it.kind;
-      m.stage = st;
-      m.nstages = nst;
-      m.np = it.np;
-      m.blk = it.blk;
-      m.group = it.group;
-      m.nc = 0;
-#pragma unroll
-      for (int i = 0; i < PG; ++i) {
-        m.pair[i] = it.pair[i];
-        m.fac[i] = it.fac[i];
-      }
       uint8_t* slot = smem + (size_t)s * SLOT;
       if (it.kind == 0) {
-        mbar_arrive(&full[s]);
+        if (lane == 0) {
+          smeta[s] = -1;
+          mbar_arrive(&full[s]);
+        }
         ++gs;
         break;
       }
+      if (st == 0) {  // the item's metadata, once (its ring entry is free: see NI)
+        ItemMeta& im = imeta[ri];
+        if (lane < PG) {
+          im.pair[lane] = pick_pair(it, lane);
+          im.fac[lane] = pick_fac(it, lane);
+        }
+        if (lane == 0) {
+          im.kind = it.kind;
+          im.nstages = nst;
+          im.np = it.np;
+          im.blk = it.blk;
+          im.group = it.group;
+          im.nc_last = it.kind == 2 ? it.n_cbs - (nst - 1) * CB_PER_STAGE : 0;
+        }
+      }
       if (it.kind == 1) {
-        const uint8_t* src =
-            p.w13 + ((size_t)it.expert * p.n_cb_arena + (p.cbo + it.blk)) * P1_TILE + (size_t)st * P1_STAGE;
-        mbar_arrive_expect_tx(&full[s], P1_STAGE + it.np * 1024);
-        bulk_g2s(slot, to_global(src), P1_STAGE, &full[s]);
-#pragma unroll
-        for (int i = 0; i < PG; ++i) {
-          if (i < it.np) {
-            const int row = it.pair[i] / p.topk;
-            bulk_g2s(slot + SLOT_W + i * 1024, to_global(p.x16 + (size_t)row * HID + st * KC), 1024, &full[s]);
-          }
+        if (lane == 0) {
+          smeta[s] = (ri << 16) | st;
+          mbar_arrive_expect_tx(&full[s], P1_STAGE + it.np * (KC * 2));
+        }
+        __syncwarp();
+        if (lane == 0) {
+          const uint8_t* src =
+              p.w13 + ((size_t)it.expert * p.n_cb_arena + (p.cbo + it.blk)) * P1_TILE + (size_t)st * P1_STAGE;
+          bulk_g2s(slot, to_global(src), P1_STAGE, &full[s]);
+        }
+        if (lane < it.np) {
+          const int row = pick_pair(it, lane) / p.topk;
+          bulk_g2s(slot + SLOT_W + lane * XPITCH, to_global(p.x16 + (size_t)row * HID * 2 + st * (KC * 2)), KC * 2,
+                   &full[s]);
         }
       } else {
-        const int cb0 = st * CB_PER_STAGE;
-        const int nc = min(CB_PER_STAGE, p.n_cb - cb0);
-        m.nc = nc;
-        const uint8_t* base = p.w2 + ((size_t)it.expert * NKT + it.blk) * ((size_t)p.n_cb_arena * P2_CB);
-        const uint8_t* csrc = base + (size_t)(p.cbo + cb0) * P2_CB_CODE;
-        const uint8_t* ssrc = base + (size_t)p.n_cb_arena * P2_CB_CODE + (size_t)(p.cbo + cb0) * P2_CB_SC;
-        mbar_arrive_expect_tx(&full[s], nc * P2_CB + it.np * nc * 128);
-        bulk_g2s(slot, to_global(csrc), nc * P2_CB_CODE, &full[s]);
-        bulk_g2s(slot + CB_PER_STAGE * P2_CB_CODE, to_global(ssrc), nc * P2_CB_SC, &full[s]);
-#pragma unroll
-        for (int i = 0; i < PG; ++i) {
-          if (i < it.np) {
-            const float* a = p.act + (size_t)it.pair[i] * p.W + cb0 * TC;
-            bulk_g2s(slot + SLOT_W + i * 512, to_global(a), nc * 128, &full[s]);
-          }
+        const int cb0 = it.cb_first + st * CB_PER_STAGE;
+        const int nc = min(CB_PER_STAGE, it.cb_first + it.n_cbs - cb0);
+        if (lane == 0) {
+          smeta[s] = (ri << 16) | st;
+          mbar_arrive_expect_tx(&full[s], nc * P2_CB + it.np * nc * 128);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          const int kt = it.blk / p.n_sub;
+          const uint8_t* base = p.w2 + ((size_t)it.expert * NKT + kt) * ((size_t)p.n_cb_arena * P2_CB);
+          bulk_g2s(slot, to_global(base + (size_t)(p.cbo + cb0) * P2_CB_CODE), nc * P2_CB_CODE, &full[s]);
+          bulk_g2s(slot + CB_PER_STAGE * P2_CB_CODE,
+                   to_global(base + (size_t)p.n_cb_arena * P2_CB_CODE + (size_t)(p.cbo + cb0) * P2_CB_SC),
+                   nc * P2_CB_SC, &full[s]);
+        }
+        if (lane < it.np) {
+          const uint8_t* a = p.act + (size_t)pick_pair(it, lane) * p.W * 4 + (size_t)cb0 * 128;
+          bulk_g2s(slot + SLOT_W + lane * XPITCH, to_global(a), nc * 128, &full[s]);
         }
       }
       ++gs;
     }
+    ++item_seq;
     if (!ok || it.kind == 0) break;
   }
-  if (!ok) {
+  if (!ok && lane == 0) {
     // Drain: every copy this CTA issued must land before the CTA exits.
     const int first = gs > NS ? gs - NS : 0;
     for (int g = first; g < gs; ++g) {
@@ -539,146 +614,112 @@ __device__ void producer(const Params& p, const Tables& tb, uint8_t* smem, uint6
   }
 }
 
-__device__ __forceinline__ void decode16(const uint4 c, uint32_t (&h)[16]) {
-  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-#pragma unroll
-    for (int b = 0; b < 4; ++b) h[4 * q + b] = e2m1x2_to_f16x2((w[q] >> (8 * b)) & 0xffu);
-  }
+// Four code bytes (rows g, g+8 x k-pairs (2t, 2t+8)) and their two block
+// scales -> the A fragment of one m16n8k16 step, scale folded in (exact).
+__device__ __forceinline__ void afrag(uint32_t word, uint32_t scales2, uint32_t (&a)[4]) {
+  const uint32_t s = e4m3x2_to_f16x2(scales2);
+  const __half2 sh = *reinterpret_cast<const __half2*>(&s);
+  const __half2 slo = __low2half2(sh), shi = __high2half2(sh);
+  uint32_t c0 = e2m1x2_to_f16x2(word & 0xffu);
+  uint32_t c1 = e2m1x2_to_f16x2((word >> 8) & 0xffu);
+  uint32_t c2 = e2m1x2_to_f16x2((word >> 16) & 0xffu);
+  uint32_t c3 = e2m1x2_to_f16x2(word >> 24);
+  __half2 h0 = __hmul2(*reinterpret_cast<__half2*>(&c0), slo);
+  __half2 h1 = __hmul2(*reinterpret_cast<__half2*>(&c1), shi);
+  __half2 h2 = __hmul2(*reinterpret_cast<__half2*>(&c2), slo);
+  __half2 h3 = __hmul2(*reinterpret_cast<__half2*>(&c3), shi);
+  a[0] = *reinterpret_cast<uint32_t*>(&h0);
+  a[1] = *reinterpret_cast<uint32_t*>(&h1);
+  a[2] = *reinterpret_cast<uint32_t*>(&h2);
+  a[3] = *reinterpret_cast<uint32_t*>(&h3);
 }
 
-__device__ __forceinline__ void scales2(uint32_t two, float& s0, float& s1) {
-  const uint32_t h = e4m3x2_to_f16x2(two);
-  s0 = f16lo_to_f32(h);
-  s1 = f16hi_to_f32(h);
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ void final_reduce(const Params& p, int kt, int lane) {
-  const int n = p.rows * TK;
-  for (int idx = lane; idx < n; idx += 32) {
-    const int row = idx / TK, c = idx - row * TK;
-    float s = 0.f;
-    for (int j = 0; j < p.topk; ++j) {
-      const int q = row * p.topk + j;
-      if (p.pexp[q] >= 0) s += __ldcg(p.y + (size_t)q * HID + kt * TK + c);
-    }
-    p.out[(size_t)row * p.out_stride + kt * TK + c] = __float2bfloat16_rn(s);
-  }
+// Activation column c of pair q -> byte offset of its (hi, lo) f16 pair in the
+// down projection's B-fragment order: per 32-column block 128 bytes, per k16
+// step 64 bytes, unit (t) 16 bytes = [hi w0, hi w1, lo w0, lo w1].
+__device__ __forceinline__ size_t act_off(const Params& p, int q, int c) {
+  const int cb = c >> 5, s = (c >> 4) & 1, kk = c & 15;
+  const int t = (kk & 7) >> 1, word = kk >> 3, half = kk & 1;
+  return (size_t)q * p.W * 4 + cb * 128 + s * 64 + t * 16 + word * 4 + half * 2;
 }
 
-__device__ void consumer(const Params& p, const uint8_t* smem, uint64_t* full, uint64_t* empty, const Meta* meta,
-                         uint64_t deadline) {
+__device__ void consumer(const Params& p, uint8_t* smem, uint64_t* full, uint64_t* empty, const ItemMeta* imeta,
+                         const int32_t* smeta, float4* redbuf, uint64_t* redbar, uint64_t deadline) {
   volatile uint32_t* status = &p.ctl->status;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = threadIdx.x;
-  float acc_a[PG], acc_b[PG];
-#pragma unroll
-  for (int i = 0; i < PG; ++i) acc_a[i] = acc_b[i] = 0.f;
+  const int g = lane >> 2, t = lane & 3;
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  float e[4] = {0.f, 0.f, 0.f, 0.f};  // second accumulator: independent MMA chain
+  uint32_t ph1_items = 0;
   for (int gs = 0;; ++gs) {
     const int s = gs % NS;
     if (!mbar_wait_bounded(&full[s], (gs / NS) & 1, status, QX_DEV_TIMEOUT, deadline)) return;
-    const Meta& ms = meta[s];
-    const int kind = ms.kind, stage = ms.stage, nstages = ms.nstages, np = ms.np, nc = ms.nc;
-    if (kind == 0) return;
+    const int sm = smeta[s];
+    if (sm < 0) return;
+    const ItemMeta& im = imeta[sm >> 16];
+    const int stage = sm & 0xffff;
+    const int kind = im.kind, nstages = im.nstages, np = im.np;
     const uint8_t* slot = smem + (size_t)s * SLOT;
     if (stage == 0) {
 #pragma unroll
-      for (int i = 0; i < PG; ++i) acc_a[i] = acc_b[i] = 0.f;
+      for (int i = 0; i < 4; ++i) d[i] = e[i] = 0.f;
     }
+    const bool have_b = g < np;
     if (kind == 1) {
-      // gate/up: lane half (lane>>4) picks the gate row, v = lane&15 the 32-element vector
-      const int v = lane & 15;
-      const int gr = 2 * warp + (lane >> 4);
-      const uint4 cg = *reinterpret_cast<const uint4*>(slot + gr * 256 + v * 16);
-      const uint4 cu = *reinterpret_cast<const uint4*>(slot + (gr + TC) * 256 + v * 16);
-      const uint32_t sgw = *reinterpret_cast<const uint16_t*>(slot + P1_CODE + gr * 32 + v * 2);
-      const uint32_t suw = *reinterpret_cast<const uint16_t*>(slot + P1_CODE + (gr + TC) * 32 + v * 2);
-      float sg0, sg1, su0, su1;
-      scales2(sgw, sg0, sg1);
-      scales2(suw, su0, su1);
-      uint32_t hg[16], hu[16];
-      decode16(cg, hg);
-      decode16(cu, hu);
-      const int sw = (v >> 1) & 3;
+      // gate/up: warp owns tile (warp & 3) = 8 gate + 8 up rows, K quarter (warp >> 2)
+      const int tile = warp & 3, kq = warp >> 2;
+      const uint8_t* xb = slot + SLOT_W + g * XPITCH;
 #pragma unroll
-      for (int i = 0; i < PG; ++i) {
-        if (i < np) {
-          const uint4* xq = reinterpret_cast<const uint4*>(slot + SLOT_W + i * 1024) + v * 4;
-          const uint4 x0 = xq[0 ^ sw], x1 = xq[1 ^ sw], x2 = xq[2 ^ sw], x3 = xq[3 ^ sw];
-          float g0 = 0.f, g1 = 0.f, u0 = 0.f, u1 = 0.f;
-          g0 = fma2_f16_f32(hg[0], x0.x, g0);  u0 = fma2_f16_f32(hu[0], x0.x, u0);
-          g0 = fma2_f16_f32(hg[1], x0.y, g0);  u0 = fma2_f16_f32(hu[1], x0.y, u0);
-          g0 = fma2_f16_f32(hg[2], x0.z, g0);  u0 = fma2_f16_f32(hu[2], x0.z, u0);
-          g0 = fma2_f16_f32(hg[3], x0.w, g0);  u0 = fma2_f16_f32(hu[3], x0.w, u0);
-          g0 = fma2_f16_f32(hg[4], x1.x, g0);  u0 = fma2_f16_f32(hu[4], x1.x, u0);
-          g0 = fma2_f16_f32(hg[5], x1.y, g0);  u0 = fma2_f16_f32(hu[5], x1.y, u0);
-          g0 = fma2_f16_f32(hg[6], x1.z, g0);  u0 = fma2_f16_f32(hu[6], x1.z, u0);
-          g0 = fma2_f16_f32(hg[7], x1.w, g0);  u0 = fma2_f16_f32(hu[7], x1.w, u0);
-          g1 = fma2_f16_f32(hg[8], x2.x, g1);  u1 = fma2_f16_f32(hu[8], x2.x, u1);
-          g1 = fma2_f16_f32(hg[9], x2.y, g1);  u1 = fma2_f16_f32(hu[9], x2.y, u1);
-          g1 = fma2_f16_f32(hg[10], x2.z, g1); u1 = fma2_f16_f32(hu[10], x2.z, u1);
-          g1 = fma2_f16_f32(hg[11], x2.w, g1); u1 = fma2_f16_f32(hu[11], x2.w, u1);
-          g1 = fma2_f16_f32(hg[12], x3.x, g1); u1 = fma2_f16_f32(hu[12], x3.x, u1);
-          g1 = fma2_f16_f32(hg[13], x3.y, g1); u1 = fma2_f16_f32(hu[13], x3.y, u1);
-          g1 = fma2_f16_f32(hg[14], x3.z, g1); u1 = fma2_f16_f32(hu[14], x3.z, u1);
-          g1 = fma2_f16_f32(hg[15], x3.w, g1); u1 = fma2_f16_f32(hu[15], x3.w, u1);
-          acc_a[i] = fmaf(g1, sg1, fmaf(g0, sg0, acc_a[i]));
-          acc_b[i] = fmaf(u1, su1, fmaf(u0, su0, acc_b[i]));
+      for (int h = 0; h < 2; ++h) {
+        const int sg = 2 * kq + h;
+        const uint4 cw = *reinterpret_cast<const uint4*>(slot + ((tile * 8 + sg) * 32 + lane) * 16);
+        const uint2 sw = *reinterpret_cast<const uint2*>(slot + P1_CODE + ((tile * 8 + sg) * 8 + g) * 8);
+        uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
+        if (have_b) {
+          x0 = *reinterpret_cast<const uint4*>(xb + (2 * sg) * 64 + t * 16);
+          x1 = *reinterpret_cast<const uint4*>(xb + (2 * sg + 1) * 64 + t * 16);
         }
+        uint32_t a[4], b[4];
+        afrag(cw.x, sw.x & 0xffffu, a);
+        afrag(cw.y, sw.x >> 16, b);
+        mma16816(d, a, x0.x, x0.y);
+        mma16816(e, b, x0.z, x0.w);
+        afrag(cw.z, sw.y & 0xffffu, a);
+        afrag(cw.w, sw.y >> 16, b);
+        mma16816(d, a, x1.x, x1.y);
+        mma16816(e, b, x1.z, x1.w);
       }
     } else {
-      // down: thread -> output row r = t/2, column blocks {2h, 2h+1} of the stage
-      const int r = t >> 1, h = t & 1;
+      // down: warp owns 16 output rows (tile = warp); B = activation hi and lo
+      const int tile = warp;
+      const int nc = stage == nstages - 1 ? im.nc_last : CB_PER_STAGE;
+      const uint8_t* ab = slot + SLOT_W + g * XPITCH;
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const int j = 2 * h + jj;
+      for (int j = 0; j < CB_PER_STAGE; ++j) {
         if (j < nc) {
-          const uint4 c = *reinterpret_cast<const uint4*>(slot + j * P2_CB_CODE + r * 16);
-          const uint32_t sw2 =
-              *reinterpret_cast<const uint16_t*>(slot + CB_PER_STAGE * P2_CB_CODE + j * P2_CB_SC + r * 2);
-          float s0, s1;
-          scales2(sw2, s0, s1);
-          uint32_t hw[16];
-          decode16(c, hw);
-          float wf[32];
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            wf[2 * k] = f16lo_to_f32(hw[k]);
-            wf[2 * k + 1] = f16hi_to_f32(hw[k]);
+          const uint2 cw = *reinterpret_cast<const uint2*>(slot + j * P2_CB_CODE + (tile * 32 + lane) * 8);
+          const uint32_t sw =
+              *reinterpret_cast<const uint32_t*>(slot + CB_PER_STAGE * P2_CB_CODE + j * P2_CB_SC + (tile * 8 + g) * 4);
+          uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
+          if (have_b) {
+            v0 = *reinterpret_cast<const uint4*>(ab + (j * 2) * 64 + t * 16);
+            v1 = *reinterpret_cast<const uint4*>(ab + (j * 2 + 1) * 64 + t * 16);
           }
-#pragma unroll
-          for (int i = 0; i < PG; ++i) {
-            if (i < np) {
-              const float4* a = reinterpret_cast<const float4*>(slot + SLOT_W + i * 512 + j * 128);
-              float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-#pragma unroll
-              for (int k = 0; k < 2; ++k) {
-                const float4 a0 = a[2 * k], a1 = a[2 * k + 1];
-                b0 = fmaf(wf[8 * k + 0], a0.x, b0);
-                b1 = fmaf(wf[8 * k + 1], a0.y, b1);
-                b0 = fmaf(wf[8 * k + 2], a0.z, b0);
-                b1 = fmaf(wf[8 * k + 3], a0.w, b1);
-                b0 = fmaf(wf[8 * k + 4], a1.x, b0);
-                b1 = fmaf(wf[8 * k + 5], a1.y, b1);
-                b0 = fmaf(wf[8 * k + 6], a1.z, b0);
-                b1 = fmaf(wf[8 * k + 7], a1.w, b1);
-              }
-#pragma unroll
-              for (int k = 2; k < 4; ++k) {
-                const float4 a0 = a[2 * k], a1 = a[2 * k + 1];
-                b2 = fmaf(wf[8 * k + 0], a0.x, b2);
-                b3 = fmaf(wf[8 * k + 1], a0.y, b3);
-                b2 = fmaf(wf[8 * k + 2], a0.z, b2);
-                b3 = fmaf(wf[8 * k + 3], a0.w, b3);
-                b2 = fmaf(wf[8 * k + 4], a1.x, b2);
-                b3 = fmaf(wf[8 * k + 5], a1.y, b3);
-                b2 = fmaf(wf[8 * k + 6], a1.z, b2);
-                b3 = fmaf(wf[8 * k + 7], a1.w, b3);
-              }
-              acc_a[i] = fmaf(b2 + b3, s1, fmaf(b0 + b1, s0, acc_a[i]));
-            }
-          }
+          uint32_t a[4], b[4];
+          afrag(cw.x, sw & 0xffffu, a);
+          afrag(cw.y, sw >> 16, b);
+          mma16816(d, a, v0.x, v0.y);
+          mma16816(e, b, v1.x, v1.y);
+          mma16816(d, a, v0.z, v0.w);
+          mma16816(e, b, v1.z, v1.w);
         }
       }
     }
@@ -687,97 +728,106 @@ __device__ void consumer(const Params& p, const uint8_t* smem, uint64_t* full, u
       if (lane == 0) mbar_arrive(&empty[s]);
       continue;
     }
-    // ---- item epilogue: pairs and factors come from the slot's meta ----
-    int pq[PG];
-    float fac[PG];
+    // ---- item epilogue: pairs and factors come from the item's metadata ----
+    int pq[2];
+    float fac[2];
 #pragma unroll
-    for (int i = 0; i < PG; ++i) {
-      pq[i] = ms.pair[i];
-      fac[i] = ms.fac[i];
+    for (int i = 0; i < 2; ++i) {
+      pq[i] = im.pair[2 * t + i];
+      fac[i] = im.fac[2 * t + i];
     }
-    const int blk = ms.blk, group = ms.group;
+    const int blk = im.blk, group = im.group;
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    if (lane == 0) mbar_arrive(&empty[s]);  // the slot and the item metadata are released here
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] += e[i];
     if (kind == 1) {
-      const int v = lane & 15;
-      const int gr = 2 * warp + (lane >> 4);
+      const int tile = warp & 3, kq = warp >> 2;
+      const uint32_t bsel = ph1_items & 1u;
+      const uint32_t par = (ph1_items >> 1) & 1u;
+      ++ph1_items;
+      float4* rb = redbuf + ((bsel * 4 + tile) * 3) * 32;
+      uint64_t* bar = &redbar[bsel * 4 + tile];
+      if (kq != 0) {
+        rb[(kq - 1) * 32 + lane] = make_float4(d[0], d[1], d[2], d[3]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar);
+        continue;
+      }
+      if (!mbar_wait_bounded(bar, par, status, QX_DEV_TIMEOUT, deadline)) return;
 #pragma unroll
-      for (int i = 0; i < PG; ++i) {
-        if (i < np) {
-          float g = acc_a[i], u = acc_b[i];
+      for (int k = 0; k < 3; ++k) {
+        const float4 v = rb[k * 32 + lane];
+        d[0] += v.x;
+        d[1] += v.y;
+        d[2] += v.z;
+        d[3] += v.w;
+      }
+      const int col = blk * TC + tile * 8 + g;
 #pragma unroll
-          for (int o = 8; o > 0; o >>= 1) {
-            g += __shfl_xor_sync(0xffffffffu, g, o);
-            u += __shfl_xor_sync(0xffffffffu, u, o);
+      for (int i = 0; i < 2; ++i) {
+        if (2 * t + i < np) {
+          float gg = d[i] * fac[i], uu = d[2 + i] * fac[i];
+          if (p.has_limit) {
+            gg = fminf(gg, p.limit);
+            uu = fminf(fmaxf(uu, -p.limit), p.limit);
           }
-          if (v == 0) {
-            float gg = g * fac[i], uu = u * fac[i];
-            if (p.has_limit) {
-              gg = fminf(gg, p.limit);
-              uu = fminf(fmaxf(uu, -p.limit), p.limit);
-            }
-            p.act[(size_t)pq[i] * p.W + blk * TC + gr] = (gg / (1.f + expf(-gg))) * uu;
-          }
+          const float a = (gg / (1.f + expf(-gg))) * uu;
+          const float as = a * p.act_scale;
+          if (!(fabsf(as) < 65504.f)) atomicOr(&p.ctl->status, (uint32_t)QX_DEV_OVERFLOW);
+          const __half hi = __float2half_rn(as);
+          const __half lo = __float2half_rn(as - __half2float(hi));
+          uint8_t* dst = p.act + act_off(p, pq[i], col);
+          *reinterpret_cast<__half*>(dst) = hi;
+          *reinterpret_cast<__half*>(dst + 8) = lo;
         }
       }
       __threadfence();
       __syncwarp();
       if (lane == 0) atomicAdd(&p.cnt1[group], 1u);
     } else {
-      const int r = t >> 1, h = t & 1;
+      const int kt = blk / p.n_sub, sub = blk % p.n_sub;
+      const int row0 = kt * TK + warp * 16 + g;
 #pragma unroll
-      for (int i = 0; i < PG; ++i) {
-        if (i < np) {
-          const float a = acc_a[i] + __shfl_xor_sync(0xffffffffu, acc_a[i], 1);
-          if (h == 0) p.y[(size_t)pq[i] * HID + blk * TK + r] = a * fac[i];
+      for (int i = 0; i < 2; ++i) {
+        if (2 * t + i < np) {
+          float* yq = p.y + ((size_t)pq[i] * p.n_sub + sub) * HID;
+          const float f = fac[i] * p.act_unscale;
+          yq[row0] = d[i] * f;
+          yq[row0 + 8] = d[2 + i] * f;
         }
-      }
-      __threadfence();
-      __syncwarp();
-      uint32_t last = 0;
-      if (lane == 0) {
-        const uint32_t old = atomicAdd(&p.ctl->cnt2[blk], 1u);
-        last = (old == p.ctl->n_groups * NCW - 1u) ? 1u : 0u;
-      }
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {
-        __threadfence();
-        final_reduce(p, blk, lane);
       }
     }
   }
 }
 
 constexpr size_t SMEM_RING = (size_t)NS * SLOT;
-constexpr size_t SMEM_BARS = 2 * NS * sizeof(uint64_t);
-constexpr size_t SMEM_META = NS * sizeof(Meta);
-constexpr size_t SMEM_BYTES = SMEM_RING + SMEM_BARS + SMEM_META + sizeof(Tables);
+constexpr size_t SMEM_BARS = (2 * NS + 8) * sizeof(uint64_t);
+constexpr size_t SMEM_META = NI * sizeof(ItemMeta) + 16 * sizeof(int32_t);
+constexpr size_t SMEM_RED = 2 * 4 * 3 * 32 * sizeof(float4);
+constexpr size_t SMEM_BYTES = SMEM_RING + SMEM_BARS + SMEM_META + SMEM_RED + sizeof(Tables);
 
 __global__ void __launch_bounds__(NTHR, 1) qx_decode_kernel(Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + SMEM_RING);
   uint64_t* empty = full + NS;
-  Meta* meta = reinterpret_cast<Meta*>(smem + SMEM_RING + SMEM_BARS);
-  Tables& tb = *reinterpret_cast<Tables*>(smem + SMEM_RING + SMEM_BARS + SMEM_META);
+  uint64_t* redbar = empty + NS;
+  ItemMeta* imeta = reinterpret_cast<ItemMeta*>(smem + SMEM_RING + SMEM_BARS);
+  int32_t* smeta = reinterpret_cast<int32_t*>(imeta + NI);
+  float4* redbuf = reinterpret_cast<float4*>(smem + SMEM_RING + SMEM_BARS + SMEM_META);
+  Tables& tb = *reinterpret_cast<Tables*>(smem + SMEM_RING + SMEM_BARS + SMEM_META + SMEM_RED);
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NCW);
     }
+    for (int i = 0; i < 8; ++i) mbar_init(&redbar[i], 3);
     fence_mbar_init();
   }
-  pdl_wait();  // the prologue's routing tables and activations are complete
+  pdl_wait();                // the prologue's routing tables and activations are complete
+  pdl_launch_dependents();   // the finalize kernel may be scheduled; it waits for this grid
   const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
   const int U = (int)p.ctl->n_unique;
-  if (p.ctl->n_groups == 0) {  // every slot was padding: the partial is zero
-    if (blockIdx.x == 0) {
-      for (int i = threadIdx.x; i < p.rows * HID; i += blockDim.x) {
-        const int row = i / HID, c = i - row * HID;
-        p.out[(size_t)row * p.out_stride + c] = __float2bfloat16_rn(0.f);
-      }
-    }
-    return;
-  }
   {
     const int4* src = reinterpret_cast<const int4*>(p.uniq);
     int4* dst = reinterpret_cast<int4*>(tb.uniq);
@@ -792,10 +842,46 @@ __global__ void __launch_bounds__(NTHR, 1) qx_decode_kernel(Params p) {
   __syncthreads();
   const int warp = threadIdx.x >> 5;
   if (warp == NCW) {
-    if ((threadIdx.x & 31) == 0) producer(p, tb, smem, full, empty, meta, deadline);
+    producer(p, tb, smem, full, empty, imeta, smeta, deadline);
     return;
   }
-  consumer(p, smem, full, empty, meta, deadline);
+  consumer(p, smem, full, empty, imeta, smeta, redbuf, redbar, deadline);
+}
+
+// out[row, k] = bf16(sum over slots j, then sub-ranges, of y[row*topk + j][sub][k]),
+// four outputs per thread, all loads issued before the ordered sum.
+__global__ void __launch_bounds__(256) qx_finalize_kernel(Params p) {
+  pdl_wait();
+  const int n4 = p.rows * (HID / 4);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+    const int row = i / (HID / 4), k = (i - row * (HID / 4)) * 4;
+    float4 v[QX_MAX_TOPK * 2];
+#pragma unroll
+    for (int j = 0; j < QX_MAX_TOPK; ++j) {
+#pragma unroll
+      for (int sub = 0; sub < 2; ++sub) {
+        float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < p.topk && sub < p.n_sub) {
+          const int q = row * p.topk + j;
+          if (p.pexp[q] >= 0) z = __ldcg(reinterpret_cast<const float4*>(p.y + ((size_t)q * p.n_sub + sub) * HID + k));
+        }
+        v[j * 2 + sub] = z;
+      }
+    }
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < QX_MAX_TOPK * 2; ++j) {
+      s.x += v[j].x;
+      s.y += v[j].y;
+      s.z += v[j].z;
+      s.w += v[j].w;
+    }
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&lo);
+    o.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(p.out + (size_t)row * p.out_stride + k) = o;
+  }
 }
 
 // ------------------------------------------------------------------ combine
@@ -883,6 +969,17 @@ static uint32_t dep_extra() {
   return e ? (uint32_t)atol(e) : 0u;
 }
 
+// Power of two applied to the stored activation so that the clamped SwiGLU
+// output (|act| <= L^2) sits below 2^14 in f16; 1 without a clamp.
+static float act_scale_for(float limit, int has_limit) {
+  if (!has_limit || !(limit > 0.f)) return 1.f;
+  const float bound = limit * limit;
+  int e = 0;
+  while (e < 24 && bound * ldexpf(1.f, e + 1) < 16384.f) ++e;
+  while (e > -24 && bound * ldexpf(1.f, e) >= 16384.f) --e;
+  return ldexpf(1.f, e);
+}
+
 }  // namespace qx
 
 using namespace qx;
@@ -900,7 +997,7 @@ size_t qx_arena_w2_bytes(int32_t n_experts, int32_t width) {
 }
 
 size_t qx_slice_workspace_bytes(int32_t rows, int32_t topk, int32_t c0, int32_t c1) {
-  if (rows <= 0 || rows > QX_MAX_ROWS || topk <= 0 || topk > QX_MAX_TOPK || c1 <= c0) return 0;
+  if (rows <= 0 || rows > QX_MAX_ROWS || topk <= 0 || topk > QX_MAX_TOPK || c1 <= c0 || (c1 - c0) % TC) return 0;
   return ws_layout(rows, topk, c1 - c0).total;
 }
 
@@ -943,6 +1040,7 @@ int qx_slice_decode(const QxArena* arena, const QxSliceArgs* a, void* stream) {
   p.n_cb = W / TC;
   p.n_cb_arena = (arena->a1 - arena->a0) / TC;
   p.W = W;
+  p.n_sub = n_sub_of(p.n_cb);
   p.w13 = arena->w13;
   p.w2 = arena->w2;
   p.g13 = arena->g13;
@@ -950,6 +1048,8 @@ int qx_slice_decode(const QxArena* arena, const QxSliceArgs* a, void* stream) {
   p.E = arena->n_experts;
   p.limit = a->swiglu_limit;
   p.has_limit = a->has_limit ? 1 : 0;
+  p.act_scale = act_scale_for(a->swiglu_limit, p.has_limit);
+  p.act_unscale = 1.f / p.act_scale;
   p.out = reinterpret_cast<__nv_bfloat16*>(a->out);
   p.out_stride = a->out_stride;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
@@ -959,8 +1059,8 @@ int qx_slice_decode(const QxArena* arena, const QxSliceArgs* a, void* stream) {
   p.pairlist = reinterpret_cast<int32_t*>(ws + L.pairlist);
   p.pexp = reinterpret_cast<int32_t*>(ws + L.pexp);
   p.xscale = reinterpret_cast<float*>(ws + L.xscale);
-  p.x16 = reinterpret_cast<__half*>(ws + L.x16);
-  p.act = reinterpret_cast<float*>(ws + L.act);
+  p.x16 = ws + L.x16;
+  p.act = ws + L.act;
   p.y = reinterpret_cast<float*>(ws + L.y);
   p.timeout_ns = timeout_ns();
   p.dep_extra = dep_extra();
@@ -980,6 +1080,16 @@ int qx_slice_decode(const QxArena* arena, const QxSliceArgs* a, void* stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, qx_decode_kernel, p) != cudaSuccess) return QX_ERR_LAUNCH;
+
+  cudaLaunchConfig_t cfg2 = {};
+  const int n4 = a->rows * (HID / 4);
+  cfg2.gridDim = dim3((n4 + 255) / 256, 1, 1);
+  cfg2.blockDim = dim3(256, 1, 1);
+  cfg2.dynamicSmemBytes = 0;
+  cfg2.stream = st;
+  cfg2.attrs = attr;
+  cfg2.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg2, qx_finalize_kernel, p) != cudaSuccess) return QX_ERR_LAUNCH;
   return QX_OK;
 }
 
@@ -1020,6 +1130,6 @@ int qx_status_read(const void* workspace, uint32_t* status, void* stream) {
   return QX_OK;
 }
 
-const char* qx_version(void) { return "qmesh_b200 0.1 sm_100a"; }
+const char* qx_version(void) { return "qmesh_b200 0.3 sm_100a"; }
 
 }  // extern "C"

@@ -13,15 +13,17 @@ C = the slice's width, H = 5120.
 
 Arena layout (this build; what the kernels stream), for arena columns [a0, a1),
 n_cb = (a1 - a0) / 32 column blocks:
-    w13 tiles [E][n_cb][10 K-chunks][18432 B]; one chunk = codes of 64 rows x 512
-        elements (32 gate rows then the 32 matching up rows, 256 B each) followed
-        by their scales (64 rows x 32 B). One (expert, column block) is one
-        contiguous 184,320-byte run, so any 32-aligned column range streams as
-        whole bulk copies.
-    w2 tiles  [E][20 row tiles][n_cb x 4096 B codes | n_cb x 512 B scales]; the
-        codes of row tile kt, column block cb are 256 rows x 16 B (32 elements),
-        the scales 256 rows x 2 B. A column range is one contiguous run of codes
-        and one of scales per (expert, row tile).
+    w13 tiles [E][n_cb][10 K-chunks][18432 B]; one chunk holds the codes and
+        block scales of 64 rows (32 gate columns and their 32 up columns) x 512
+        elements, ordered so that each thread's tensor-core A fragment is one
+        4-byte word (see pack_w13). One (expert, column block) is one contiguous
+        184,320-byte run, so any 32-aligned column range streams as whole bulk
+        copies.
+    w2 tiles  [E][20 row tiles][n_cb x 4096 B codes | n_cb x 512 B scales]; per
+        256-row output tile and 32-column block, the same fragment order
+        (see pack_w2). A column range is one contiguous run of codes and one of
+        scales per (expert, row tile).
+Both layouts hold exactly the pack's bytes, only permuted.
 """
 
 from __future__ import annotations
@@ -72,66 +74,78 @@ def global_scale(w: torch.Tensor) -> torch.Tensor:
 
 def pack_w13(c13: torch.Tensor, s13: torch.Tensor, src_a0: int, a0: int, a1: int) -> torch.Tensor:
     """Pack-format w13 (codes [E, 2C, H/2], scales [E, 2C, H/16] of source columns
-    [src_a0, src_a0 + C)) -> arena w13 tiles for columns [a0, a1), flat uint8."""
+    [src_a0, src_a0 + C)) -> arena w13 tiles for columns [a0, a1), flat uint8.
+
+    Per (expert, 32-column block, 512-element K chunk) one 18,432-byte stage:
+      codes  [tile 4][step group 8][lane 32][step 4][4 B]  (16,384 B)
+      scales [tile 4][step group 8][g 8][step 4][2 B]      (2,048 B)
+    A tile is 8 gate rows then their 8 up rows (columns tile*8 + g). The 4 code
+    bytes of (lane = 4g + t, k16 step) are the m16n8k16 A fragment:
+    (gate g, k 2t..2t+1), (up g, k 2t..), (gate g, k 2t+8..), (up g, k 2t+8..);
+    the 2 scale bytes are (gate g, up g) of that step's 16-element block.
+    """
     e, two_c, _ = c13.shape
     c = two_c // 2
     lo, hi = a0 - src_a0, a1 - src_a0
     if lo < 0 or hi > c or (hi - lo) % TC:
         raise ValueError(f"columns [{a0}, {a1}) not inside the source slice or not 32-aligned")
     n_cb = (hi - lo) // TC
-
-    def rows(t):
-        g = t[:, lo:hi]
-        u = t[:, c + lo:c + hi]
-        return g, u
-
-    cg, cu = rows(c13)
-    sg, su = rows(s13)
-    # [E, n_cb, 32, NKC, 256] -> gate/up concatenated -> [E, n_cb, NKC, 64, 256]
-    cg = cg.reshape(e, n_cb, TC, NKC, KC // 2)
-    cu = cu.reshape(e, n_cb, TC, NKC, KC // 2)
-    codes = torch.cat([cg, cu], dim=2).permute(0, 1, 3, 2, 4).reshape(e, n_cb, NKC, 2 * TC * KC // 2)
-    sg = sg.reshape(e, n_cb, TC, NKC, KC // 16)
-    su = su.reshape(e, n_cb, TC, NKC, KC // 16)
-    scales = torch.cat([sg, su], dim=2).permute(0, 1, 3, 2, 4).reshape(e, n_cb, NKC, 2 * TC * KC // 16)
+    # codes: [E, cb, tile, g, kc, sg, j, h, t] per gate/up, then bytes (h, hh)
+    gc = c13[:, lo:hi].reshape(e, n_cb, 4, 8, NKC, 8, 4, 2, 4)
+    uc = c13[:, c + lo:c + hi].reshape(e, n_cb, 4, 8, NKC, 8, 4, 2, 4)
+    x = torch.stack([gc, uc], dim=-1)                       # [.., h, t, hh]
+    codes = x.permute(0, 1, 4, 2, 5, 3, 8, 6, 7, 9).reshape(e, n_cb, NKC, 16384)
+    gs = s13[:, lo:hi].reshape(e, n_cb, 4, 8, NKC, 8, 4)
+    us = s13[:, c + lo:c + hi].reshape(e, n_cb, 4, 8, NKC, 8, 4)
+    y = torch.stack([gs, us], dim=-1)                       # [E, cb, tile, g, kc, sg, j, hh]
+    scales = y.permute(0, 1, 4, 2, 5, 3, 6, 7).reshape(e, n_cb, NKC, 2048)
     return torch.cat([codes, scales], dim=-1).contiguous().view(-1)
 
 
 def pack_w2(c2: torch.Tensor, s2: torch.Tensor, src_a0: int, a0: int, a1: int) -> torch.Tensor:
-    """Pack-format w2 (codes [E, H, C/2], scales [E, H, C/16]) -> arena w2 tiles."""
+    """Pack-format w2 (codes [E, H, C/2], scales [E, H, C/16]) -> arena w2 tiles.
+
+    Per (expert, 256-row output tile kt): codes [cb][tile 16][lane 32][step 2][4 B]
+    for every 32-column block, then scales [cb][tile 16][g 8][step 2][2 B]. Tile
+    rows are kt*256 + tile*16 + (g | g+8); fragment bytes as in pack_w13 with
+    rows g and g+8 in place of gate and up.
+    """
     e, h, c_half = c2.shape
     lo, hi = a0 - src_a0, a1 - src_a0
     if lo < 0 or hi > 2 * c_half or (hi - lo) % TC:
         raise ValueError(f"columns [{a0}, {a1}) not inside the source slice or not 32-aligned")
     n_cb = (hi - lo) // TC
-    cc = c2[:, :, lo // 2:hi // 2].reshape(e, NKT, TK, n_cb, 16).permute(0, 1, 3, 2, 4)
-    ss = s2[:, :, lo // 16:hi // 16].reshape(e, NKT, TK, n_cb, 2).permute(0, 1, 3, 2, 4)
-    cc = cc.reshape(e, NKT, n_cb * TK * 16)
-    ss = ss.reshape(e, NKT, n_cb * TK * 2)
+    cc = c2[:, :, lo // 2:hi // 2].reshape(e, NKT, 16, 2, 8, n_cb, 2, 2, 4)   # [E, kt, tile, hh, g, cb, s, h, t]
+    cc = cc.permute(0, 1, 5, 2, 4, 8, 6, 7, 3).reshape(e, NKT, n_cb * 4096)
+    ss = s2[:, :, lo // 16:hi // 16].reshape(e, NKT, 16, 2, 8, n_cb, 2)      # [E, kt, tile, hh, g, cb, s]
+    ss = ss.permute(0, 1, 5, 2, 4, 6, 3).reshape(e, NKT, n_cb * 512)
     return torch.cat([cc, ss], dim=-1).contiguous().view(-1)
 
 
 def unpack_w13(tiles: torch.Tensor, n_experts: int, width: int) -> tuple[torch.Tensor, torch.Tensor]:
     """Inverse of pack_w13 (arena -> pack-format codes/scales of the arena's columns)."""
-    n_cb = width // TC
-    t = tiles.view(n_experts, n_cb, NKC, P1_STAGE)
-    codes = t[..., :2 * TC * KC // 2].reshape(n_experts, n_cb, NKC, 2 * TC, KC // 2).permute(0, 1, 3, 2, 4)
-    scales = t[..., 2 * TC * KC // 2:].reshape(n_experts, n_cb, NKC, 2 * TC, KC // 16).permute(0, 1, 3, 2, 4)
-    codes = codes.reshape(n_experts, n_cb, 2, TC, HIDDEN // 2)
-    scales = scales.reshape(n_experts, n_cb, 2, TC, HIDDEN // 16)
-    c13 = torch.cat([codes[:, :, 0].reshape(n_experts, width, -1), codes[:, :, 1].reshape(n_experts, width, -1)], 1)
-    s13 = torch.cat([scales[:, :, 0].reshape(n_experts, width, -1), scales[:, :, 1].reshape(n_experts, width, -1)], 1)
-    return c13.contiguous(), s13.contiguous()
+    e, n_cb = n_experts, width // TC
+    t = tiles.view(e, n_cb, NKC, P1_STAGE)
+    x = t[..., :16384].reshape(e, n_cb, NKC, 4, 8, 8, 4, 4, 2, 2)   # [E, cb, kc, tile, sg, g, t, j, h, hh]
+    x = x.permute(0, 1, 3, 5, 2, 4, 7, 8, 6, 9)                      # [E, cb, tile, g, kc, sg, j, h, t, hh]
+    gate = x[..., 0].reshape(e, width, HIDDEN // 2)
+    up = x[..., 1].reshape(e, width, HIDDEN // 2)
+    y = t[..., 16384:].reshape(e, n_cb, NKC, 4, 8, 8, 4, 2)          # [E, cb, kc, tile, sg, g, j, hh]
+    y = y.permute(0, 1, 3, 5, 2, 4, 6, 7)                            # [E, cb, tile, g, kc, sg, j, hh]
+    gs = y[..., 0].reshape(e, width, HIDDEN // 16)
+    us = y[..., 1].reshape(e, width, HIDDEN // 16)
+    return torch.cat([gate, up], 1).contiguous(), torch.cat([gs, us], 1).contiguous()
 
 
 def unpack_w2(tiles: torch.Tensor, n_experts: int, width: int) -> tuple[torch.Tensor, torch.Tensor]:
     """Inverse of pack_w2."""
-    n_cb = width // TC
-    t = tiles.view(n_experts, NKT, n_cb * P2_CB)
-    cc = t[..., :n_cb * TK * 16].reshape(n_experts, NKT, n_cb, TK, 16).permute(0, 1, 3, 2, 4)
-    ss = t[..., n_cb * TK * 16:].reshape(n_experts, NKT, n_cb, TK, 2).permute(0, 1, 3, 2, 4)
-    return (cc.reshape(n_experts, HIDDEN, width // 2).contiguous(),
-            ss.reshape(n_experts, HIDDEN, width // 16).contiguous())
+    e, n_cb = n_experts, width // TC
+    t = tiles.view(e, NKT, n_cb * P2_CB)
+    cc = t[..., :n_cb * 4096].reshape(e, NKT, n_cb, 16, 8, 4, 2, 2, 2)  # [E, kt, cb, tile, g, t, s, h, hh]
+    cc = cc.permute(0, 1, 3, 8, 4, 2, 6, 7, 5)                          # [E, kt, tile, hh, g, cb, s, h, t]
+    ss = t[..., n_cb * 4096:].reshape(e, NKT, n_cb, 16, 8, 2, 2)        # [E, kt, cb, tile, g, s, hh]
+    ss = ss.permute(0, 1, 3, 6, 4, 2, 5)                                # [E, kt, tile, hh, g, cb, s]
+    return (cc.reshape(e, HIDDEN, width // 2).contiguous(), ss.reshape(e, HIDDEN, width // 16).contiguous())
 
 
 def swizzle_offset(row: torch.Tensor, kb: torch.Tensor, kbp: int) -> torch.Tensor:

@@ -28,19 +28,28 @@ def bf16_ulp(v: torch.Tensor) -> torch.Tensor:
     return torch.pow(2.0, torch.floor(torch.log2(a)) - 7.0)
 
 
-def element_ulp(ref: torch.Tensor) -> torch.Tensor:
+def element_ulp(ref: torch.Tensor, mag: torch.Tensor | None = None) -> torch.Tensor:
+    """BF16 ulp per element at max(|ref|, mag, 2^-10 * rms(row)).
+
+    `mag` is for outputs that are sums of BF16-rounded terms (the combine of
+    per-rank partials): their ulp is taken at the largest term, because one
+    ulp of a partial is the protocol's own resolution there.
+    """
     r2 = ref.reshape(-1, ref.shape[-1]) if ref.dim() > 1 else ref.reshape(1, -1)
     rms = r2.pow(2).mean(dim=-1, keepdim=True).sqrt()
     floor = (ULP_FLOOR * rms).expand_as(r2)
-    return bf16_ulp(torch.maximum(r2.abs(), floor)).reshape(ref.shape)
+    m = torch.maximum(r2.abs(), floor)
+    if mag is not None:
+        m = torch.maximum(m, mag.float().cpu().abs().reshape(m.shape))
+    return bf16_ulp(m).reshape(ref.shape)
 
 
-def parity(out: torch.Tensor, ref: torch.Tensor) -> dict:
+def parity(out: torch.Tensor, ref: torch.Tensor, mag: torch.Tensor | None = None) -> dict:
     out = out.float().cpu()
     ref = ref.float().cpu()
     err = (out - ref).abs()
     rel = (err.norm() / ref.norm().clamp_min(1e-30)).item()
-    u = err / element_ulp(ref)
+    u = err / element_ulp(ref, mag)
     i = int(u.argmax())
     idx = [int(v) for v in torch.unravel_index(torch.tensor(i), ref.shape)]
     return {"rel_l2": rel, "max_ulp": u.max().item(), "max_abs": err.max().item(),
@@ -48,8 +57,8 @@ def parity(out: torch.Tensor, ref: torch.Tensor) -> dict:
                                                                 "ref": ref.flatten()[i].item()}}
 
 
-def assert_parity(out, ref, what=""):
-    p = parity(out, ref)
+def assert_parity(out, ref, what="", mag=None):
+    p = parity(out, ref, mag)
     assert p["rel_l2"] <= REL_L2 and p["max_ulp"] <= MAX_ULP, f"{what} {p}"
     return p
 

@@ -52,19 +52,41 @@ def test_pack_unpack_round_trip(a0, a1):
     assert torch.equal(q4.pack_w13(src13, srcs13, a0, a0, a1), t13)
 
 
-def test_tile_bytes_contain_expected_codes():
-    """Spot-check the byte map the kernel relies on: gate row n, element k."""
+def test_tile_bytes_match_kernel_fragment_addressing():
+    """Spot-check the byte addresses the decode kernel reads (qx_decode.cu consumer):
+    gate/up codes at ((tile*8 + sg)*32 + lane)*16 + j*4 + b, scales at
+    16384 + ((tile*8 + sg)*8 + g)*8 + j*2 + hh; down codes at
+    cb*4096 + (tile*32 + lane)*8 + s*4 + b, scales at n_cb*4096 + cb*512 + (tile*8 + g)*4 + s*2 + hh."""
     from qmesh_b200 import nvfp4 as q4
+    g0 = torch.Generator().manual_seed(4)
     e, inter = 1, 64
-    c13 = torch.randint(0, 256, (e, 2 * inter, 2560), dtype=torch.uint8)
-    s13 = torch.randint(0, 256, (e, 2 * inter, 320), dtype=torch.uint8)
-    t = q4.pack_w13(c13, s13, 0, 0, 64)
-    for cb, kc, row, byte in [(0, 0, 0, 0), (1, 3, 17, 100), (1, 9, 63, 255), (0, 5, 40, 7)]:
-        off = (cb * 10 + kc) * 18432 + row * 256 + byte
-        src_row = cb * 32 + row if row < 32 else inter + cb * 32 + row - 32
-        assert t[off] == c13[0, src_row, kc * 256 + byte]
-        soff = (cb * 10 + kc) * 18432 + 16384 + row * 32 + byte % 32
-        assert t[soff] == s13[0, src_row, kc * 32 + byte % 32]
+    c13 = torch.randint(0, 256, (e, 2 * inter, 2560), generator=g0, dtype=torch.uint8)
+    s13 = torch.randint(0, 256, (e, 2 * inter, 320), generator=g0, dtype=torch.uint8)
+    t13 = q4.pack_w13(c13, s13, 0, 0, 64)
+    for cb, kc, tile, sg, lane, j, b in [(0, 0, 0, 0, 0, 0, 0), (1, 3, 2, 5, 17, 3, 1), (1, 9, 3, 7, 31, 2, 3),
+                                         (0, 5, 1, 4, 6, 1, 2)]:
+        g, t = lane // 4, lane % 4
+        h, hh = b // 2, b % 2
+        row = cb * 32 + tile * 8 + g + (inter if hh else 0)
+        step = kc * 32 + sg * 4 + j
+        off = (cb * 10 + kc) * 18432 + ((tile * 8 + sg) * 32 + lane) * 16 + j * 4 + b
+        assert t13[off] == c13[0, row, step * 8 + h * 4 + t]
+        soff = (cb * 10 + kc) * 18432 + 16384 + ((tile * 8 + sg) * 8 + g) * 8 + j * 2 + hh
+        assert t13[soff] == s13[0, row, step]
+    w = 96
+    n_cb = w // 32
+    c2 = torch.randint(0, 256, (e, 5120, w // 2), generator=g0, dtype=torch.uint8)
+    s2 = torch.randint(0, 256, (e, 5120, w // 16), generator=g0, dtype=torch.uint8)
+    t2 = q4.pack_w2(c2, s2, 0, 0, w)
+    for kt, cb, tile, lane, s_, b in [(0, 0, 0, 0, 0, 0), (7, 2, 15, 29, 1, 3), (19, 1, 4, 10, 0, 2)]:
+        g, t = lane // 4, lane % 4
+        h, hh = b // 2, b % 2
+        row = kt * 256 + tile * 16 + hh * 8 + g
+        base = kt * n_cb * 4608
+        off = base + cb * 4096 + (tile * 32 + lane) * 8 + s_ * 4 + b
+        assert t2[off] == c2[0, row, cb * 16 + s_ * 8 + h * 4 + t]
+        soff = base + n_cb * 4096 + cb * 512 + (tile * 8 + g) * 4 + s_ * 2 + hh
+        assert t2[soff] == s2[0, row, cb * 2 + s_]
 
 
 def test_unswizzle_reference_arena_scales():
