@@ -38,6 +38,9 @@ INTER = 2304
 N_EXPERTS = 384
 TOPK = 6
 EXPERT_BYTES = 2 * INTER * (HIDDEN // 2 + HIDDEN // 16) + HIDDEN * (INTER // 2 + INTER // 16)  # 19,906,560
+# DRAM bytes (read + write) per unique expert per launch of qx_decode_kernel, from the ncu capture in
+# profiles/qx_decode_kernel_rows6.md (545.86 MB over 27 unique experts, full 2304 columns).
+DRAM_BYTES_PER_UNIQUE = 545.86e6 / 27
 METRIC = "MoE-layer decode µs (6 rows) & NVFP4 weight GB/s vs HBM peak, 1/2/4/8 GPU"
 
 
@@ -258,7 +261,9 @@ def run_ours(args) -> dict | None:
             "tokens_per_s": round(rows / (us_layer * 1e-6), 1),
             "weight_gbs": round(gbs, 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                         "frac": round(gbs / peak, 4), "peak_kind": peak_kind,
+                         "traffic": int(mean_u * DRAM_BYTES_PER_UNIQUE * width / INTER),
+                         "traffic_source": "ncu dram bytes per unique expert (small-arena capture) x mean unique experts",
                          "kernel_us": round(k_mean, 3), "alg_bytes_per_launch": int(alg_bytes)},
             "e2e": {"value": round(us_e2e, 3), "unit": "us/layer", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
