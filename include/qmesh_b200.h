@@ -101,6 +101,33 @@ size_t qx_slice_workspace_bytes(int32_t rows, int32_t topk, int32_t c0, int32_t 
  * capture-safe. */
 int qx_slice_decode(const QxArena* arena, const QxSliceArgs* args, void* stream);
 
+/* Limits of qx_slice_decode_static. */
+#define QX_STATIC_MAX_ROWS 8
+#define QX_STATIC_MAX_TOPK 8
+#define QX_STATIC_MAX_WIDTH 2304
+
+/* The slice of qx_slice_decode for callers that cannot allocate device memory.
+ * No counterpart in the reference: its worker always owns its scratch.
+ *
+ * Some callers can't call cudaMalloc: a serving process whose device memory is
+ * fully claimed by its own arena and pools at start-up (the reference's GX worker
+ * sizes its expert arena to the free memory and refuses to start otherwise), or
+ * a host runtime embedding this library through an FFI without a device
+ * allocator of its own. This entry point needs no workspace from the caller: its
+ * scratch is one static array in the library (about 3.2 MiB per GPU that loads
+ * the library, held until the process exits), large enough for
+ * QX_STATIC_MAX_ROWS rows, QX_STATIC_MAX_TOPK slots and QX_STATIC_MAX_WIDTH
+ * columns; larger calls return QX_ERR_SHAPE. args->workspace and
+ * args->workspace_bytes are ignored; inputs and outputs are the caller's, as in
+ * qx_slice_decode. It allocates nothing and calls no allocating routine.
+ *
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture. Every call
+ * on a device shares the one array, and the kernels reinitialise what must
+ * start at zero on each call: calls that overlap on the GPU (two streams, or
+ * two host threads) race on the array and must be serialised by the caller. */
+int qx_slice_decode_static(const QxArena* arena, const QxSliceArgs* args, void* stream);
+
 /* Fixed-order combine: out = bf16(fp32(parts[0]) + ... + fp32(parts[n-1])), in
  * that order, one rounding (out_f32: keep FP32). parts[i] are BF16 [rows, hidden]
  * rows of stride part_stride elements; they may live on peer GPUs (P2P-mapped

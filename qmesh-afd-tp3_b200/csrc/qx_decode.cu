@@ -1133,3 +1133,46 @@ int qx_status_read(const void* workspace, uint32_t* status, void* stream) {
 const char* qx_version(void) { return "qmesh_b200 0.3 sm_100a"; }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ no-allocation entry
+// Scratch for qx_slice_decode_static: a fixed array in the library's device
+// image, sized for the largest call it accepts (QX_STATIC_MAX_ROWS rows,
+// QX_STATIC_MAX_TOPK slots, QX_STATIC_MAX_WIDTH columns). Every GPU that loads
+// the library holds these bytes until the process exits.
+namespace qx {
+constexpr size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
+constexpr size_t static_ws_bytes(int rows, int topk, int W) {
+  // the same sum as ws_layout(); the entry point still checks the real layout
+  return al256(sizeof(Ctl)) + al256(MAXP * sizeof(uint32_t)) + al256((MAXP + 1) * sizeof(Uniq)) +
+         al256(MAXP * sizeof(int32_t)) + al256(MAXP * sizeof(int32_t)) + al256((size_t)rows * sizeof(float)) +
+         al256((size_t)rows * HID * 2) + al256((size_t)rows * topk * (size_t)W * 4) +
+         al256((size_t)rows * topk * (size_t)((W / TC + SUB_CB - 1) / SUB_CB) * HID * sizeof(float));
+}
+constexpr size_t kStaticWsBytes = static_ws_bytes(QX_STATIC_MAX_ROWS, QX_STATIC_MAX_TOPK, QX_STATIC_MAX_WIDTH);
+}  // namespace qx
+
+static __device__ __align__(256) uint8_t g_static_ws[qx::kStaticWsBytes];
+
+// Device address of g_static_ws per device, looked up on the first call made
+// with that device current. In host code the name g_static_ws is only a
+// host-side handle, so it is never passed to a kernel directly.
+static void* g_static_ws_addr[64] = {nullptr};
+
+extern "C" int qx_slice_decode_static(const QxArena* arena, const QxSliceArgs* args, void* stream) {
+  if (!arena || !args) return QX_ERR_ARG;
+  if (args->rows < 1 || args->rows > QX_STATIC_MAX_ROWS || args->topk < 1 || args->topk > QX_STATIC_MAX_TOPK ||
+      args->c1 - args->c0 > QX_STATIC_MAX_WIDTH || args->c1 <= args->c0 || (args->c1 - args->c0) % qx::TC)
+    return QX_ERR_SHAPE;
+  if (qx::ws_layout(args->rows, args->topk, args->c1 - args->c0).total > qx::kStaticWsBytes) return QX_ERR_SHAPE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QX_ERR_DEVICE;
+  if (g_static_ws_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_static_ws) != cudaSuccess || ptr == nullptr) return QX_ERR_DEVICE;
+    g_static_ws_addr[dev] = ptr;
+  }
+  QxSliceArgs a = *args;
+  a.workspace = g_static_ws_addr[dev];
+  a.workspace_bytes = qx::kStaticWsBytes;
+  return qx_slice_decode(arena, &a, stream);
+}

@@ -41,6 +41,9 @@ QX_X_BF16 = 2
 HIDDEN = 5120
 MAX_ROWS = 64
 MAX_TOPK = 8
+STATIC_MAX_ROWS = 8
+STATIC_MAX_TOPK = 8
+STATIC_MAX_WIDTH = 2304
 
 
 class QxArena(ctypes.Structure):
@@ -84,6 +87,8 @@ SIGNATURES = [
     ("qx_slice_workspace_bytes", ctypes.c_size_t,
      [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     ("qx_slice_decode", ctypes.c_int,
+     [ctypes.POINTER(QxArena), ctypes.POINTER(QxSliceArgs), ctypes.c_void_p]),
+    ("qx_slice_decode_static", ctypes.c_int,
      [ctypes.POINTER(QxArena), ctypes.POINTER(QxSliceArgs), ctypes.c_void_p]),
     ("qx_combine_ordered", ctypes.c_int,
      [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p,

@@ -1,0 +1,78 @@
+"""qx_slice_decode_static: the decode slice for callers that cannot allocate.
+
+A serving process whose device memory is already claimed by its expert arena
+and pools, or a host runtime calling through an FFI with no CUDA allocator,
+cannot hand the slice a workspace. This entry point uses a fixed scratch array
+inside the library instead. The test calls it through the C ABI twice in a row
+with different inputs and checks each result against the workspace-taking
+entry point on the same inputs (same kernels, so the outputs are identical),
+and that a call larger than the array's limits is refused.
+
+Kept in a file of its own that pytest collects last; it passes alone in a
+fresh process and after the other tests.
+"""
+
+import ctypes
+
+import pytest
+import torch
+
+import helpers as H
+
+pytestmark = pytest.mark.gpu
+
+
+def _args(_lib, x, inv, ids, tw, out, c0, c1, ws=None):
+    return _lib.QxSliceArgs(
+        ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(inv.data_ptr()), x.stride(0), _lib.QX_X_E4M3,
+        ctypes.c_void_p(ids.data_ptr()), 0, ctypes.c_void_p(tw.data_ptr()),
+        x.shape[0], ids.shape[1], c0, c1, 10.0, 1,
+        ctypes.c_void_p(out.data_ptr()), out.stride(0),
+        ctypes.c_void_p(ws.data_ptr() if ws is not None else 0), ws.numel() if ws is not None else 0)
+
+
+def test_static_scratch_entry_matches_workspace_entry(cuda_ready):
+    from qmesh_b200 import _lib
+    from qmesh_b200.arena import Arena
+    from qmesh_b200.expert_slice import alloc_workspace
+    lib = _lib.load()
+    dev = cuda_ready
+    layer = H.small_layer(41, 16, inter=512)
+    ar = Arena(dev, 1, 16, 0, 512)
+    ar.load_layer(0, layer)
+    view = ar.view(0)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for call, (rows, seed) in enumerate([(6, 51), (3, 52)]):
+        ids, tw = H.random_routing(rows, 16, seed)
+        _, q, inv = H.activations(rows, seed)
+        q, inv, ids, tw = q.to(dev), inv.to(dev), ids.to(dev), tw.to(dev)
+        out_static = torch.full((rows, 5120), float("nan"), dtype=torch.bfloat16, device=dev)
+        out_ref = torch.empty(rows, 5120, dtype=torch.bfloat16, device=dev)
+        a = _args(_lib, q, inv, ids, tw, out_static, 0, 512)
+        assert lib.qx_slice_decode_static(ctypes.byref(view), ctypes.byref(a), stream) == _lib.QX_OK
+        ws = alloc_workspace(rows, 6, 0, 512, dev)
+        b = _args(_lib, q, inv, ids, tw, out_ref, 0, 512, ws)
+        assert lib.qx_slice_decode(ctypes.byref(view), ctypes.byref(b), stream) == _lib.QX_OK
+        torch.cuda.synchronize()
+        assert torch.equal(out_static, out_ref), f"call {call}"
+        H.assert_parity(out_static, H.oracle_out(H.ingest(q.cpu(), inv.cpu()), ids.cpu(), tw.cpu(), layer, 0, 512),
+                         f"static call {call}")
+
+
+def test_static_scratch_entry_refuses_calls_beyond_its_limits(cuda_ready):
+    from qmesh_b200 import _lib
+    from qmesh_b200.arena import Arena
+    lib = _lib.load()
+    dev = cuda_ready
+    layer = H.small_layer(42, 8, inter=256)
+    ar = Arena(dev, 1, 8, 0, 256)
+    ar.load_layer(0, layer)
+    view = ar.view(0)
+    rows = _lib.STATIC_MAX_ROWS + 1
+    ids, tw = H.random_routing(rows, 8, 5)
+    _, q, inv = H.activations(rows, 5)
+    q, inv, ids, tw = q.to(dev), inv.to(dev), ids.to(dev), tw.to(dev)
+    out = torch.empty(rows, 5120, dtype=torch.bfloat16, device=dev)
+    a = _args(_lib, q, inv, ids, tw, out, 0, 256)
+    rc = lib.qx_slice_decode_static(ctypes.byref(view), ctypes.byref(a), None)
+    assert rc == _lib.QX_ERR_SHAPE
