@@ -124,6 +124,7 @@ def run_ours(args) -> dict | None:
     from qmesh_b200.arena import Arena
     from qmesh_b200.combine import combine_ordered
     from qmesh_b200.expert_slice import alloc_workspace, launch
+    from qmesh_b200.shard import combine_across_ranks, shard_range
     build.build()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -134,8 +135,8 @@ def run_ours(args) -> dict | None:
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
     rows = args.rows
-    width = INTER // world
-    a0, a1 = rank * width, (rank + 1) * width
+    a0, a1 = shard_range(rank, world)
+    width = a1 - a0
     layers = args.layers
     n_exp = args.experts
     ar = Arena(dev, layers, n_exp, a0, a1)
@@ -157,9 +158,7 @@ def run_ours(args) -> dict | None:
         q, inv, ids, tw = dq[i % len(dq)]
         launch(views[i % layers], q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=stream.cuda_stream)
         if world > 1:
-            dist.all_gather(gathered, part)
-            if rank == 0:
-                combine_ordered(gathered, out=out)
+            combine_across_ranks(part, dst=0, out=out, combine=combine_ordered, gathered=gathered)
 
     for i in range(args.warmup):
         step(i)
@@ -198,9 +197,7 @@ def run_ours(args) -> dict | None:
         launch(views[i % layers], dev_in[0], dev_in[2], dev_in[3], part, a0, a1, ws, x_scale=dev_in[1],
                stream=stream.cuda_stream)
         if world > 1:
-            dist.all_gather(gathered, part)
-            if rank == 0:
-                combine_ordered(gathered, out=out)
+            if combine_across_ranks(part, dst=0, out=out, combine=combine_ordered, gathered=gathered) is not None:
                 out_h.copy_(out, non_blocking=True)
         else:
             out_h.copy_(part, non_blocking=True)
