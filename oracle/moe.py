@@ -73,6 +73,24 @@ def make_layer(n_experts: int, gen: torch.Generator, hidden: int = HIDDEN, inter
     return out
 
 
+def random_code_layer(n_experts: int, gen: torch.Generator, hidden: int = HIDDEN, inter: int = INTER):
+    """Pack tensors filled with uniform random NVFP4 codes and moderate e4m3 scales.
+
+    For timing only: the CPU path's cost depends on the shapes, not on the
+    values, and drawing codes directly skips the quantiser (seconds per expert).
+    """
+    def codes(*shape):
+        return torch.randint(0, 256, shape, generator=gen, dtype=torch.uint8)
+
+    def scales(*shape):  # e4m3 bytes 0x30..0x47: 0.5 .. 3.75
+        return torch.randint(0x30, 0x48, shape, generator=gen, dtype=torch.uint8)
+
+    e = n_experts
+    return dict(c13=codes(e, 2 * inter, hidden // 2), s13=scales(e, 2 * inter, hidden // 16),
+                g13=torch.full((e,), 1e-3), c2=codes(e, hidden, inter // 2),
+                s2=scales(e, hidden, inter // 16), g2=torch.full((e,), 1e-3))
+
+
 def config0(seed: int = 0, n_experts: int = 8, rows: int = 1, hidden: int = HIDDEN,
             inter: int = INTER):
     """8 experts, hidden 5120, intermediate 2304, rows=1, top-6.
