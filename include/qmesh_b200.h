@@ -140,6 +140,16 @@ int qx_combine_ordered(const uint16_t* const* parts, int32_t n_parts, int64_t pa
  * `stream`): bit set of QX_DEV_*. */
 int qx_status_read(const void* workspace, uint32_t* status, void* stream);
 
+/* Self-check of the block-scaled NVFP4 tensor-core path (no counterpart in the
+ * reference): d[128][n] (FP32, row-major) = sum over nkb 64-wide K blocks of
+ * (A * SFA) x (B * SFB)^T, computed by tcgen05.mma.kind::mxf4nvf4 with the
+ * operand layouts the decode kernels stream. `a` holds nkb K blocks of 4608
+ * bytes (a 128-row tile of 4096 bytes, then its 512-byte scale atom); `b` holds
+ * nkb K blocks of n*32 + 512*ceil(n/128) bytes (tile, then one atom per 128 rows). n in {16, 32, ..., 256}, nkb in 1..8, a and b
+ * 16-byte aligned, status a device word (QX_DEV_TIMEOUT on a wait that ran out). */
+int qx_diag_nvf4_tile(const uint8_t* a, const uint8_t* b, int32_t n, int32_t nkb, float* d,
+                      uint32_t* status, void* stream);
+
 /* Library version string. */
 const char* qx_version(void);
 

@@ -1,0 +1,127 @@
+// tcgen05 (5th-generation tensor core) helpers for sm_100a: TMEM allocation,
+// shared-memory matrix descriptors, the block-scaled NVFP4 MMA
+// (kind::mxf4nvf4, e2m1 x e2m1 with one UE4M3 scale per 16 elements along K),
+// scale-factor copies into TMEM, commits and accumulator loads.
+//
+// Operand layout used throughout (K-major, no swizzle): one MMA consumes K = 64
+// e2m1 values per row = 32 bytes = two 16-byte "core matrix" columns. A tile of
+// R rows (R % 8 == 0) for one 64-wide K block is stored as
+//     [R/8 row groups][2 K halves][8 rows][16 bytes]
+// so the core matrix of (row group g, half h) starts at g*256 + h*128 bytes:
+// leading (K) byte offset 128, stride (row-group) byte offset 256. Inside the
+// 16 bytes, element 2i is the low nibble of byte i.
+//
+// Scale factors of one 64-wide K block for up to 128 rows form a 512-byte atom:
+// byte (row % 32) * 16 + (row / 32) * 4 + j holds the scale of elements
+// [16j, 16j + 16) of `row`. `tcgen05.cp.32x128b.warpx4` places the atom's 32
+// sixteen-byte lines in TMEM lanes 0..31 and copies them to the other three lane
+// quarters, four 32-bit columns wide: the arrangement the MMA reads its scales
+// from (lane = row % 32, byte = (row / 32) * 4 + j). For a B operand of more
+// than 128 rows, rows [128a, 128a + 128) form atom a, copied to the next four
+// columns (byte (row / 32) * 4 + j still holds for the 8-column span).
+#pragma once
+
+#include <stdint.h>
+
+#include "qx_ptx.cuh"
+
+namespace qx {
+namespace tc {
+
+constexpr uint32_t KBLK = 64;             // e2m1 elements per MMA along K
+constexpr uint32_t ROWB = KBLK / 2;       // bytes per row per K block
+constexpr uint32_t SF_ATOM = 512;         // scale bytes per K block (<= 128 rows)
+constexpr uint32_t LBO = 128;             // K-half to K-half
+constexpr uint32_t SBO = 256;             // row group to row group
+
+// Byte offset of (row, k) inside one K block's operand tile (k in [0, 64)); the
+// nibble is k & 1.
+__host__ __device__ constexpr uint32_t opnd_off(uint32_t row, uint32_t k) {
+  return (row >> 3) * SBO + (k >> 5) * LBO + (row & 7) * 16 + ((k & 31) >> 1);
+}
+// Byte offset of the scale of (row, 16-block j) inside one K block's atom.
+__host__ __device__ constexpr uint32_t sf_off(uint32_t row, uint32_t j) {
+  return (row & 31) * 16 + (row >> 5) * 4 + j;
+}
+
+// ---- TMEM allocation (warp-wide, .sync.aligned) --------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// ---- ordering between thread syncs and tcgen05 operations ----------------------
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// ---- descriptors ---------------------------------------------------------------
+// Shared-memory matrix descriptor, K-major, no swizzle (layout type 0),
+// descriptor version 1, base offset 0.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  return d;
+}
+
+// Instruction descriptor of kind::mxf4nvf4: A and B e2m1 (format 1), UE4M3
+// scales (bit 23 clear), both K-major, dense, M = 128, N = n (multiple of 16,
+// 16..256), K = 64, scale-factor byte ids 0.
+__host__ __device__ constexpr uint32_t idesc_nvf4(uint32_t n) {
+  return (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+// ---- tensor-core operations (issued by one thread) -----------------------------
+// D[tmem_d] (+)= (A * SFA) x (B * SFB)^T for one 64-wide K block.
+__device__ __forceinline__ void mma_nvf4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t tsfa, uint32_t tsfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb)
+      : "memory");
+}
+
+// One 512-byte scale atom (32 lines x 16 bytes) from shared memory into TMEM
+// lanes 0..127 (copied to all four lane quarters), 4 columns at `taddr`.
+__device__ __forceinline__ void cp_sf_atom(uint32_t taddr, uint32_t saddr) {
+  const uint64_t d = sdesc(saddr, 0, 128);
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(d) : "memory");
+}
+
+// Arrive once on `bar` when every tcgen05 operation this thread issued so far
+// has completed (the operands in shared memory may then be overwritten and the
+// accumulator read).
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// ---- accumulator loads ----------------------------------------------------------
+// Lane i of the calling warp receives TMEM lane (taddr.lane + i), 16
+// consecutive 32-bit columns starting at taddr.col. The wait sits in the same
+// asm statement so no use of the registers can be scheduled before it.
+__device__ __forceinline__ void ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];\n\ttcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+}  // namespace tc
+}  // namespace qx

@@ -95,6 +95,9 @@ SIGNATURES = [
       ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]),
     ("qx_status_read", ctypes.c_int,
      [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32), ctypes.c_void_p]),
+    ("qx_diag_nvf4_tile", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+      ctypes.c_void_p, ctypes.c_void_p]),
     ("qx_version", ctypes.c_char_p, []),
 ]
 
