@@ -139,7 +139,7 @@ def run_ours(args) -> dict | None:
     width = a1 - a0
     layers = args.layers
     n_exp = args.experts
-    ar = Arena(dev, layers, n_exp, a0, a1)
+    ar = Arena(dev, layers, n_exp, a0, a1, layout=args.layout)
     ar.check_memory()
     for li in range(layers):
         ar.fill_synthetic(li, seed=1000 + li)
@@ -147,7 +147,7 @@ def run_ours(args) -> dict | None:
     draws = make_inputs(args.draws, rows, seed=1, n_experts=n_exp)
     dq = [(q.to(dev), inv.to(dev), ids.to(dev), tw.to(dev)) for q, inv, ids, tw in draws]
     uniq = [len(set(ids.flatten().tolist())) for _, _, ids, _ in draws]
-    ws = alloc_workspace(rows, TOPK, a0, a1, dev)
+    ws = alloc_workspace(rows, TOPK, a0, a1, dev, args.layout)
     part = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
     gathered = [torch.empty_like(part) for _ in range(world)] if world > 1 else None
     out = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
@@ -156,7 +156,8 @@ def run_ours(args) -> dict | None:
 
     def step(i: int) -> None:
         q, inv, ids, tw = dq[i % len(dq)]
-        launch(views[i % layers], q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=stream.cuda_stream)
+        launch(views[i % layers], q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=stream.cuda_stream,
+               layout=args.layout)
         if world > 1:
             combine_across_ranks(part, dst=0, out=out, combine=combine_ordered, gathered=gathered)
 
@@ -195,7 +196,7 @@ def run_ours(args) -> dict | None:
         for d, s in zip(dev_in, src):
             d.copy_(s, non_blocking=True)
         launch(views[i % layers], dev_in[0], dev_in[2], dev_in[3], part, a0, a1, ws, x_scale=dev_in[1],
-               stream=stream.cuda_stream)
+               stream=stream.cuda_stream, layout=args.layout)
         if world > 1:
             if combine_across_ranks(part, dst=0, out=out, combine=combine_ordered, gathered=gathered) is not None:
                 out_h.copy_(out, non_blocking=True)
@@ -224,7 +225,8 @@ def run_ours(args) -> dict | None:
     for i, (a, b) in enumerate(evs):
         q, inv, ids, tw = dq[i % len(dq)]
         a.record(stream)
-        launch(views[i % layers], q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=stream.cuda_stream)
+        launch(views[i % layers], q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=stream.cuda_stream,
+               layout=args.layout)
         b.record(stream)
     torch.cuda.synchronize()
     k_us = [a.elapsed_time(b) * 1e3 for a, b in evs]
@@ -254,7 +256,9 @@ def run_ours(args) -> dict | None:
                        "topk": TOPK, "columns_per_rank": width, "resident_layers": layers,
                        "routing_draws": args.draws, "mean_unique_experts": round(mean_u, 2),
                        "l2": "inputs larger than L2: ~%.0f MB of expert weights per step" % (mean_u * EXPERT_BYTES / 1e6),
-                       "parallelism": f"column-split tp{world}"},
+                       "parallelism": f"column-split tp{world}",
+                       "kernel": "tcgen05 mxf4nvf4 (8-term NVFP4 activations)" if args.layout == "tc"
+                       else "register dequant + mma.sync"},
             "tokens_per_s": round(rows / (us_layer * 1e-6), 1),
             "weight_gbs": round(gbs, 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
@@ -346,6 +350,8 @@ def main() -> int:
     ap.add_argument("--draws", type=int, default=16)
     ap.add_argument("--cpu-layers", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--layout", default="tc", choices=["tc", "frag"],
+                    help="arena layout / kernel: tc = tcgen05 block-scaled MMA, frag = register dequant + mma.sync")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

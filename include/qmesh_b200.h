@@ -140,6 +140,20 @@ int qx_combine_ordered(const uint16_t* const* parts, int32_t n_parts, int64_t pa
  * `stream`): bit set of QX_DEV_*. */
 int qx_status_read(const void* workspace, uint32_t* status, void* stream);
 
+/* ---- tensor-core slice (tcgen05 block-scaled NVFP4 MMA) ----------------------
+ * Same call contract as qx_slice_decode over an arena in the tensor-core tile
+ * layout: w13 [E][ceil(W/64)][80][4608 B], w2 [E][40][ceil(W/64)][4608 B] for
+ * arena width W = a1 - a0 (each 4608-byte K block = a 128-row x 64-element
+ * operand tile, then its 512-byte scale atom; columns past a1 are zero). The
+ * activations enter the MMA as eight residual NVFP4 terms, so results stay
+ * within the same tolerance of the reference's FP32 arithmetic. Requires
+ * (c0 - a0) % 64 == 0 and c1 % 32 == 0. Replaces the same reference body as
+ * qx_slice_decode (gx/kernels/ext_variant.cu:11-24). */
+size_t qx_arena_tc_w13_bytes(int32_t n_experts, int32_t width);
+size_t qx_arena_tc_w2_bytes(int32_t n_experts, int32_t width);
+size_t qx_slice_workspace_tc_bytes(int32_t rows, int32_t topk, int32_t c0, int32_t c1);
+int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* args, void* stream);
+
 /* Self-check of the block-scaled NVFP4 tensor-core path (no counterpart in the
  * reference): d[128][n] (FP32, row-major) = sum over nkb 64-wide K blocks of
  * (A * SFA) x (B * SFB)^T, computed by tcgen05.mma.kind::mxf4nvf4 with the

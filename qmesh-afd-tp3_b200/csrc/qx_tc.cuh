@@ -123,5 +123,48 @@ __device__ __forceinline__ void ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// As ld16, 8 columns.
+__device__ __forceinline__ void ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- NVFP4 encoders for operands built on the device ---------------------------
+// e2m1 code (nibble) of y, round to nearest even, saturating at +-6.
+__device__ __forceinline__ uint32_t e2m1_rn(float y) {
+  uint32_t r;
+  asm("{ .reg .b8 b; cvt.rn.satfinite.e2m1x2.f32 b, %1, %2; cvt.u32.u8 %0, b; }" : "=r"(r) : "f"(0.f), "f"(y));
+  return r & 15u;
+}
+// Value of an e2m1 code (exact).
+__device__ __forceinline__ float e2m1_val(uint32_t code) { return f16lo_to_f32(e2m1x2_to_f16x2(code & 15u)); }
+// Value of an e4m3 byte (exact).
+__device__ __forceinline__ float e4m3_val(uint32_t b) { return f16lo_to_f32(e4m3x2_to_f16x2(b & 0xFFu)); }
+// Smallest e4m3 byte whose value is >= v (v >= 0); 0 for v == 0; 448 caps.
+__device__ __forceinline__ uint32_t e4m3_ru(float v) {
+  if (!(v > 0.f)) return 0u;
+  uint32_t two;
+  asm("{ .reg .b16 h; cvt.rn.satfinite.e4m3x2.f32 h, %1, %2; cvt.u32.u16 %0, h; }" : "=r"(two) : "f"(0.f), "f"(v));
+  uint32_t b = two & 0xFFu;
+  if (e4m3_val(b) < v && b < 0x7Eu) ++b;
+  return b;
+}
+// e4m3 byte divided by 2^sh (sh >= 0), rounded to nearest even on the e4m3 grid.
+__device__ __forceinline__ uint32_t e4m3_shift(uint32_t b, int sh) {
+  b &= 0xFFu;
+  if (sh <= 0 || b == 0u) return b;
+  const int e = (int)((b >> 3) & 15u);
+  if (e - sh >= 1) return (uint32_t)((e - sh) << 3) | (b & 7u);   // stays normal: exact
+  const float v = ldexpf(e4m3_val(b), -sh);                       // < 2^-6: subnormal grid 2^-9
+  return (uint32_t)__float2int_rn(v * 512.f);
+}
+
 }  // namespace tc
 }  // namespace qx

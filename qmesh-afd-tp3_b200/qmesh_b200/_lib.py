@@ -95,6 +95,12 @@ SIGNATURES = [
       ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]),
     ("qx_status_read", ctypes.c_int,
      [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32), ctypes.c_void_p]),
+    ("qx_arena_tc_w13_bytes", ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32]),
+    ("qx_arena_tc_w2_bytes", ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32]),
+    ("qx_slice_workspace_tc_bytes", ctypes.c_size_t,
+     [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+    ("qx_slice_decode_tc", ctypes.c_int,
+     [ctypes.POINTER(QxArena), ctypes.POINTER(QxSliceArgs), ctypes.c_void_p]),
     ("qx_diag_nvf4_tile", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
       ctypes.c_void_p, ctypes.c_void_p]),

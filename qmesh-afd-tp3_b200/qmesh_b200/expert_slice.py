@@ -1,6 +1,7 @@
 """The routed-expert slice call: the drop-in for the reference's decode body.
 
-Two forms over the same C entry point (qx_slice_decode):
+Two forms over the same C entry points (qx_slice_decode_tc for a tensor-core
+layout arena, qx_slice_decode for a register-dequant layout arena):
 
 * ``expert_slice(layer, x, ids, tw, c0=, c1=, x_scale=)`` -- the north-star form:
   FP8 e4m3 activations [rows, 5120] with an FP32 dequant scale per row (or one
@@ -27,16 +28,18 @@ from .arena import Arena
 SWIGLU_LIMIT = 10.0
 
 
-def workspace_bytes(rows: int, topk: int, c0: int, c1: int) -> int:
-    n = _lib.load().qx_slice_workspace_bytes(rows, topk, c0, c1)
+def workspace_bytes(rows: int, topk: int, c0: int, c1: int, layout: str = "tc") -> int:
+    lib = _lib.load()
+    fn = lib.qx_slice_workspace_tc_bytes if layout == "tc" else lib.qx_slice_workspace_bytes
+    n = fn(rows, topk, c0, c1)
     if n == 0:
         raise ValueError(f"no workspace for rows={rows} topk={topk} columns [{c0}, {c1})")
     return n
 
 
-def alloc_workspace(rows: int, topk: int, c0: int, c1: int, device) -> torch.Tensor:
+def alloc_workspace(rows: int, topk: int, c0: int, c1: int, device, layout: str = "tc") -> torch.Tensor:
     """Workspace for calls of up to `rows` rows over `c1 - c0` columns."""
-    return torch.empty(workspace_bytes(rows, topk, c0, c1), dtype=torch.uint8, device=device)
+    return torch.empty(workspace_bytes(rows, topk, c0, c1, layout), dtype=torch.uint8, device=device)
 
 
 def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
@@ -45,8 +48,9 @@ def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
 
 def launch(view: _lib.QxArena, x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, out: torch.Tensor,
            c0: int, c1: int, workspace: torch.Tensor, x_scale: torch.Tensor | None = None,
-           swiglu_limit: float = SWIGLU_LIMIT, has_limit: bool = True, stream=None) -> None:
-    """Validate and launch one slice call (no allocation, no host sync)."""
+           swiglu_limit: float = SWIGLU_LIMIT, has_limit: bool = True, stream=None, layout: str = "tc") -> None:
+    """Validate and launch one slice call (no allocation, no host sync). `layout` is
+    the arena's: "tc" runs qx_slice_decode_tc, "frag" qx_slice_decode."""
     lib = _lib.load()
     rows = x.shape[0]
     if x.dtype == torch.bfloat16:
@@ -79,8 +83,9 @@ def launch(view: _lib.QxArena, x: torch.Tensor, ids: torch.Tensor, tw: torch.Ten
         _ptr(out), out.stride(0), _ptr(workspace), workspace.numel())
     if stream is None:
         stream = torch.cuda.current_stream(x.device).cuda_stream
-    rc = lib.qx_slice_decode(ctypes.byref(view), ctypes.byref(args), ctypes.c_void_p(stream))
-    _lib.check(rc, "qx_slice_decode")
+    name = "qx_slice_decode_tc" if layout == "tc" else "qx_slice_decode"
+    rc = getattr(lib, name)(ctypes.byref(view), ctypes.byref(args), ctypes.c_void_p(stream))
+    _lib.check(rc, name)
 
 
 def expert_slice(arena: Arena, li: int, x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor,
@@ -94,9 +99,9 @@ def expert_slice(arena: Arena, li: int, x: torch.Tensor, ids: torch.Tensor, tw: 
     if out is None:
         out = torch.empty(rows, _lib.HIDDEN, dtype=torch.bfloat16, device=x.device)
     if workspace is None:
-        workspace = alloc_workspace(rows, ids.shape[1], c0, c1, x.device)
+        workspace = alloc_workspace(rows, ids.shape[1], c0, c1, x.device, arena.layout)
     launch(arena.view(li), x, ids, tw, out, c0, c1, workspace, x_scale=x_scale,
-           swiglu_limit=max(swiglu_limit, 0.0), has_limit=swiglu_limit > 0)
+           swiglu_limit=max(swiglu_limit, 0.0), has_limit=swiglu_limit > 0, layout=arena.layout)
     return out
 
 
@@ -120,7 +125,7 @@ def make_body(arena: Arena, swiglu_limit: float, max_rows: int = 16, topk: int =
     _lib.load()
     has_limit = bool(swiglu_limit > 0)
     limit = float(max(swiglu_limit, 0.0))
-    ws = alloc_workspace(max_rows, topk, arena.a0, arena.a1, arena.dev)
+    ws = alloc_workspace(max_rows, topk, arena.a0, arena.a1, arena.dev, arena.layout)
 
     def body(li: int, r: int, x, ids, tw, out, ws13=None, ws2=None, a1g=None) -> None:
         if not arena.loaded(li):
@@ -133,5 +138,5 @@ def make_body(arena: Arena, swiglu_limit: float, max_rows: int = 16, topk: int =
         if not 1 <= r <= max_rows:
             raise ValueError(f"row count {r} outside 1..{max_rows}")
         launch(arena.view(li), x[:r], ids[:r], tw[:r], out[:r], arena.a0, arena.a1, ws,
-               swiglu_limit=limit, has_limit=has_limit)
+               swiglu_limit=limit, has_limit=has_limit, layout=arena.layout)
     return body

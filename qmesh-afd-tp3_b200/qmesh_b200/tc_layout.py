@@ -69,3 +69,124 @@ def interleave(tiles: torch.Tensor, atoms: torch.Tensor) -> torch.Tensor:
     """[KB, R*32] tiles + [KB, 512] atoms -> flat bytes [KB * (R*32 + 512)], each K
     block's tile followed by its scale atom (the unit one bulk copy stages)."""
     return torch.cat([tiles, atoms], dim=1).reshape(-1).contiguous()
+
+
+# ---------------------------------------------------------------- arena layout
+# For arena columns [a0, a1) (width W, NTA = ceil(W / 64) column tiles; columns
+# past a1 are zero rows):
+#   w13  [E][NTA][80 K blocks][4608 B]: tile i is rows 0..63 = gate columns
+#        a0 + 64i + r, rows 64..127 = their up columns, over K = 5120; each K block
+#        is the 4096-byte operand tile then its 512-byte scale atom. A column
+#        tile streams as one contiguous 368,640-byte run.
+#   w2   [E][40 row tiles][NTA K blocks][4608 B]: row tile j is output rows
+#        128j .. 128j + 127 over K = the arena's columns (zero past a1). Any
+#        64-aligned column range of one row tile is one contiguous run.
+
+HIDDEN = 5120
+KB1 = HIDDEN // KBLK         # 80
+HT = HIDDEN // 128           # 40
+A_KB = 128 * ROWB + SF_ATOM  # 4608
+
+
+def tiles_of(width: int) -> int:
+    return (width + KBLK - 1) // KBLK
+
+
+def _operand_from_bytes(rows_bytes: torch.Tensor) -> torch.Tensor:
+    """[..., 128, KB*32] code bytes -> [..., KB, 4096] operand tiles."""
+    *lead, r, nb = rows_bytes.shape
+    kb = nb // ROWB
+    t = rows_bytes.reshape(*lead, r // 8, 8, kb, 2, 16)
+    n = len(lead)
+    perm = list(range(n)) + [n + 2, n, n + 3, n + 1, n + 4]
+    return t.permute(*perm).reshape(*lead, kb, r * ROWB)
+
+
+def _bytes_from_operand(tiles: torch.Tensor, r: int = 128) -> torch.Tensor:
+    """Inverse of _operand_from_bytes."""
+    *lead, kb, _ = tiles.shape
+    t = tiles.reshape(*lead, kb, r // 8, 2, 8, 16)
+    n = len(lead)
+    perm = list(range(n)) + [n + 1, n + 3, n, n + 2, n + 4]
+    return t.permute(*perm).reshape(*lead, r, kb * ROWB)
+
+
+def _atoms_from_scales(sc: torch.Tensor) -> torch.Tensor:
+    """[..., 128, KB*4] scale bytes -> [..., KB, 512] atoms."""
+    *lead, r, nb = sc.shape
+    kb = nb // 4
+    t = sc.reshape(*lead, 4, 32, kb, 4)
+    n = len(lead)
+    perm = list(range(n)) + [n + 2, n + 1, n, n + 3]
+    return t.permute(*perm).reshape(*lead, kb, SF_ATOM)
+
+
+def _scales_from_atoms(atoms: torch.Tensor) -> torch.Tensor:
+    """Inverse of _atoms_from_scales."""
+    *lead, kb, _ = atoms.shape
+    t = atoms.reshape(*lead, kb, 32, 4, 4)
+    n = len(lead)
+    perm = list(range(n)) + [n + 2, n + 1, n, n + 3]
+    return t.permute(*perm).reshape(*lead, 128, kb * 4)
+
+
+def _pad_rows(t: torch.Tensor, dim: int, n: int) -> torch.Tensor:
+    if t.shape[dim] == n:
+        return t
+    shape = list(t.shape)
+    shape[dim] = n - t.shape[dim]
+    return torch.cat([t, torch.zeros(shape, dtype=t.dtype, device=t.device)], dim=dim)
+
+
+def pack_w13(c13: torch.Tensor, s13: torch.Tensor, src_a0: int, a0: int, a1: int) -> torch.Tensor:
+    """Pack-format w13 (codes [E, 2C, H/2], scales [E, 2C, H/16], source columns
+    from src_a0) -> tensor-core arena w13 for columns [a0, a1), flat uint8."""
+    e, two_c, _ = c13.shape
+    c = two_c // 2
+    lo, hi = a0 - src_a0, a1 - src_a0
+    if lo < 0 or hi > c or (hi - lo) % 32:
+        raise ValueError(f"columns [{a0}, {a1}) not inside the source slice or not 32-aligned")
+    nta = tiles_of(hi - lo)
+    w = nta * KBLK
+    gate = _pad_rows(c13[:, lo:hi], 1, w).reshape(e, nta, 64, HIDDEN // 2)
+    up = _pad_rows(c13[:, c + lo:c + hi], 1, w).reshape(e, nta, 64, HIDDEN // 2)
+    ops = _operand_from_bytes(torch.cat([gate, up], dim=2))                     # [E, NTA, 80, 4096]
+    gs = _pad_rows(s13[:, lo:hi], 1, w).reshape(e, nta, 64, HIDDEN // 16)
+    us = _pad_rows(s13[:, c + lo:c + hi], 1, w).reshape(e, nta, 64, HIDDEN // 16)
+    atoms = _atoms_from_scales(torch.cat([gs, us], dim=2))                      # [E, NTA, 80, 512]
+    return torch.cat([ops, atoms], dim=-1).contiguous().view(-1)
+
+
+def pack_w2(c2: torch.Tensor, s2: torch.Tensor, src_a0: int, a0: int, a1: int) -> torch.Tensor:
+    """Pack-format w2 (codes [E, H, C/2], scales [E, H, C/16]) -> tensor-core arena
+    w2 for columns [a0, a1), flat uint8."""
+    e, h, c_half = c2.shape
+    lo, hi = a0 - src_a0, a1 - src_a0
+    if lo < 0 or hi > 2 * c_half or (hi - lo) % 32:
+        raise ValueError(f"columns [{a0}, {a1}) not inside the source slice or not 32-aligned")
+    nta = tiles_of(hi - lo)
+    codes = _pad_rows(c2[:, :, lo // 2:hi // 2], 2, nta * ROWB).reshape(e, HT, 128, nta * ROWB)
+    scales = _pad_rows(s2[:, :, lo // 16:hi // 16], 2, nta * 4).reshape(e, HT, 128, nta * 4)
+    return torch.cat([_operand_from_bytes(codes), _atoms_from_scales(scales)], dim=-1).contiguous().view(-1)
+
+
+def unpack_w13(flat: torch.Tensor, n_experts: int, width: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Inverse of pack_w13 -> (codes [E, 2W, H/2], scales [E, 2W, H/16])."""
+    e, nta = n_experts, tiles_of(width)
+    t = flat.view(e, nta, KB1, A_KB)
+    rows = _bytes_from_operand(t[..., :128 * ROWB])                            # [E, NTA, 128, 2560]
+    sc = _scales_from_atoms(t[..., 128 * ROWB:])                               # [E, NTA, 128, 320]
+    gate = rows[:, :, :64].reshape(e, nta * 64, -1)[:, :width]
+    up = rows[:, :, 64:].reshape(e, nta * 64, -1)[:, :width]
+    gs = sc[:, :, :64].reshape(e, nta * 64, -1)[:, :width]
+    us = sc[:, :, 64:].reshape(e, nta * 64, -1)[:, :width]
+    return torch.cat([gate, up], 1).contiguous(), torch.cat([gs, us], 1).contiguous()
+
+
+def unpack_w2(flat: torch.Tensor, n_experts: int, width: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Inverse of pack_w2 -> (codes [E, H, W/2], scales [E, H, W/16])."""
+    e, nta = n_experts, tiles_of(width)
+    t = flat.view(e, HT, nta, A_KB)
+    codes = _bytes_from_operand(t[..., :128 * ROWB]).reshape(e, HIDDEN, nta * ROWB)[:, :, :width // 2]
+    scales = _scales_from_atoms(t[..., 128 * ROWB:]).reshape(e, HIDDEN, nta * 4)[:, :, :width // 16]
+    return codes.contiguous(), scales.contiguous()

@@ -1,19 +1,24 @@
 """CPU model of the residual NVFP4 term decomposition the tensor-core decode path
-feeds to `tcgen05.mma.kind::mxf4nvf4` (test infrastructure).
+feeds to `tcgen05.mma.kind::mxf4nvf4` (test infrastructure; the kernel's own
+arithmetic, so tests can compare its buffers bit for bit).
 
-A vector v (one activation row, or one routed pair's SwiGLU output) becomes T
-NVFP4 terms, v ~= sum_t G_t * s_{t,b} * q_{t,k}:
+A vector v (one activation row, or one routed pair's SwiGLU output over a
+64-column tile) becomes T = 8 NVFP4 terms, v ~= sum_t G_t * s_{t,b} * q_{t,k}:
 
-  * G_t = 2^(E - 2t), E = ceil(log2(amax(v) / (6 * 448))), a per-vector power of
-    two (applied to the accumulator column in the epilogue);
-  * s_{t,b} = the smallest e4m3 value >= amax_b(r_t) / (6 G_t), one per 16 elements
-    (the MMA's block scale; rounding up keeps |r / (s G)| <= 6);
-  * q_{t,k} = e2m1 round-to-nearest-even of r_t,k / (s_{t,b} G_t);
-  * r_{t+1} = r_t - G_t s q (exact: every factor is a short power-of-two product).
+  * E = the smallest integer with 2688 * 2^E >= amax(v) (0 when v == 0), clamped to
+    [-100, 100]; G_t = 2^(E - 2t), applied to the accumulator column in the epilogue;
+  * s_{t,b} = the smallest e4m3 value >= fp32(amax_b(r_t) / (6 G_t)), one per 16
+    elements (the MMA's block scale); 0 when the block's residual is 0;
+  * q_{t,k} = e2m1 round-to-nearest-even of fp32(r_t,k / (s_{t,b} G_t)), saturating
+    at +-6;
+  * r_{t+1} = r_t - G_t s q, exact in fp32 (q s has at most 6 significant bits and
+    lies within a factor 2 of r when q != 0).
 
-Each term shrinks a block's residual by about 6x, and the 4x step between
-consecutive G_t keeps every block scale at or below the one before it, so the
-scales never overflow e4m3.
+Each term shrinks a block's residual about 6x; the 4x step between consecutive
+G_t keeps each block scale at or below the previous one, so none overflows e4m3.
+A tile decomposed with its own exponent E_loc is brought to a common exponent
+E >= E_loc by dividing every scale byte by 2^(E - E_loc) (exact while the result
+stays a normal e4m3 number, else rounded to nearest even on the subnormal grid).
 """
 
 from __future__ import annotations
@@ -22,7 +27,9 @@ import torch
 
 from oracle import nvfp4 as q4
 
+TERMS = 8
 E4M3_MAX = 448.0
+E_MIN, E_MAX = -100, 100
 
 
 def _e4m3_positive_table() -> torch.Tensor:
@@ -42,32 +49,56 @@ def e4m3_round_up(v: torch.Tensor) -> torch.Tensor:
 
 
 def exponent_for(amax: torch.Tensor) -> torch.Tensor:
-    """E with 2^E >= amax / 2688 (int32); amax == 0 gives a harmless E."""
-    a = amax.to(torch.float64) / (6.0 * E4M3_MAX)
-    e = torch.ceil(torch.log2(torch.where(a > 0, a, torch.ones_like(a))))
-    return torch.where(a > 0, e, torch.full_like(e, -126.0)).to(torch.int32)
+    """Smallest E with 2688 * 2^E >= amax, clamped to [-100, 100]; 0 for amax == 0."""
+    a = amax.to(torch.float64)
+    pos = a > 0
+    e = torch.ceil(torch.log2(torch.where(pos, a, torch.ones_like(a)) / 2688.0))
+    e = torch.where(2688.0 * torch.pow(2.0, e - 1) >= a, e - 1, e)
+    e = torch.where(2688.0 * torch.pow(2.0, e) < a, e + 1, e)
+    e = torch.where(pos, e.clamp(E_MIN, E_MAX), torch.zeros_like(e))
+    return e.to(torch.int32)
 
 
-def decompose(v: torch.Tensor, terms: int, exp: torch.Tensor | None = None):
+def decompose(v: torch.Tensor, terms: int = TERMS, exp: torch.Tensor | None = None):
     """v float32 [n, K] (K % 16 == 0) -> (codes uint8 [n, T, K] nibbles,
     scales uint8 [n, T, K/16] e4m3 bytes, E int32 [n]); exp overrides E."""
     n, k = v.shape
-    r = v.to(torch.float64).clone()
+    r = v.to(torch.float32).to(torch.float64).clone()
     e = exponent_for(v.abs().amax(dim=1)) if exp is None else exp.to(torch.int32)
     codes = torch.zeros(n, terms, k, dtype=torch.uint8)
     scales = torch.zeros(n, terms, k // 16, dtype=torch.uint8)
     for t in range(terms):
         g = torch.pow(2.0, (e - 2 * t).to(torch.float64)).view(n, 1)
         amax_b = r.view(n, k // 16, 16).abs().amax(dim=2)
-        sb = e4m3_round_up(amax_b / (6.0 * g))
+        v32 = amax_b.to(torch.float32) / (6.0 * g).to(torch.float32)
+        sb = e4m3_round_up(v32)
         s = q4.e4m3_decode(sb).to(torch.float64)
         sg = (s * g).repeat_interleave(16, dim=1)
-        ratio = torch.where(sg > 0, r / torch.where(sg > 0, sg, torch.ones_like(sg)), torch.zeros_like(r))
-        c = q4.e2m1_encode(ratio.to(torch.float32))
+        ratio = torch.where(sg > 0, r.to(torch.float32) / torch.where(sg > 0, sg, torch.ones_like(sg)).to(torch.float32),
+                            torch.zeros(n, k, dtype=torch.float32))
+        c = q4.e2m1_encode(ratio)
         codes[:, t] = c
         scales[:, t] = sb
         r = r - q4.e2m1_decode(c).to(torch.float64) * sg
     return codes, scales, e
+
+
+def shift_scales(scales: torch.Tensor, shift: torch.Tensor) -> torch.Tensor:
+    """e4m3 bytes divided by 2^shift (shift >= 0, broadcast), rounded to nearest even."""
+    val = q4.e4m3_decode(scales).to(torch.float64) * torch.pow(2.0, -shift.to(torch.float64))
+    return q4.e4m3_encode(val.to(torch.float32))
+
+
+def decompose_tiles(v: torch.Tensor, tile: int = 64, terms: int = TERMS):
+    """Tile-local decomposition (each `tile` columns with their own exponent), then
+    every tile's scales shifted to the largest exponent. Returns (codes, scales, E)."""
+    n, k = v.shape
+    parts = [decompose(v[:, i:i + tile], terms) for i in range(0, k, tile)]
+    eloc = torch.stack([p[2] for p in parts], dim=1)                 # [n, tiles]
+    emax = eloc.max(dim=1).values
+    codes = torch.cat([p[0] for p in parts], dim=2)
+    scales = torch.cat([shift_scales(p[1], (emax - eloc[:, i]).view(n, 1, 1)) for i, p in enumerate(parts)], dim=2)
+    return codes, scales, emax
 
 
 def reconstruct(codes: torch.Tensor, scales: torch.Tensor, e: torch.Tensor) -> torch.Tensor:

@@ -12,11 +12,14 @@ from oracle import moe, nvfp4 as oq
 pytestmark = pytest.mark.gpu
 
 
-def _arena(dev, layer, a0=0, a1=None, n_layers=1, li=0, src_a0=0):
+LAYOUTS = ["tc", "frag"]   # tensor-core kernel, register-dequant kernel
+
+
+def _arena(dev, layer, a0=0, a1=None, n_layers=1, li=0, src_a0=0, layout="tc"):
     from qmesh_b200.arena import Arena
     inter = layer["c13"].shape[1] // 2
     a1 = inter if a1 is None else a1
-    ar = Arena(dev, n_layers, layer["c13"].shape[0], a0, a1)
+    ar = Arena(dev, n_layers, layer["c13"].shape[0], a0, a1, layout=layout)
     ar.load_layer(li, layer, src_a0=src_a0)
     return ar
 
@@ -30,16 +33,21 @@ def _run(ar, q, inv, ids, tw, c0=None, c1=None, ws=None, **kw):
     return out
 
 
+@pytest.fixture(scope="module", params=LAYOUTS)
+def layout(request):
+    return request.param
+
+
 @pytest.fixture(scope="module")
-def small(cuda_ready):
+def small(cuda_ready, layout):
     layer = H.small_layer(21, 16, inter=512)
-    return layer, _arena(cuda_ready, layer)
+    return layer, _arena(cuda_ready, layer, layout=layout)
 
 
-def test_config0_parity(cuda_ready):
+def test_config0_parity(cuda_ready, layout):
     """8 experts, hidden 5120, intermediate 2304, rows=1, top-6."""
     c = H.config0_cached(0)
-    ar = _arena(cuda_ready, c)
+    ar = _arena(cuda_ready, c, layout=layout)
     out = _run(ar, c["q"], c["inv"], c["ids"], c["tw"])
     ref = H.oracle_out(H.ingest(c["q"], c["inv"]), c["ids"], c["tw"], c, 0, 2304)
     p = H.assert_parity(out, ref, "config0")
@@ -80,7 +88,7 @@ def test_padding_and_corrupt_ids(small):
     ids[1, 2] = -1
     ids[2, :] = -1
     _, q, inv = H.activations(rows, 9)
-    ws = alloc_workspace(rows, 6, 0, 512, ar.dev)
+    ws = alloc_workspace(rows, 6, 0, 512, ar.dev, ar.layout)
     out = _run(ar, q, inv, ids, tw, ws=ws)
     assert device_status(ws) == 0
     keep = ids >= 0
@@ -156,7 +164,7 @@ def test_column_ranges_and_ordered_combine(small):
 
 def test_rank_arena_equals_full_arena_slice(small, cuda_ready):
     layer, ar = small
-    rank = _arena(cuda_ready, layer, a0=128, a1=384)
+    rank = _arena(cuda_ready, layer, a0=128, a1=384, layout=ar.layout)
     rows = 6
     ids, tw = H.random_routing(rows, 16, 15)
     _, q, inv = H.activations(rows, 15)
@@ -218,7 +226,7 @@ def test_bounded_wait_reports_timeout_and_context_survives(small, monkeypatch):
     layer, ar = small
     ids, tw = H.random_routing(2, 16, 18)
     _, q, inv = H.activations(2, 18)
-    ws = alloc_workspace(2, 6, 0, 512, ar.dev)
+    ws = alloc_workspace(2, 6, 0, 512, ar.dev, ar.layout)
     monkeypatch.setenv("QX_TEST_DEP_EXTRA", "1")
     monkeypatch.setenv("QX_TIMEOUT_MS", "50")
     _run(ar, q, inv, ids, tw, ws=ws)
@@ -230,9 +238,9 @@ def test_bounded_wait_reports_timeout_and_context_survives(small, monkeypatch):
     H.assert_parity(out, H.oracle_out(H.ingest(q, inv), ids, tw, layer, 0, 512), "after timeout")
 
 
-def _full_layer_case(dev, seed, rows, n_experts=384, bias=None, a0=0, a1=2304):
+def _full_layer_case(dev, seed, rows, n_experts=384, bias=None, a0=0, a1=2304, layout="tc"):
     from qmesh_b200.arena import Arena
-    ar = Arena(dev, 1, n_experts, a0, a1)
+    ar = Arena(dev, 1, n_experts, a0, a1, layout=layout)
     ar.fill_synthetic(0, seed)
     gen = torch.Generator().manual_seed(seed)
     logits = torch.randn(rows, n_experts, generator=gen)
@@ -252,17 +260,17 @@ def _check_full(ar, ids, tw, q, inv, c0, c1):
     return H.assert_parity(out, ref, f"full layer rows={ids.shape[0]}"), len(experts)
 
 
-def test_config1_full_layer(cuda_ready):
+def test_config1_full_layer(cuda_ready, layout):
     """384 experts, rows=6, full columns, seed 1."""
-    ar, ids, tw, q, inv = _full_layer_case(cuda_ready, 1, 6)
+    ar, ids, tw, q, inv = _full_layer_case(cuda_ready, 1, 6, layout=layout)
     p, u = _check_full(ar, ids, tw, q, inv, 0, 2304)
     print("config1", p, "unique experts", u)
 
 
-def test_config3_zipf_rows48_shard(cuda_ready):
+def test_config3_zipf_rows48_shard(cuda_ready, layout):
     """BASELINE config 3 shape on one rank of the 8-way split: rows=48, Zipf bias."""
     gen = torch.Generator().manual_seed(3)
     bias = moe.zipf_bias(384, 1.1, gen)
-    ar, ids, tw, q, inv = _full_layer_case(cuda_ready, 3, 48, bias=bias, a0=2016, a1=2304)
+    ar, ids, tw, q, inv = _full_layer_case(cuda_ready, 3, 48, bias=bias, a0=2016, a1=2304, layout=layout)
     p, u = _check_full(ar, ids, tw, q, inv, 2016, 2304)
     print("config3 shard", p, "unique experts", u)

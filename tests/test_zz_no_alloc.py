@@ -38,7 +38,7 @@ def test_static_scratch_entry_matches_workspace_entry(cuda_ready):
     lib = _lib.load()
     dev = cuda_ready
     layer = H.small_layer(41, 16, inter=512)
-    ar = Arena(dev, 1, 16, 0, 512)
+    ar = Arena(dev, 1, 16, 0, 512, layout="frag")
     ar.load_layer(0, layer)
     view = ar.view(0)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
@@ -50,7 +50,7 @@ def test_static_scratch_entry_matches_workspace_entry(cuda_ready):
         out_ref = torch.empty(rows, 5120, dtype=torch.bfloat16, device=dev)
         a = _args(_lib, q, inv, ids, tw, out_static, 0, 512)
         assert lib.qx_slice_decode_static(ctypes.byref(view), ctypes.byref(a), stream) == _lib.QX_OK
-        ws = alloc_workspace(rows, 6, 0, 512, dev)
+        ws = alloc_workspace(rows, 6, 0, 512, dev, "frag")
         b = _args(_lib, q, inv, ids, tw, out_ref, 0, 512, ws)
         assert lib.qx_slice_decode(ctypes.byref(view), ctypes.byref(b), stream) == _lib.QX_OK
         torch.cuda.synchronize()
@@ -65,7 +65,7 @@ def test_static_scratch_entry_refuses_calls_beyond_its_limits(cuda_ready):
     lib = _lib.load()
     dev = cuda_ready
     layer = H.small_layer(42, 8, inter=256)
-    ar = Arena(dev, 1, 8, 0, 256)
+    ar = Arena(dev, 1, 8, 0, 256, layout="frag")
     ar.load_layer(0, layer)
     view = ar.view(0)
     rows = _lib.STATIC_MAX_ROWS + 1
