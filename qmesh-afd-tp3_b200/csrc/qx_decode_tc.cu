@@ -8,34 +8,35 @@
 // g, u = g13 * x.W, act = min(g,L)/(1+exp(-min(g,L))) * clamp(u,-L,L),
 // y_j = g2 * tw_j * act.W2, out = bf16(sum_j y_j)). The activation side of each
 // product enters the MMA as eight residual NVFP4 terms with power-of-two column
-// scales (x = sum_t 2^(E-2t) s_t q_t), which reproduces the FP32 activation to
-// about 2^-24 of its block maximum; each term's product with the weights is
-// exact in the tensor core and the eight partial sums meet in FP32 in the
-// epilogue.
+// scales: the gate/up input x as 16 unscaled e2m1 terms (x = sum_t 2^(E-2t) q_t,
+// to 2^-30 of the row maximum), the SwiGLU output as 8 block-scaled NVFP4 terms
+// (to about 2^-24 of each 16-element block's maximum). Each term's product with
+// the weights is exact in the tensor core and the partial sums meet in FP32 in
+// the epilogue.
 //
 // Kernels, chained with programmatic dependent launch:
-//   tc_prep_kernel     one CTA per activation row: reference ingest and the
-//                      row's 8-term decomposition into a per-row staging buffer;
-//                      one routing CTA: unique experts, groups of <= 24 routed
-//                      pairs of one expert, per-group operand buffers, the item
-//                      counts.
-//   tc_decode_kernel   persistent, one CTA per SM, 6 warps:
-//                      warp 0  producer: claims items from one atomic queue and
-//                              streams each item's weight tile (bulk async copy,
-//                              4 K blocks = 18,432 bytes per stage) and activation
-//                              terms into a shared-memory ring;
-//                      warp 1  MMA issuer: copies each K block's scale atoms into
-//                              TMEM and issues one M=128 x N x K=64 block-scaled
-//                              MMA per K block into a double-buffered TMEM
-//                              accumulator;
-//                      warps 2-5 epilogue: gate/up items -> SwiGLU -> the pair's
-//                              activation terms for the down projection (tile-local
-//                              exponent, fixed up by the group's last tile);
-//                              down items -> y_j = g2 tw_j act.W2 per output row.
+//   tc_route_kernel    one CTA: unique experts, groups of <= 6 routed pairs of
+//                      one expert, per-group operand buffers, the item counts.
+//   tc_decode_kernel   persistent, one CTA per SM, 7 warps:
+//                      warp 0    producer: claims items from one atomic queue and
+//                                streams each item's weight tile (bulk async copy,
+//                                4 K blocks = 18,432 bytes per stage) and activation
+//                                operand into a shared-memory ring;
+//                      warps 1, 6  MMA issuers: each copies its K blocks' scale atoms
+//                                into TMEM and issues one M=128 x N x K=64
+//                                block-scaled MMA per K block (blocks 0-1 / 2-3 of
+//                                every stage) into its own accumulator;
+//                      warps 2-5 first the x terms (every (row, 256-element chunk)
+//                                unit spread over the CTAs, written into each
+//                                routed group's operand), then the epilogue:
+//                                gate/up items -> SwiGLU -> the pair's activation
+//                                terms for the down projection (tile-local
+//                                exponent, fixed up by the group's last tile); down
+//                                items -> y_j = g2 tw_j act.W2 per output row.
 //                      Items: gate/up (group, 64-column tile: 64 gate + 64 up rows
 //                      over K = 5120) then down (group, 128-row output tile over
-//                      the slice's columns). A down item waits (bounded) for its
-//                      group's activation terms.
+//                      the slice's columns). A gate/up item waits (bounded) for its
+//                      group's x terms, a down item for its activation terms.
 //   tc_finalize_kernel out = bf16(sum over slots j in order of y_j).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -52,35 +53,64 @@ namespace tcd {
 
 constexpr int HID = QX_HIDDEN;                 // 5120
 constexpr int KB1 = HID / 64;                  // 80 K blocks in a gate/up item
-constexpr int TERMS = 8;                       // activation terms = rows per pair in B
-constexpr int GMAX = 24;                       // routed pairs per group (N <= 192)
+constexpr int TERMS = 8;                       // SwiGLU-output terms = B rows per pair (down items)
+constexpr int XTERMS = 16;                     // x terms = B rows per pair (gate/up items)
+constexpr int GMAX = 6;                        // routed pairs per group (gate/up N = 16 x 6 = 96)
 constexpr int SK = 4;                          // K blocks per stage
 constexpr int A_KB = 128 * tc::ROWB + tc::SF_ATOM;  // 4608 weight bytes per K block
 constexpr int A_STAGE = SK * A_KB;             // 18432
 constexpr int HT = HID / 128;                  // 40 output-row tiles in a down item set
 constexpr int MAXP = QX_MAX_ROWS * QX_MAX_TOPK;
 constexpr int MAXE = 4096;
-constexpr int MAXNS = 8;
+constexpr int MAXNS = 12;                      // ring slots
 constexpr int NI = MAXNS + 2;
-constexpr int NTHR = 192;
-constexpr int XT_CODES = KB1 * 256;            // per row: 8 term-rows x 32 bytes per K block
-constexpr int XT_ROW = XT_CODES + KB1 * 32;    // + 8 terms x 4 scale bytes per K block
-constexpr uint32_t TM_COLS = 512, TM_ACC = 192, TM_SFA = 384, TM_SFB = 400;
+constexpr int NTHR = 224;                      // producer, issuer 0, 4 epilogue warps, issuer 1
+// Two MMA issuer warps split every stage: K blocks 0-1 go to issuer 0, 2-3 to
+// issuer 1, each into its own accumulator (summed in the epilogue); one thread
+// cannot issue block-scaled MMAs as fast as the tensor pipe executes them.
+// TMEM columns, in four 128-column slots (accumulators use the first 96):
+//   accumulator (buffer b, issuer i) at 256 b + 128 i;
+//   in the 32-column gaps: the constant all-1.0 scale atom of every gate/up
+//   MMA (two atoms: operand rows 0..127, 128..255) at 96; the scale atoms of
+//   issuer i's K blocks of a stage, in two banks alternating by stage (weights
+//   at +0/+4, down activations at +8/+12) at 224 + 128 i + 16 bank. A stage's
+//   scale copies are issued before its MMAs into the bank the previous stage's
+//   MMAs do not read, so no MMA waits on the copy just before it.
+constexpr uint32_t TM_COLS = 512, TM_SLOT = 128, TM_ONE = 96, TM_SF = 224, TM_BANK = 16;
+constexpr int NISS = 2, KB_PER_ISS = SK / NISS;
+static_assert(GMAX * TERMS <= 128, "a down operand keeps one scale atom per K block");
+static_assert(GMAX * XTERMS <= 96 && ((GMAX * TERMS + 15) / 16) * 16 <= 96, "an accumulator fits its slot");
 constexpr int E_LO = -100, E_HI = 100;
+constexpr int XE_LO = -90, XE_HI = 100;
 
 struct Ctl {
-  uint32_t work, status, n_groups, n1, n2;
-  uint32_t pad[59];
+  uint32_t work, status, n_groups, n1, n2, n_valid, b_max;   // b_max: widest activation stage (bytes)
+  uint32_t pad[57];
 };
 static_assert(sizeof(Ctl) == 256, "ctl block is 256 bytes");
 
 struct Group {      // one group: <= GMAX routed pairs of one expert
-  int32_t expert, gsz, pair_off, n, na, kbs;
+  int32_t expert, gsz, pair_off;
+  int32_t n1, sbs1;   // gate/up activation operand: 16 x gsz rows, bytes per stage
+  int32_t n2, na2, sbs2;  // down activation operand: round16(8 x gsz) rows, its scale atoms, bytes per stage
   int64_t xb_off, ab_off;
   float g13, g2;
-  int32_t pad[4];
+  int32_t pad[2];
 };
 static_assert(sizeof(Group) == 64, "group record is 64 bytes");
+
+struct GroupS {     // the group record each CTA keeps in shared memory
+  int32_t expert, gsz, pair_off, n1, sbs1, n2, na2, sbs2, xb_off, ab_off;
+  float g13, g2;
+};
+static_assert(sizeof(GroupS) == 48, "shared group record is 48 bytes");
+
+struct PairS {      // per group position: pair index and its routing weight
+  int32_t pq;
+  float tw;
+  int32_t pad[2];
+};
+static_assert(sizeof(PairS) == 16, "shared pair record is 16 bytes");
 
 struct Params {
   const void* x;
@@ -107,15 +137,20 @@ struct Params {
   int32_t* pos_pair;  // [P] pair index at group position
   uint32_t* cnt1;     // [P] gate/up tiles finished per group
   uint32_t* ready;    // [P] group activation terms complete
-  uint32_t* xready;   // [P] group x terms gathered
+  uint32_t* xcnt;     // [P] per group: x-term chunks written (complete at 20 x gsz)
+  int32_t* pgrp;      // [P] per pair: (group << 8) | position in the group, or -1
   int32_t* emax;      // [P] per group position: common activation exponent
   int32_t* eloc;      // [P][NT] per group position and tile: tile exponent
   int32_t* xexp;      // [rows]
-  uint8_t* xt;        // [rows][XT_ROW]
-  uint8_t* xb;        // per group: [80][kbs]
-  uint8_t* ab;        // per group: [NT][kbs]
+  uint8_t* xb;        // per group: 20 stages of sbs1 bytes (x terms, K = 5120)
+  uint8_t* ab;        // per group: ceil(NT/4) stages of sbs2 bytes (SwiGLU-output terms)
   float* y;           // [P][HID]
-  int ns, slot, bst;  // ring stages, bytes per stage, activation bytes per stage
+  int x_off;          // shared-memory offset of the SwiGLU exchange (2 x gmax x 64 floats)
+  int tab_off;        // shared-memory offset of the group and pair tables
+  int ring_off, ring_bytes;  // shared-memory span of the stage rings
+  int gmax;           // pairs per group at most
+  int ns, bst, b_off; // set on the device from the largest group: ring slots, activation
+                      // bytes per slot, offset of the activation ring
   uint64_t timeout_ns;
   uint32_t dep_extra; // test hook: extra arrivals a down item waits for (0 in service)
 };
@@ -128,14 +163,32 @@ struct ItemMeta {
 
 __host__ __device__ inline size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// Upper bound of the per-group operand bytes for P pairs and nkb K blocks: a
-// group of g pairs uses nkb * (round16(8g) * 32 + 512 * atoms) bytes.
-__host__ inline size_t group_bytes_bound(int P, int nkb) {
-  return (size_t)nkb * ((size_t)P * 256 + (size_t)P * (256 + 1024));
+// Scale-atom bytes of one K block of an n-row activation operand: rows < 32 use
+// only the first 4 bytes of their line, so n <= 32 rows need n lines of 16
+// bytes (the 512-byte copy into TMEM reads past them; those lanes are rows the
+// MMA does not have); otherwise one 512-byte atom per 128 rows.
+__host__ __device__ inline int atom_bytes(int n) { return n <= 32 ? n * 16 : ((n + 127) / 128) * 512; }
+__host__ __device__ inline int kbs_of(int n) { return n * 32 + atom_bytes(n); }
+
+// Down-projection activation operand of a group (n = round16(8 gsz) rows):
+// stages of SK K blocks, each K block the n x 32-byte code tile then its scale
+// atoms (atom_bytes(n)). The gate/up operand (16 x gsz rows of x terms) is
+// codes only: K block kb at kb * n1 * 32.
+__host__ __device__ inline int sbs_of(int n) { return SK * kbs_of(n); }
+__host__ __device__ inline size_t b_codes(int n, int sbs, int kb) {
+  return (size_t)(kb / SK) * sbs + (size_t)(kb % SK) * kbs_of(n);
+}
+__host__ __device__ inline size_t b_scales(int n, int sbs, int kb, int r) {
+  return b_codes(n, sbs, kb) + (size_t)n * 32 + (size_t)(r >> 7) * tc::SF_ATOM + tc::sf_off((uint32_t)(r & 127), 0);
 }
 
+// Upper bound of a call's per-group operand bytes for P routed pairs and nkb K
+// blocks: per pair and K block at most 16 x 32 code bytes (gate/up) or
+// 256 + 256 + 1024 (down: codes, padding pair, scale atoms).
+__host__ inline size_t group_bytes_bound(int P, int nkb) { return (size_t)nkb * P * 1536; }
+
 struct WsLayout {
-  size_t ctl, groups, pexp, pos_pair, cnt1, ready, xready, emax, eloc, xexp, xt, xb, ab, y, total;
+  size_t ctl, groups, pexp, pos_pair, cnt1, ready, xcnt, pgrp, emax, eloc, xexp, xb, ab, y, total;
 };
 
 __host__ inline WsLayout ws_layout(int rows, int topk, int W) {
@@ -148,13 +201,13 @@ __host__ inline WsLayout ws_layout(int rows, int topk, int W) {
   L.pos_pair = o; o = al256(o + (size_t)P * 4);
   L.cnt1 = o;     o = al256(o + (size_t)P * 4);
   L.ready = o;    o = al256(o + (size_t)P * 4);
-  L.xready = o;   o = al256(o + (size_t)P * 4);
+  L.xcnt = o;     o = al256(o + (size_t)P * 4);
+  L.pgrp = o;     o = al256(o + (size_t)P * 4);
   L.emax = o;     o = al256(o + (size_t)P * 4);
   L.eloc = o;     o = al256(o + (size_t)P * NT * 4);
   L.xexp = o;     o = al256(o + (size_t)rows * 4);
-  L.xt = o;       o = al256(o + (size_t)rows * XT_ROW);
   L.xb = o;       o = al256(o + group_bytes_bound(P, KB1));
-  L.ab = o;       o = al256(o + group_bytes_bound(P, NT));
+  L.ab = o;       o = al256(o + group_bytes_bound(P, (NT + SK - 1) / SK * SK));
   L.y = o;        o = al256(o + (size_t)P * HID * 4);
   L.total = o;
   return L;
@@ -172,104 +225,70 @@ __device__ __forceinline__ int term_exponent(float amax) {
   return e;
 }
 
-// Eight NVFP4 terms of 16 values sharing one block (registers in, codes out):
-// writes the 8 bytes of each term's codes and its scale byte.
-__device__ __forceinline__ void terms16(float (&r)[16], int e, uint2* codes_out, uint8_t* sc_out) {
-#pragma unroll 1
-  for (int t = 0; t < TERMS; ++t) {
-    const float g = ldexpf(1.f, e - 2 * t);
-    float a = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) a = fmaxf(a, fabsf(r[i]));
-    const uint32_t sb = tc::e4m3_ru(__fdiv_rn(a, 6.f * g));
-    const float sg = tc::e4m3_val(sb) * g;
-    uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint32_t c = sg > 0.f ? tc::e2m1_rn(__fdiv_rn(r[i], sg)) : 0u;
-      r[i] -= tc::e2m1_val(c) * sg;
-      if (i < 8) w0 |= c << (4 * i);
-      else w1 |= c << (4 * (i - 8));
-    }
-    codes_out[t] = make_uint2(w0, w1);
-    sc_out[t] = (uint8_t)sb;
-  }
+// Smallest E with 6 * 2^E >= amax (0 for amax == 0), clamped to [-90, 100]:
+// the first unscaled x term then lies within the e2m1 range.
+__device__ __forceinline__ int x_exponent(float amax) {
+  if (!(amax > 0.f)) return 0;
+  int ex;
+  frexpf(amax, &ex);
+  int e = ex - 3;
+  while (e > XE_LO && ldexpf(6.f, e - 1) >= amax) --e;
+  while (e < XE_HI && ldexpf(6.f, e) < amax) ++e;
+  return e;
 }
 
-// One activation row: reference ingest, exponent, 8 terms per 16-element block,
-// staged as xt[r] = codes [kb][term][32 bytes] then scales [kb][term][4].
-__device__ void row_terms(const Params& p, int r) {
-  __shared__ float red[8];
-  const int t = threadIdx.x;
-  float inv = 1.f;
-  if (p.x_fmt == QX_X_E4M3) inv = p.x_scale[r];
-  else if (p.x_fmt == QX_X_E4M3_POST) inv = p.x_scale[0];
-  const uint8_t* xr = reinterpret_cast<const uint8_t*>(p.x) + (size_t)r * p.x_stride;
-  // 320 blocks of 16 elements; thread t owns blocks t and t + 256.
-  float v[2][16];
+constexpr int XCH = 256;                 // activation elements per x-term unit
+constexpr int NXCH = HID / XCH;          // 20 units per row
+
+// The reference's bf16 activation value of element k (gx/gx_ingest.py:151-154).
+__device__ __forceinline__ float ingest_one(const Params& p, const uint8_t* xr, int k, float inv) {
+  if (p.x_fmt == QX_X_BF16) return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(xr)[k] << 16);
+  const uint32_t f2 = e4m3x2_to_f16x2(xr[k]);
+  return __bfloat162float(__float2bfloat16_rn(__fmul_rn(f16lo_to_f32(f2), inv)));
+}
+
+// max |x| over one row, by the 128 epilogue threads (5 KB of L2 reads); red: 4 floats
+// of shared memory. Every thread gets the result.
+__device__ float row_amax128(const Params& p, const uint8_t* xr, float inv, float* red, int tid) {
   float amax = 0.f;
+  if (p.x_fmt == QX_X_BF16) {
+    for (int u = tid; u < HID / 8; u += 128) {
+      const uint4 w = *reinterpret_cast<const uint4*>(xr + (size_t)u * 16);
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int b = t + 256 * h;
+      for (int k = 0; k < 4; ++k) {
+        amax = fmaxf(amax, fabsf(__uint_as_float(ww[k] << 16)));
+        amax = fmaxf(amax, fabsf(__uint_as_float(ww[k] & 0xffff0000u)));
+      }
+    }
+  } else {
+    uint4 wv[3];                            // all loads first (320 units over 128 threads)
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[h][i] = 0.f;
-    if (b < HID / 16) {
-      if (p.x_fmt == QX_X_BF16) {
-        const uint4* src = reinterpret_cast<const uint4*>(xr + (size_t)b * 32);
+    for (int i = 0; i < 3; ++i) {
+      const int u = tid + 128 * i;
+      wv[i] = u < HID / 16 ? *reinterpret_cast<const uint4*>(xr + (size_t)u * 16) : make_uint4(0, 0, 0, 0);
+    }
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const uint4 w = src[q];
-          const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    for (int i = 0; i < 3; ++i) {
+      const uint32_t ww[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            v[h][8 * q + 2 * k] = __uint_as_float(ww[k] << 16);
-            v[h][8 * q + 2 * k + 1] = __uint_as_float(ww[k] & 0xffff0000u);
-          }
-        }
-      } else {
-        const uint4 w = *reinterpret_cast<const uint4*>(xr + (size_t)b * 16);
-        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+      for (int k = 0; k < 4; ++k) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const uint32_t f2 = e4m3x2_to_f16x2(ww[k] >> (16 * hh));
-            v[h][4 * k + 2 * hh] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(f16lo_to_f32(f2), inv)));
-            v[h][4 * k + 2 * hh + 1] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(f16hi_to_f32(f2), inv)));
-          }
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t f2 = e4m3x2_to_f16x2(ww[k] >> (16 * hh));
+          amax = fmaxf(amax, fabsf(__bfloat162float(__float2bfloat16_rn(__fmul_rn(f16lo_to_f32(f2), inv)))));
+          amax = fmaxf(amax, fabsf(__bfloat162float(__float2bfloat16_rn(__fmul_rn(f16hi_to_f32(f2), inv)))));
         }
       }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[h][i]));
     }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  if ((t & 31) == 0) red[t >> 5] = amax;
-  __syncthreads();
-  amax = red[0];
-#pragma unroll
-  for (int i = 1; i < 8; ++i) amax = fmaxf(amax, red[i]);
-  const int e = term_exponent(amax);
-  if (t == 0) p.xexp[r] = e;
-  uint8_t* xt = p.xt + (size_t)r * XT_ROW;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int b = t + 256 * h;
-    if (b < HID / 16) {
-      uint2 codes[TERMS];
-      uint8_t sc[TERMS];
-      terms16(v[h], e, codes, sc);
-      const int kb = b >> 2, j = b & 3;
-      // operand offset of (term-row t, element 16j) in a K block: (16j >> 5) * 128 + t * 16 + (16j & 31) / 2
-      uint8_t* cb = xt + (size_t)kb * 256 + (j >> 1) * 128 + (j & 1) * 8;
-#pragma unroll
-      for (int tt = 0; tt < TERMS; ++tt) *reinterpret_cast<uint2*>(cb + tt * 16) = codes[tt];
-      uint8_t* sb = xt + XT_CODES + (size_t)kb * 32 + j;
-#pragma unroll
-      for (int tt = 0; tt < TERMS; ++tt) sb[tt * 4] = sc[tt];
-    }
-  }
+  if ((tid & 31) == 0) red[tid >> 5] = amax;
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  const float m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  asm volatile("bar.sync 1, 128;" ::: "memory");   // red may be reused after this
+  return m;
 }
 
 // In-place exclusive scan of v[0..n) (n <= 512) by a 256-thread block; returns
@@ -313,17 +332,20 @@ __device__ void route(const Params& p) {
   __shared__ uint32_t bits[MAXE / 32];
   __shared__ int wpref[MAXE / 32];
   __shared__ int cntu[MAXP], offu[MAXP], ngu[MAXP], pu[MAXP], ppos[MAXP];
-  __shared__ int gu[MAXP], gk[MAXP], xsz[MAXP], asz[MAXP];
+  __shared__ int gu[MAXP], gk[MAXP], xsz[MAXP], asz[MAXP], spexp[MAXP], spos[MAXP];
   __shared__ int wt[9];
+  __shared__ int nmx;
   const int t = threadIdx.x;
   const int nw = (p.E + 31) / 32;
   const int gmax = min(GMAX, p.rows);
+  if (t == 0) nmx = 0;
   for (int i = t; i < MAXE / 32; i += blockDim.x) bits[i] = 0;
   for (int i = t; i < MAXP; i += blockDim.x) cntu[i] = 0;
   for (int i = t; i < p.P; i += blockDim.x) {
     p.cnt1[i] = 0;
     p.ready[i] = 0;
-    p.xready[i] = 0;
+    p.xcnt[i] = 0;
+    p.pgrp[i] = -1;
     p.emax[i] = INT_MIN;
   }
   uint32_t* c = reinterpret_cast<uint32_t*>(p.ctl);
@@ -340,6 +362,7 @@ __device__ void route(const Params& p) {
       atomicOr(&p.ctl->status, (uint32_t)QX_DEV_BAD_ID);
     }
     p.pexp[q] = e;
+    spexp[q] = e;
   }
   __syncthreads();
   for (int i = t; i < nw; i += blockDim.x) wpref[i] = __popc(bits[i]);
@@ -347,7 +370,7 @@ __device__ void route(const Params& p) {
   const int U = block_scan_excl(wpref, nw, wt);
   // pair rank inside its expert in (row, slot) order: count earlier pairs of the same expert
   for (int q = t; q < p.P; q += blockDim.x) {
-    const int e = p.pexp[q];
+    const int e = spexp[q];
     if (e >= 0) {
       const int u = wpref[e >> 5] + __popc(bits[e >> 5] & ((1u << (e & 31)) - 1u));
       pu[q] = u;
@@ -360,12 +383,15 @@ __device__ void route(const Params& p) {
     ngu[u] = (cntu[u] + gmax - 1) / gmax;
   }
   __syncthreads();
-  block_scan_excl(offu, U, wt);
+  const int n_valid = block_scan_excl(offu, U, wt);
   for (int u = t; u < U; u += blockDim.x) gu[u] = ngu[u];
   __syncthreads();
   const int G = block_scan_excl(gu, U, wt);   // gu[u] = first group of unique u
   for (int q = t; q < p.P; q += blockDim.x) {
-    if (p.pexp[q] >= 0) p.pos_pair[offu[pu[q]] + ppos[q]] = q;
+    if (spexp[q] >= 0) {
+      p.pos_pair[offu[pu[q]] + ppos[q]] = q;
+      spos[offu[pu[q]] + ppos[q]] = q;
+    }
   }
   // group -> (unique, index within the unique); even split of the unique's pairs
   for (int u = t; u < U; u += blockDim.x)
@@ -377,9 +403,11 @@ __device__ void route(const Params& p) {
     const int u = gk[g] >> 10, k = gk[g] & 1023, ng = ngu[u], cnt = cntu[u];
     const int lo = k * cnt / ng, hi = (k + 1) * cnt / ng;
     const int gsz = hi - lo;
-    const int n = ((8 * gsz + 15) / 16) * 16;
-    const int na = (n + 127) / 128;
-    const int kbs = n * tc::ROWB + na * tc::SF_ATOM;
+    const int n1 = XTERMS * gsz, sbs1 = SK * n1 * 32;
+    const int n2 = ((TERMS * gsz + 15) / 16) * 16;
+    const int na2 = (n2 + 127) / 128;
+    const int sbs2 = sbs_of(n2);
+    atomicMax(&nmx, sbs1 > sbs2 ? sbs1 : sbs2);
     Group& d = p.groups[g];
     int e = 0;
     {
@@ -396,15 +424,21 @@ __device__ void route(const Params& p) {
     d.expert = e;
     d.gsz = gsz;
     d.pair_off = offu[u] + lo;
-    d.n = n;
-    d.na = na;
-    d.kbs = kbs;
+    d.n1 = n1;
+    d.sbs1 = sbs1;
+    d.n2 = n2;
+    d.na2 = na2;
+    d.sbs2 = sbs2;
     d.g13 = p.g13[e];
     d.g2 = p.g2[e];
-    xsz[g] = KB1 * kbs;
-    asz[g] = p.NT * kbs;
+    xsz[g] = (KB1 / SK) * sbs1;
+    asz[g] = ((p.NT + SK - 1) / SK) * sbs2;
   }
   __syncthreads();
+  for (int g = t; g < G; g += blockDim.x) {       // pair -> (group, position in the group)
+    const Group& d = p.groups[g];
+    for (int q = 0; q < d.gsz; ++q) p.pgrp[spos[d.pair_off + q]] = (g << 8) | q;
+  }
   block_scan_excl(xsz, G, wt);
   block_scan_excl(asz, G, wt);
   for (int g = t; g < G; g += blockDim.x) {
@@ -415,41 +449,84 @@ __device__ void route(const Params& p) {
     p.ctl->n_groups = G;
     p.ctl->n1 = G * p.NT;
     p.ctl->n2 = G * HT;
+    p.ctl->n_valid = n_valid;
+    p.ctl->b_max = nmx;
   }
 }
 
-__global__ void __launch_bounds__(256) tc_prep_kernel(Params p) {
+__global__ void __launch_bounds__(256) tc_route_kernel(Params p) {
   pdl_launch_dependents();
-  if ((int)blockIdx.x < p.rows) row_terms(p, blockIdx.x);
-  else route(p);
+  route(p);
 }
 
 // ------------------------------------------------------------------ main kernel
-// Gather the x terms of group g's rows into its MMA operand buffer, and zero the
-// scale bytes of the padding pair (odd group sizes) in both operand buffers.
-__device__ void gather_group(const Params& p, const Group& gr, int tid, int nthr) {
-  uint8_t* xb = p.xb + gr.xb_off;
-  const int codes16 = KB1 * 16;              // 16-byte units of one row's codes
-  for (int i = tid; i < gr.gsz * codes16; i += nthr) {
-    const int q = i / codes16, u = i - q * codes16, kb = u >> 4, w = u & 15;
-    const int row = p.pos_pair[gr.pair_off + q] / p.topk;
-    const uint4 v = *reinterpret_cast<const uint4*>(p.xt + (size_t)row * XT_ROW + (size_t)kb * 256 + w * 16);
-    *reinterpret_cast<uint4*>(xb + (size_t)kb * gr.kbs + q * 256 + w * 16) = v;
-  }
-  for (int i = tid; i < gr.gsz * KB1 * TERMS; i += nthr) {
-    const int q = i / (KB1 * TERMS), u = i - q * (KB1 * TERMS), kb = u / TERMS, t = u - kb * TERMS;
-    const int row = p.pos_pair[gr.pair_off + q] / p.topk;
-    const uint32_t s = *reinterpret_cast<const uint32_t*>(p.xt + (size_t)row * XT_ROW + XT_CODES + kb * 32 + t * 4);
-    const int n = 8 * q + t;
-    *reinterpret_cast<uint32_t*>(xb + (size_t)kb * gr.kbs + gr.n * tc::ROWB + (n >> 7) * tc::SF_ATOM +
-                                 tc::sf_off(n & 127, 0)) = s;
-  }
-  if (gr.n > 8 * gr.gsz) {                   // padding pair: zero scales
-    uint8_t* ab = p.ab + gr.ab_off;
-    for (int i = tid; i < (KB1 + p.NT) * TERMS; i += nthr) {
-      const int kb = i / TERMS, t = i - kb * TERMS, n = 8 * gr.gsz + t;
-      uint8_t* base = kb < KB1 ? xb + (size_t)kb * gr.kbs : ab + (size_t)(kb - KB1) * gr.kbs;
-      *reinterpret_cast<uint32_t*>(base + gr.n * tc::ROWB + (n >> 7) * tc::SF_ATOM + tc::sf_off(n & 127, 0)) = 0u;
+// Startup duty of the epilogue warps: units (row r, 256-element chunk c),
+// u = blockIdx.x, blockIdx.x + gridDim.x, ... over rows x 20: the reference
+// ingest, the row's exponent E (every unit of the row computes the same), the 16
+// unscaled x terms q_t = rne(r_t / 2^(E - 2t)) of the chunk's elements (two per
+// thread), written straight into the gate/up operand of every group row r is
+// routed to (its position q there owns operand rows 16q .. 16q + 15), then one
+// count per target group on xcnt (a group's operand is complete at 20 x gsz).
+__device__ void x_terms_duty(const Params& p, const GroupS* gs, float* red, int tid) {
+  const int lane = tid & 31;
+  for (int u = blockIdx.x; u < p.rows * NXCH; u += gridDim.x) {
+    const int r = u / NXCH, c = u - r * NXCH;
+    float inv = 1.f;
+    if (p.x_fmt == QX_X_E4M3) inv = p.x_scale[r];
+    else if (p.x_fmt == QX_X_E4M3_POST) inv = p.x_scale[0];
+    const uint8_t* xr = reinterpret_cast<const uint8_t*>(p.x) + (size_t)r * p.x_stride;
+    const int e = x_exponent(row_amax128(p, xr, inv, red, tid));
+    if (c == 0 && tid == 0) p.xexp[r] = e;
+    uint8_t* tgt[QX_MAX_TOPK];
+    int tn1[QX_MAX_TOPK], tgrp[QX_MAX_TOPK];
+#pragma unroll
+    for (int j = 0; j < QX_MAX_TOPK; ++j) {
+      tgt[j] = nullptr;
+      tn1[j] = 0;
+      tgrp[j] = -1;
+      if (j < p.topk) {
+        const int pg = p.pgrp[r * p.topk + j];
+        if (pg >= 0) {
+          const GroupS& G = gs[pg >> 8];
+          tgt[j] = p.xb + G.xb_off + (size_t)(pg & 255) * 512;
+          tn1[j] = G.n1;
+          tgrp[j] = pg >> 8;
+        }
+      }
+    }
+    float v[2];
+    int kb[2], kk[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int k = c * XCH + h * 128 + tid;
+      v[h] = ingest_one(p, xr, k, inv);
+      kb[h] = k >> 6;
+      kk[h] = k & 63;
+    }
+#pragma unroll 1
+    for (int tt = 0; tt < XTERMS; ++tt) {
+      const float g = ldexpf(1.f, e - 2 * tt);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t code = tc::e2m1_of(v[h], g);    // exact: v / g is a power-of-two rescale
+        v[h] = fmaf(-tc::e2m1_val(code), g, v[h]);
+        const uint32_t w = tc::pack8(code, lane);
+        if ((lane & 7) == 0) {
+          const size_t in_kb = (size_t)(tt >> 3) * 256 + (kk[h] >> 5) * 128 + (tt & 7) * 16 + ((kk[h] & 31) >> 1);
+#pragma unroll
+          for (int j = 0; j < QX_MAX_TOPK; ++j)
+            if (tgt[j]) *reinterpret_cast<uint32_t*>(tgt[j] + (size_t)kb[h] * tn1[j] * 32 + in_kb) = w;
+        }
+      }
+    }
+    // Every thread's stores are made visible before the counts; the counts are
+    // fire-and-forget reductions (the producer acquires them).
+    __threadfence();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (tid == 0) {
+#pragma unroll
+      for (int j = 0; j < QX_MAX_TOPK; ++j)
+        if (tgrp[j] >= 0) red_add_release_gpu(&p.xcnt[tgrp[j]], 1u);
     }
   }
 }
@@ -484,14 +561,17 @@ __device__ bool wait_flag(const uint32_t* flag, uint32_t need, volatile uint32_t
   }
 }
 
-struct Smem {       // fixed part of the dynamic shared memory, after the ring
+struct Smem {       // fixed part of the dynamic shared memory, before the rings
+  alignas(16) uint8_t one_atom[512];   // e4m3 1.0 scale atom (gate/up activation scales)
   uint64_t full[MAXNS], empty[MAXNS], acc_full[2], acc_empty[2], meta_full[NI], meta_empty[NI];
   ItemMeta meta[NI];
-  uint64_t drain;
-  uint32_t tmem_base, last_flag, prod_scratch, mma_scratch;   // scratch: status words of drain waits
-  float xg[GMAX][64];   // gate values of a gate/up item, by pair and column
-  float xu[GMAX][64];   // up values
+  uint64_t drain[NISS];
+  uint64_t init_bar;
+  uint32_t tmem_base, last_flag, prod_scratch, mma_scratch[NISS];   // scratch: status words of drain waits
   float amx[GMAX][2];   // per pair, per half: |act| maximum
+  int32_t em[GMAX];     // down item: the group's common activation exponents
+  int32_t xe[GMAX];     // gate/up item: the group's rows' x exponents
+  float red4[4];        // 4-warp reduction scratch
 };
 
 // After an abort: wait (bounded) until the copies of the last ring round have
@@ -504,10 +584,11 @@ __device__ void drain_copies(const Params& p, Smem& S, uint32_t sc) {
     mbar_wait_bounded(&S.full[i % p.ns], (i / p.ns) & 1, &S.prod_scratch, 1u, grace);
 }
 
-__device__ void producer(const Params& p, uint8_t* ring, Smem& S, volatile uint32_t* status, uint64_t deadline) {
+__device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* gs, volatile uint32_t* status,
+                         uint64_t deadline) {
   const uint32_t n1 = p.ctl->n1, n2 = p.ctl->n2;
   uint32_t sc = 0, mc = 0;
-  int ready_g1 = -1, ready_g2 = -1;   // last group whose flags were seen set
+  int seen_x = -1, seen_a = -1;       // last group whose x / activation flag was seen set
   bool ok = true;
   uint32_t item = atomicAdd(&p.ctl->work, 1u);
   for (;;) {
@@ -528,8 +609,8 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, volatile uint3
       m.nkb_last = p.NT - (m.nst - 1) * SK;
     }
     const int mi = (int)(mc % NI);
-    if (mc >= (uint32_t)NI && !mbar_wait_bounded(&S.meta_empty[mi], ((mc / NI) - 1) & 1, status, QX_DEV_TIMEOUT,
-                                                 deadline)) {
+    if (mc >= (uint32_t)NI &&
+        !mbar_wait_bounded(&S.meta_empty[mi], ((mc / NI) - 1) & 1, status, QX_DEV_TIMEOUT, deadline)) {
       drain_copies(p, S, sc);
       return;
     }
@@ -540,48 +621,67 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, volatile uint3
       if (!ok) drain_copies(p, S, sc);
       return;
     }
-    const uint32_t next = atomicAdd(&p.ctl->work, 1u);   // claimed ahead; used after this item
-    const Group& gr = p.groups[m.group];
-    const int e = gr.expert, kbs = gr.kbs;
+    const uint32_t next = atomicAdd(&p.ctl->work, 1u);   // the following item, claimed ahead
+    const GroupS& gr = gs[m.group];
+    const int sbs = m.kind == 1 ? gr.sbs1 : gr.sbs2;
     const uint8_t* a_src;
     const uint8_t* b_src;
+    const uint32_t* flag;
+    uint32_t need;
+    bool check;
     if (m.kind == 1) {
-      if (ready_g1 != m.group) {
-        if (!wait_flag(&p.xready[m.group], 1u, status, deadline)) { ok = false; item = next; continue; }
-        fence_proxy_async_global();
-        ready_g1 = m.group;
-      }
-      a_src = p.w13 + ((size_t)e * p.NTA + p.tile0 + m.tile) * (size_t)KB1 * A_KB;
+      a_src = p.w13 + ((size_t)gr.expert * p.NTA + p.tile0 + m.tile) * (size_t)KB1 * A_KB;
       b_src = p.xb + gr.xb_off;
+      flag = &p.xcnt[m.group];
+      need = (uint32_t)(NXCH * gr.gsz);
+      check = seen_x != m.group;
     } else {
-      if (ready_g2 != m.group) {
-        if (!wait_flag(&p.ready[m.group], 1u + p.dep_extra, status, deadline)) { ok = false; item = next; continue; }
-        fence_proxy_async_global();
-        ready_g2 = m.group;
-      }
-      a_src = p.w2 + (((size_t)e * HT + m.tile) * p.NTA + p.tile0) * (size_t)A_KB;
+      a_src = p.w2 + (((size_t)gr.expert * HT + m.tile) * p.NTA + p.tile0) * (size_t)A_KB;
       b_src = p.ab + gr.ab_off;
+      flag = &p.ready[m.group];
+      need = 1u + p.dep_extra;
+      check = seen_a != m.group;
     }
-    for (int s = 0; s < m.nst && ok; ++s, ++sc) {
+    for (int s = 0; s < m.nst; ++s, ++sc) {
       const int slot = (int)(sc % (uint32_t)p.ns);
+      // slot (weights + activation operand) free once stage sc - ns completed
       if (sc >= (uint32_t)p.ns &&
           !mbar_wait_bounded(&S.empty[slot], ((sc / p.ns) - 1) & 1, status, QX_DEV_TIMEOUT, deadline)) {
         ok = false;
         break;
       }
       const int nkb = s < m.nst - 1 ? SK : m.nkb_last;
-      uint8_t* dst = ring + (size_t)slot * p.slot;
-      mbar_arrive_expect_tx(&S.full[slot], (uint32_t)(nkb * A_KB + nkb * kbs));
+      uint8_t* dst = ring + (size_t)slot * A_STAGE;
+      uint8_t* bdst = ring + p.b_off + (size_t)slot * p.bst;
+      mbar_arrive_expect_tx(&S.full[slot], (uint32_t)(nkb * A_KB + sbs));
       bulk_g2s(dst, a_src + (size_t)s * SK * A_KB, (uint32_t)(nkb * A_KB), &S.full[slot]);
-      bulk_g2s(dst + A_STAGE, b_src + (size_t)s * SK * kbs, (uint32_t)(nkb * kbs), &S.full[slot]);
+      if (check) {
+        // The weights of the first stage are already in flight; the activation
+        // operand waits for its producer. On a timeout the copy is still issued
+        // (of stale bytes) so the stage completes and nothing is left pending.
+        if (!wait_flag(flag, need, status, deadline)) ok = false;
+        fence_proxy_async_global();
+        check = false;
+        if (ok) {
+          if (m.kind == 1) seen_x = m.group; else seen_a = m.group;
+        }
+      }
+      bulk_g2s(bdst, b_src + (size_t)s * sbs, (uint32_t)sbs, &S.full[slot]);
+      if (!ok) {
+        ++sc;
+        break;
+      }
     }
     item = next;
   }
 }
 
-__device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, uint32_t tbase, volatile uint32_t* status,
-                           uint64_t deadline) {
+// Issuer `iss` of every stage's K blocks [2 iss, 2 iss + 2) into accumulator
+// (buffer, iss). Both issuers consume every stage and item in the same order.
+__device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS* gs, uint32_t tbase, int iss,
+                           volatile uint32_t* status, uint64_t deadline) {
   uint32_t sc = 0, mc = 0, ic = 0;
+  const uint32_t sfbase = tbase + TM_SF + (uint32_t)iss * TM_SLOT;
   for (;;) {
     const int mi = (int)(mc % NI);
     if (!mbar_wait_bounded(&S.meta_full[mi], (mc / NI) & 1, status, QX_DEV_TIMEOUT, deadline)) break;
@@ -589,113 +689,138 @@ __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, uint32_t tba
     mbar_arrive(&S.meta_empty[mi]);
     ++mc;
     if (m.kind == 0) break;
-    const Group& gr = p.groups[m.group];
-    const uint32_t n = (uint32_t)gr.n, na = (uint32_t)gr.na, kbs = (uint32_t)gr.kbs;
+    const GroupS& gr = gs[m.group];
+    const bool up = m.kind == 1;                       // gate/up: unscaled x terms, constant B scales
+    const uint32_t n = (uint32_t)(up ? gr.n1 : gr.n2);   // down operands have one scale atom (n <= 96)
+    const uint32_t cstride = up ? n * tc::ROWB : (uint32_t)kbs_of((int)n);   // K block to K block in a stage
     const uint32_t idesc = tc::idesc_nvf4(n);
     const int buf = (int)(ic & 1u);
     if (ic >= 2 && !mbar_wait_bounded(&S.acc_empty[buf], ((ic / 2) - 1) & 1, status, QX_DEV_TIMEOUT, deadline))
       break;
     tc::fence_after_sync();
-    const uint32_t tacc = tbase + (uint32_t)buf * TM_ACC;
-    bool ok = true;
+    const uint32_t tacc = tbase + (uint32_t)buf * 2u * TM_SLOT + (uint32_t)iss * TM_SLOT;
+    bool ok = true, first = true;
     for (int s = 0; s < m.nst; ++s, ++sc) {
       const int slot = (int)(sc % (uint32_t)p.ns);
+      // The stage's operands were written by the bulk copies (async proxy) the
+      // barrier tracks; the MMAs read them through the same proxy, so the wait
+      // alone orders them (no thread-sync fence, as for any TMA-fed stage).
       if (!mbar_wait_bounded(&S.full[slot], (sc / p.ns) & 1, status, QX_DEV_TIMEOUT, deadline)) {
         ok = false;
         break;
       }
-      tc::fence_after_sync();
       const int nkb = s < m.nst - 1 ? SK : m.nkb_last;
-      const uint32_t a0 = smem_u32(ring + (size_t)slot * p.slot);
-      const uint32_t b0 = a0 + A_STAGE;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const uint32_t sa = a0 + kb * A_KB, sbb = b0 + kb * kbs;
-        const uint32_t tsfa = tbase + TM_SFA + 4 * kb, tsfb = tbase + TM_SFB + 4 * na * kb;
-        tc::cp_sf_atom(tsfa, sa + 128 * tc::ROWB);
-        for (uint32_t at = 0; at < na; ++at) tc::cp_sf_atom(tsfb + 4 * at, sbb + n * tc::ROWB + at * tc::SF_ATOM);
-        tc::mma_nvf4(tacc, tc::sdesc(sa, tc::LBO, tc::SBO), tc::sdesc(sbb, tc::LBO, tc::SBO), idesc, tsfa, tsfb,
-                     (s > 0 || kb > 0) ? 1u : 0u);
+      const int k0 = iss * KB_PER_ISS, k1 = min(nkb, k0 + KB_PER_ISS);
+      const uint32_t a0 = smem_u32(ring + (size_t)slot * A_STAGE);
+      const uint32_t b0 = smem_u32(ring + p.b_off + (size_t)slot * p.bst);
+      const uint32_t bank = sfbase + (sc & 1u) * TM_BANK;
+      for (int kb = k0; kb < k1; ++kb) {   // this issuer's scale atoms of the stage first ...
+        const uint32_t j = (uint32_t)(kb - k0);
+        tc::cp_sf_atom(bank + 4 * j, a0 + kb * A_KB + 128 * tc::ROWB);
+        if (!up) tc::cp_sf_atom(bank + 8 + 4 * j, b0 + kb * cstride + n * tc::ROWB);
       }
-      tc::commit(&S.empty[slot]);
+      for (int kb = k0; kb < k1; ++kb) {   // ... then its MMAs
+        const uint32_t j = (uint32_t)(kb - k0);
+        const uint32_t sa = a0 + kb * A_KB, sbb = b0 + kb * cstride;
+        tc::mma_nvf4(tacc, tc::sdesc(sa, tc::LBO, tc::SBO), tc::sdesc(sbb, tc::LBO, tc::SBO), idesc, bank + 4 * j,
+                     up ? tbase + TM_ONE : bank + 8 + 4 * j, first ? 0u : 1u);
+        first = false;
+      }
+      tc::commit(&S.empty[slot]);          // arrives when this issuer's work on the stage is done
     }
     if (!ok) break;
     tc::commit(&S.acc_full[buf]);
     ++ic;
   }
-  // Let every tensor-core operation issued so far complete before TMEM is freed.
-  tc::commit(&S.drain);
-  S.mma_scratch = 0;
-  mbar_wait_bounded(&S.drain, 0, &S.mma_scratch, 1u, globaltimer_ns() + p.timeout_ns);
+  // Let every tensor-core operation this thread issued complete before TMEM is freed.
+  tc::commit(&S.drain[iss]);
+  S.mma_scratch[iss] = 0;
+  mbar_wait_bounded(&S.drain[iss], 0, &S.mma_scratch[iss], 1u, globaltimer_ns() + p.timeout_ns);
 }
+
+// Whether issuer 1 wrote its accumulator for an item (it owns K blocks 2-3 of each stage).
+__device__ __forceinline__ bool second_acc(const ItemMeta& m) { return m.nst > 1 || m.nkb_last > KB_PER_ISS; }
 
 // Scale of term t for exponent e: 2^(e - 2t), exact.
 __device__ __forceinline__ float term_scale(int e, int t) { return ldexpf(1.f, e - 2 * t); }
 
-__device__ void epilogue(const Params& p, Smem& S, uint32_t tbase, volatile uint32_t* status, uint64_t deadline) {
+__device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, const PairS* ps, uint32_t tbase,
+                         volatile uint32_t* status, uint64_t deadline) {
+  float* xu = xg + p.gmax * 64;                  // gate and up values of a gate/up item, [pair][column]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int et = threadIdx.x - 64;                 // 0..127
   const int quarter = warp & 3;                    // TMEM lane quarter this warp may read
   const int m = quarter * 32 + lane;               // accumulator row
   const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
 
-  // Gather duty: groups g = blockIdx.x, blockIdx.x + gridDim.x, ...
-  const int G = (int)p.ctl->n_groups;
-  for (int g = blockIdx.x; g < G; g += gridDim.x) {
-    const Group gr = p.groups[g];
-    gather_group(p, gr, et, 128);
-    __threadfence();
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (et == 0) st_release_gpu(&p.xready[g], 1u);
-  }
+  x_terms_duty(p, gs, S.red4, et);
 
   uint32_t mc = 0, ic = 0;
   for (;;) {
     const int mi = (int)(mc % NI);
-    bool got = mbar_wait_bounded(&S.meta_full[mi], (mc / NI) & 1, status, QX_DEV_TIMEOUT, deadline);
+    const bool got = mbar_wait_bounded(&S.meta_full[mi], (mc / NI) & 1, status, QX_DEV_TIMEOUT, deadline);
     const ItemMeta mt = S.meta[mi];
     if (!bar_and(1, 128, got)) break;
     if (et == 0) mbar_arrive(&S.meta_empty[mi]);
     ++mc;
     if (mt.kind == 0) break;
-    const Group gr = p.groups[mt.group];
+    const GroupS& gr = gs[mt.group];
+    bool ok = true;
+    if (mt.kind == 1 && et < gr.gsz) {
+      // The rows' x exponents (written with the x terms), fetched while the MMAs run.
+      ok = wait_flag(&p.xcnt[mt.group], (uint32_t)(NXCH * gr.gsz), status, deadline);
+      S.xe[et] = __ldcg(&p.xexp[ps[gr.pair_off + et].pq / p.topk]);
+    }
+    if (mt.kind == 2 && et < gr.gsz) {
+      // The group's common exponents, fetched while the MMAs run.
+      ok = wait_flag(&p.ready[mt.group], 1u + p.dep_extra, status, deadline);
+      S.em[et] = __ldcg(&p.emax[gr.pair_off + et]);
+    }
     const int buf = (int)(ic & 1u);
-    const bool ok = mbar_wait_bounded(&S.acc_full[buf], (ic / 2) & 1, status, QX_DEV_TIMEOUT, deadline);
+    ok = mbar_wait_bounded(&S.acc_full[buf], (ic / 2) & 1, status, QX_DEV_TIMEOUT, deadline) && ok;
     if (!bar_and(1, 128, ok)) break;
     tc::fence_after_sync();
-    const uint32_t tacc = tbase + lanes + (uint32_t)buf * TM_ACC;
+    const uint32_t tacc = tbase + lanes + (uint32_t)buf * 2u * TM_SLOT;   // issuer 1's at + TM_SLOT
+    const bool two = second_acc(mt);
     if (mt.kind == 1) {
       // ---- gate/up tile: rows 0..63 gate, 64..127 up of columns [64 tile, 64 tile + 64)
       const bool up = m >= 64;
       const int c = m & 63;
       for (int q = 0; q < gr.gsz; ++q) {
-        float v[8];
-        tc::ld8(tacc + 8 * q, v);
-        const int row = p.pos_pair[gr.pair_off + q] / p.topk;
-        const int xe = p.xexp[row];
+        float v[16];
+        tc::ld16(tacc + XTERMS * q, v);
+        if (two) {
+          float v1[16];
+          tc::ld16(tacc + TM_SLOT + XTERMS * q, v1);
+#pragma unroll
+          for (int t = 0; t < XTERMS; ++t) v[t] += v1[t];
+        }
+        const int xe = S.xe[q];
         float s = 0.f;
 #pragma unroll
-        for (int t = 0; t < TERMS; ++t) s += v[t] * term_scale(xe, t);
+        for (int t = XTERMS - 1; t >= 0; --t) s += v[t] * term_scale(xe, t);   // smallest terms first
         s *= gr.g13;
-        if (up) S.xu[q][c] = s; else S.xg[q][c] = s;
+        if (up) xu[q * 64 + c] = s; else xg[q * 64 + c] = s;
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.acc_empty[buf]);
       asm volatile("bar.sync 1, 128;" ::: "memory");
       const int col0 = mt.tile * 64;
-      uint8_t* ab = p.ab + gr.ab_off + (size_t)mt.tile * gr.kbs;
+      uint8_t* ab = p.ab + gr.ab_off;
+      const size_t cb = b_codes(gr.n2, gr.sbs2, mt.tile);
       if (!up) {
         // SwiGLU per pair, |act| maxima per half tile
         const int half = warp & 1;   // quarters 0, 1 <-> columns 0..31, 32..63
         for (int q = 0; q < gr.gsz; ++q) {
-          float g = S.xg[q][c], u = S.xu[q][c];
+          float g = xg[q * 64 + c], u = xu[q * 64 + c];
           if (p.has_limit) {
             g = fminf(g, p.limit);
             u = fminf(fmaxf(u, -p.limit), p.limit);
           }
           float a = (g / (1.f + expf(-g))) * u;
           if (col0 + c >= p.W) a = 0.f;
-          S.xg[q][c] = a;
+          xg[q * 64 + c] = a;
           float mx = fabsf(a);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -704,31 +829,24 @@ __device__ void epilogue(const Params& p, Smem& S, uint32_t tbase, volatile uint
         asm volatile("bar.sync 2, 64;" ::: "memory");
         for (int q = 0; q < gr.gsz; ++q) {
           const int el = term_exponent(fmaxf(S.amx[q][0], S.amx[q][1]));
-          float r = S.xg[q][c];
+          float r = xg[q * 64 + c];
+#pragma unroll 1
           for (int t = 0; t < TERMS; ++t) {
-            const float gs = ldexpf(1.f, el - 2 * t);
-            float a16 = fabsf(r);
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) a16 = fmaxf(a16, __shfl_xor_sync(0xffffffffu, a16, o));
-            const uint32_t sb = tc::e4m3_ru(__fdiv_rn(a16, 6.f * gs));
-            const float sg = tc::e4m3_val(sb) * gs;
-            const uint32_t code = sg > 0.f ? tc::e2m1_rn(__fdiv_rn(r, sg)) : 0u;
-            r -= tc::e2m1_val(code) * sg;
-            uint32_t w = code << (4 * (lane & 7));
-            w |= __shfl_xor_sync(0xffffffffu, w, 1);
-            w |= __shfl_xor_sync(0xffffffffu, w, 2);
-            w |= __shfl_xor_sync(0xffffffffu, w, 4);
+            uint32_t sb;
+            const uint32_t code = tc::term_step(r, ldexpf(1.f, el - 2 * t), &sb);
+            const uint32_t w = tc::pack8(code, lane);
             const int n = 8 * q + t;
             if ((lane & 7) == 0)
-              *reinterpret_cast<uint32_t*>(ab + q * 256 + half * 128 + t * 16 + (lane >> 3) * 4) = w;
-            if ((lane & 15) == 0)
-              ab[gr.n * tc::ROWB + (n >> 7) * tc::SF_ATOM + tc::sf_off(n & 127, (uint32_t)(c >> 4))] = (uint8_t)sb;
+              *reinterpret_cast<uint32_t*>(ab + cb + q * 256 + half * 128 + t * 16 + (lane >> 3) * 4) = w;
+            if ((lane & 15) == 0) ab[b_scales(gr.n2, gr.sbs2, mt.tile, n) + (c >> 4)] = (uint8_t)sb;
           }
           if (c == 0) {
             p.eloc[(size_t)(gr.pair_off + q) * p.NT + mt.tile] = el;
             atomicMax(&p.emax[gr.pair_off + q], el);
           }
         }
+        if (gr.n2 > TERMS * gr.gsz && c < TERMS)       // padding pair of the down operand: zero scales
+          *reinterpret_cast<uint32_t*>(ab + b_scales(gr.n2, gr.sbs2, mt.tile, TERMS * gr.gsz + c)) = 0u;
         __threadfence();
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -746,8 +864,7 @@ __device__ void epilogue(const Params& p, Smem& S, uint32_t tbase, volatile uint
           if (sh <= 0) continue;
           for (int t = 0; t < TERMS; ++t) {
             const int n = 8 * q + t;
-            uint32_t* w = reinterpret_cast<uint32_t*>(ab0 + (size_t)tile * gr.kbs + gr.n * tc::ROWB +
-                                                      (n >> 7) * tc::SF_ATOM + tc::sf_off(n & 127, 0));
+            uint32_t* w = reinterpret_cast<uint32_t*>(ab0 + b_scales(gr.n2, gr.sbs2, tile, n));
             const uint32_t b = __ldcg(w);
             uint32_t nb = 0;
 #pragma unroll
@@ -762,17 +879,21 @@ __device__ void epilogue(const Params& p, Smem& S, uint32_t tbase, volatile uint
     } else {
       // ---- down tile: output rows [128 tile, 128 tile + 128)
       const int h = mt.tile * 128 + m;
-      (void)ld_acquire_gpu(&p.ready[mt.group]);
       for (int q = 0; q < gr.gsz; ++q) {
         float v[8];
         tc::ld8(tacc + 8 * q, v);
-        const int pq = p.pos_pair[gr.pair_off + q];
-        const int ea = __ldcg(&p.emax[gr.pair_off + q]);
+        if (two) {
+          float v1[8];
+          tc::ld8(tacc + TM_SLOT + 8 * q, v1);
+#pragma unroll
+          for (int t = 0; t < TERMS; ++t) v[t] += v1[t];
+        }
+        const PairS pr = ps[gr.pair_off + q];
+        const int ea = S.em[q];
         float s = 0.f;
 #pragma unroll
         for (int t = 0; t < TERMS; ++t) s += v[t] * term_scale(ea, t);
-        const float f = gr.g2 * p.tw[pq];
-        p.y[(size_t)pq * HID + h] = s * f;
+        p.y[(size_t)pr.pq * HID + h] = s * (gr.g2 * pr.tw);
       }
       tc::fence_before_sync();
       __syncwarp();
@@ -782,47 +903,104 @@ __device__ void epilogue(const Params& p, Smem& S, uint32_t tbase, volatile uint
   }
 }
 
+__device__ void load_tables(const Params& p, GroupS* gs, PairS* ps) {
+  const int G = (int)p.ctl->n_groups, nv = (int)p.ctl->n_valid;
+  for (int i = threadIdx.x; i < G; i += NTHR) {
+    const Group g = p.groups[i];
+    GroupS s;
+    s.expert = g.expert;
+    s.gsz = g.gsz;
+    s.pair_off = g.pair_off;
+    s.n1 = g.n1;
+    s.sbs1 = g.sbs1;
+    s.n2 = g.n2;
+    s.na2 = g.na2;
+    s.sbs2 = g.sbs2;
+    s.xb_off = (int32_t)g.xb_off;
+    s.ab_off = (int32_t)g.ab_off;
+    s.g13 = g.g13;
+    s.g2 = g.g2;
+    gs[i] = s;
+  }
+  for (int i = threadIdx.x; i < nv; i += NTHR) {
+    const int pq = p.pos_pair[i];
+    PairS s;
+    s.pq = pq;
+    s.tw = p.tw[pq];
+    s.pad[0] = s.pad[1] = 0;
+    ps[i] = s;
+  }
+}
+
 __global__ void __launch_bounds__(NTHR, 1) tc_decode_kernel(Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* ring = smem;
-  Smem& S = *reinterpret_cast<Smem*>(smem + (size_t)p.ns * p.slot);
+  Smem& S = *reinterpret_cast<Smem*>(smem);
+  uint8_t* ring = smem + p.ring_off;
+  float* xg = reinterpret_cast<float*>(smem + p.x_off);
+  GroupS* gs = reinterpret_cast<GroupS*>(smem + p.tab_off);
+  PairS* ps = reinterpret_cast<PairS*>(smem + p.tab_off + (size_t)p.P * sizeof(GroupS));
   const int warp = threadIdx.x >> 5;
   volatile uint32_t* status = &p.ctl->status;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < p.ns; ++s) {
+    for (int s = 0; s < MAXNS; ++s) {
       mbar_init(&S.full[s], 1);
-      mbar_init(&S.empty[s], 1);
+      mbar_init(&S.empty[s], NISS);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&S.acc_full[b], 1);
+      mbar_init(&S.acc_full[b], NISS);
       mbar_init(&S.acc_empty[b], 4);
     }
     for (int i = 0; i < NI; ++i) {
       mbar_init(&S.meta_full[i], 1);
-      mbar_init(&S.meta_empty[i], 2);
+      mbar_init(&S.meta_empty[i], NISS + 1);
     }
-    mbar_init(&S.drain, 1);
+    for (int i = 0; i < NISS; ++i) mbar_init(&S.drain[i], 1);
+    mbar_init(&S.init_bar, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
     tc::tmem_alloc(&S.tmem_base, TM_COLS);
     tc::tmem_relinquish();
   }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (threadIdx.x == 32) {
+    // The gate/up MMAs' activation scales: a constant atom of e4m3 1.0, copied
+    // into TMEM before any issuer starts (bounded wait for the copy).
+    for (int i = 0; i < 512 / 4; ++i) reinterpret_cast<uint32_t*>(S.one_atom)[i] = 0x38383838u;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc::cp_sf_atom(S.tmem_base + TM_ONE, smem_u32(S.one_atom));       // operand rows 0..127
+    tc::cp_sf_atom(S.tmem_base + TM_ONE + 4, smem_u32(S.one_atom));   // rows 128..255
+    tc::commit(&S.init_bar);
+    S.mma_scratch[0] = 0;
+    mbar_wait_bounded(&S.init_bar, 0, &S.mma_scratch[0], 1u, globaltimer_ns() + p.timeout_ns);
+  }
   pdl_wait();                // routing tables and row terms are complete
   pdl_launch_dependents();
+  {
+    // Ring geometry from the largest group of this call: every slot holds one
+    // weight stage and one activation stage of the widest operand.
+    const int bmx = (int)p.ctl->b_max;
+    p.bst = bmx < 16 ? 16 : bmx;
+    int ns = (p.ring_bytes - 512) / (A_STAGE + p.bst);   // 512: slack for the last scale-atom read
+    p.ns = ns > MAXNS ? MAXNS : ns;
+    p.b_off = p.ns * A_STAGE;
+  }
+  load_tables(p, gs, ps);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = S.tmem_base;
   const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
   if (warp == 0) {
-    if ((threadIdx.x & 31) == 0) producer(p, ring, S, status, deadline);
-  } else if (warp == 1) {
-    if ((threadIdx.x & 31) == 0) mma_issuer(p, ring, S, tbase, status, deadline);
+    if ((threadIdx.x & 31) == 0) producer(p, ring, S, gs, status, deadline);
+  } else if (warp == 1 || warp == 6) {
+    if ((threadIdx.x & 31) == 0) mma_issuer(p, ring, S, gs, tbase, warp == 1 ? 0 : 1, status, deadline);
   } else {
-    epilogue(p, S, tbase, status, deadline);
+    epilogue(p, S, xg, gs, ps, tbase, status, deadline);
   }
-  // The producer drained its copies and the issuer its tensor-core work (both
+  // The producer drained its copies and the issuers their tensor-core work (all
   // bounded) before returning; the epilogue's last TMEM reads are complete.
   tc::fence_before_sync();
   __syncthreads();
@@ -982,28 +1160,35 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream)
   p.pos_pair = reinterpret_cast<int32_t*>(ws + L.pos_pair);
   p.cnt1 = reinterpret_cast<uint32_t*>(ws + L.cnt1);
   p.ready = reinterpret_cast<uint32_t*>(ws + L.ready);
-  p.xready = reinterpret_cast<uint32_t*>(ws + L.xready);
+  p.xcnt = reinterpret_cast<uint32_t*>(ws + L.xcnt);
+  p.pgrp = reinterpret_cast<int32_t*>(ws + L.pgrp);
   p.emax = reinterpret_cast<int32_t*>(ws + L.emax);
   p.eloc = reinterpret_cast<int32_t*>(ws + L.eloc);
   p.xexp = reinterpret_cast<int32_t*>(ws + L.xexp);
-  p.xt = ws + L.xt;
   p.xb = ws + L.xb;
   p.ab = ws + L.ab;
   p.y = reinterpret_cast<float*>(ws + L.y);
-  const int nmax = ((8 * (a->rows < GMAX ? a->rows : GMAX) + 15) / 16) * 16;
-  p.bst = SK * (nmax * (int)qx::tc::ROWB + ((nmax + 127) / 128) * (int)qx::tc::SF_ATOM);
-  p.slot = A_STAGE + p.bst;
-  const size_t fixed = sizeof(Smem) + 128;
-  int ns = (int)((SMEM_LIMIT - fixed) / (size_t)p.slot);
-  if (ns > MAXNS) ns = MAXNS;
-  if (ns < 2) return QX_ERR_SHAPE;
-  p.ns = ns;
+  p.gmax = a->rows < GMAX ? a->rows : GMAX;
+  const int nmax = ((8 * p.gmax + 15) / 16) * 16;
+  {
+    const int s1 = SK * XTERMS * p.gmax * 32, s2 = sbs_of(nmax);
+    p.bst = s1 > s2 ? s1 : s2;   // the widest possible group, for the shape check
+  }
+  // shared memory: [Smem][exchange][tables][rings: ns weight stages | ns activation stages]
+  const size_t tables = (size_t)p.P * (sizeof(GroupS) + sizeof(PairS));
+  const size_t xchg = (size_t)2 * p.gmax * 64 * sizeof(float);
+  p.x_off = (int)((sizeof(Smem) + 15) & ~size_t(15));
+  p.tab_off = (int)(((size_t)p.x_off + xchg + 15) & ~size_t(15));
+  p.ring_off = (int)(((size_t)p.tab_off + tables + 127) & ~size_t(127));
+  p.ring_bytes = (int)(SMEM_LIMIT - (size_t)p.ring_off);
+  if (p.ring_bytes - 512 < 2 * (A_STAGE + p.bst)) return QX_ERR_SHAPE;   // two slots of the widest group
+  p.ns = p.b_off = 0;
   p.timeout_ns = timeout_ns();
   p.dep_extra = dep_extra();
-  const size_t smem_bytes = (size_t)ns * p.slot + sizeof(Smem);
+  const size_t smem_bytes = SMEM_LIMIT;
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  tc_prep_kernel<<<a->rows + 1, 256, 0, st>>>(p);
+  tc_route_kernel<<<1, 256, 0, st>>>(p);
   if (cudaGetLastError() != cudaSuccess) return QX_ERR_LAUNCH;
 
   cudaLaunchAttribute attr[1];

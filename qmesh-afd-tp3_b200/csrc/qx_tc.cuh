@@ -137,25 +137,69 @@ __device__ __forceinline__ void ld8(uint32_t taddr, float (&v)[8]) {
 }
 
 // ---- NVFP4 encoders for operands built on the device ---------------------------
-// e2m1 code (nibble) of y, round to nearest even, saturating at +-6.
-__device__ __forceinline__ uint32_t e2m1_rn(float y) {
-  uint32_t r;
-  asm("{ .reg .b8 b; cvt.rn.satfinite.e2m1x2.f32 b, %1, %2; cvt.u32.u8 %0, b; }" : "=r"(r) : "f"(0.f), "f"(y));
-  return r & 15u;
-}
 // Value of an e2m1 code (exact).
 __device__ __forceinline__ float e2m1_val(uint32_t code) { return f16lo_to_f32(e2m1x2_to_f16x2(code & 15u)); }
 // Value of an e4m3 byte (exact).
 __device__ __forceinline__ float e4m3_val(uint32_t b) { return f16lo_to_f32(e4m3x2_to_f16x2(b & 0xFFu)); }
-// Smallest e4m3 byte whose value is >= v (v >= 0); 0 for v == 0; 448 caps.
-__device__ __forceinline__ uint32_t e4m3_ru(float v) {
-  if (!(v > 0.f)) return 0u;
+
+// Smallest e4m3 byte b with val(b) * g6 >= a (a >= 0; g6 = 6 * 2^k, inv_g6 its
+// reciprocal); 0 for a == 0; 448 caps. The hardware round-to-nearest of the
+// quotient estimate is at most one e4m3 step below the answer, and
+// val(b) * g6 is exact, so one exact comparison settles it.
+__device__ __forceinline__ uint32_t e4m3_ceil(float a, float g6, float inv_g6) {
+  if (!(a > 0.f)) return 0u;
   uint32_t two;
-  asm("{ .reg .b16 h; cvt.rn.satfinite.e4m3x2.f32 h, %1, %2; cvt.u32.u16 %0, h; }" : "=r"(two) : "f"(0.f), "f"(v));
+  asm("{ .reg .b16 h; cvt.rn.satfinite.e4m3x2.f32 h, %1, %2; cvt.u32.u16 %0, h; }"
+      : "=r"(two)
+      : "f"(0.f), "f"(a * inv_g6));
   uint32_t b = two & 0xFFu;
-  if (e4m3_val(b) < v && b < 0x7Eu) ++b;
+  if (b < 0x7Eu && e4m3_val(b) * g6 < a) ++b;
   return b;
 }
+
+// e2m1 code of the exact quotient r / sg (|r| <= 6 sg), round to nearest with
+// ties to the even code, by comparing |r| with the seven midpoints times sg
+// (each product is exact). 0 when sg == 0.
+__device__ __forceinline__ uint32_t e2m1_of(float r, float sg) {
+  if (!(sg > 0.f)) return 0u;
+  const float a = fabsf(r);
+  uint32_t i = (a > 0.25f * sg) ? 1u : 0u;
+  i += (a >= 0.75f * sg) ? 1u : 0u;
+  i += (a > 1.25f * sg) ? 1u : 0u;
+  i += (a >= 1.75f * sg) ? 1u : 0u;
+  i += (a > 2.5f * sg) ? 1u : 0u;
+  i += (a >= 3.5f * sg) ? 1u : 0u;
+  i += (a > 5.f * sg) ? 1u : 0u;
+  return i | ((__float_as_uint(r) >> 28) & 8u);
+}
+
+// One residual NVFP4 term of a 16-element block spread one element per lane over
+// 16 consecutive lanes (lane groups 0-15 and 16-31 are independent blocks): the
+// block scale byte (returned in *sb), the lane's e2m1 code (returned), and the
+// residual update r -= code * scale * g, exact. g = 2^k.
+__device__ __forceinline__ uint32_t term_step(float& r, float g, uint32_t* sb) {
+  float a = fabsf(r);
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  const float g6 = 6.f * g;
+  const uint32_t b = e4m3_ceil(a, g6, __frcp_rn(g6));
+  const float sg = e4m3_val(b) * g;
+  const uint32_t code = e2m1_of(r, sg);
+  r = fmaf(-e2m1_val(code), sg, r);
+  *sb = b;
+  return code;
+}
+
+// Packs the codes of 8 consecutive lanes into one word (lane 8j + i -> nibble i);
+// the word is valid in every lane of the group.
+__device__ __forceinline__ uint32_t pack8(uint32_t code, int lane) {
+  uint32_t w = code << (4 * (lane & 7));
+  w |= __shfl_xor_sync(0xffffffffu, w, 1);
+  w |= __shfl_xor_sync(0xffffffffu, w, 2);
+  w |= __shfl_xor_sync(0xffffffffu, w, 4);
+  return w;
+}
+
 // e4m3 byte divided by 2^sh (sh >= 0), rounded to nearest even on the e4m3 grid.
 __device__ __forceinline__ uint32_t e4m3_shift(uint32_t b, int sh) {
   b &= 0xFFu;

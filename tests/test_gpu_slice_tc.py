@@ -1,7 +1,8 @@
-"""Tensor-core slice internals on the GPU: the activation-term operands the
-prologue builds must equal the CPU model of the decomposition bit for bit
+"""Tensor-core slice internals on the GPU: the x-term operands the kernel
+builds must equal the CPU model of the decomposition bit for bit
 (tests/nvfp4_terms.py), so that a parity failure of the full slice can be told
-apart from a failure of the operand encoding."""
+apart from a failure of the operand encoding; and slices whose width is not a
+multiple of the 64-column tile."""
 
 import pytest
 import torch
@@ -13,7 +14,6 @@ from oracle import nvfp4 as oq
 pytestmark = pytest.mark.gpu
 
 HID = 5120
-XT_ROW = 80 * 256 + 80 * 32
 
 
 def _al(v):
@@ -25,24 +25,25 @@ def ws_offsets(rows, topk, width):
     p, nt = rows * topk, (width + 63) // 64
     o, off = 0, {}
     for name, size in [("ctl", 256), ("groups", p * 64), ("pexp", p * 4), ("pos_pair", p * 4), ("cnt1", p * 4),
-                       ("ready", p * 4), ("xready", p * 4), ("emax", p * 4), ("eloc", p * nt * 4),
-                       ("xexp", rows * 4), ("xt", rows * XT_ROW)]:
+                       ("ready", p * 4), ("xcnt", p * 4), ("pgrp", p * 4), ("emax", p * 4),
+                       ("eloc", p * nt * 4), ("xexp", rows * 4), ("xb", 0)]:
         off[name] = o
         o = _al(o + size)
     return off
 
 
-def _xt_unpack(xt_row):
-    """One staged row -> (codes [8, 5120] nibbles, scales [8, 320])."""
-    codes = xt_row[:80 * 256].reshape(80, 2, 8, 16)                  # kb, half, term, byte
-    nib = torch.stack([codes & 15, codes >> 4], dim=-1)              # kb, half, term, byte, nibble
-    nib = nib.permute(2, 0, 1, 3, 4).reshape(8, HID)
-    sc = xt_row[80 * 256:].reshape(80, 8, 4).permute(1, 0, 2).reshape(8, 320)
-    return nib, sc
+def _kb_unpack(block):
+    """One pair's 512-byte tile of one K block ([row group 2][K half 2][row 8][16 bytes],
+    rows = its 16 terms) -> nibbles [16 terms, 64]."""
+    codes = block.reshape(2, 2, 8, 16)
+    nib = torch.stack([codes & 15, codes >> 4], dim=-1)              # rg, half, row, byte, nibble
+    return nib.permute(0, 2, 1, 3, 4).reshape(16, 64)
 
 
 @pytest.mark.parametrize("rows,seed", [(1, 3), (6, 4)])
-def test_row_terms_match_cpu_model(cuda_ready, rows, seed):
+def test_x_terms_match_cpu_model(cuda_ready, rows, seed):
+    """Every group's gate/up operand holds, at each pair position, the 16 x terms
+    of that pair's row, bit for bit."""
     from qmesh_b200.arena import Arena
     from qmesh_b200.expert_slice import alloc_workspace, expert_slice
     dev = cuda_ready
@@ -56,18 +57,29 @@ def test_row_terms_match_cpu_model(cuda_ready, rows, seed):
     torch.cuda.synchronize()
     off = ws_offsets(rows, 6, 256)
     w = ws.cpu()
+    n_groups = int(w[4 * 2:4 * 3].view(torch.int32))                 # ctl.n_groups
     xexp = w[off["xexp"]:off["xexp"] + rows * 4].view(torch.int32)
+    pos_pair = w[off["pos_pair"]:off["pos_pair"] + rows * 6 * 4].view(torch.int32)
     x = H.ingest(q, inv)
-    codes, scales, e = NT.decompose(x)
+    codes, e = NT.decompose_x(x)
     assert torch.equal(xexp, e), (xexp, e)
-    for r in range(rows):
-        nib, sc = _xt_unpack(w[off["xt"] + r * XT_ROW:off["xt"] + (r + 1) * XT_ROW])
-        assert torch.equal(sc, scales[r]), f"row {r}: scale bytes differ at {(sc != scales[r]).nonzero()[:5].tolist()}"
-        assert torch.equal(nib, codes[r]), f"row {r}: codes differ at {(nib != codes[r]).nonzero()[:5].tolist()}"
-    # the terms reproduce the activation to ~2^-24 of each block's maximum
-    rec = NT.reconstruct(codes, scales, e)
-    blk = x.abs().view(rows, -1, 16).amax(dim=2).repeat_interleave(16, dim=1).double()
-    assert ((rec - x.double()).abs() <= blk * 2.0 ** -22 + 1e-30).all()
+    seen = 0
+    for g in range(n_groups):
+        rec = w[off["groups"] + 64 * g:off["groups"] + 64 * (g + 1)]
+        gsz, pair_off, n1 = (int(v) for v in rec[4:16].view(torch.int32))
+        xb_off = int(rec[32:40].view(torch.int64))
+        for qq in range(gsz):
+            row = int(pos_pair[pair_off + qq]) // 6
+            for kb in range(80):
+                base = off["xb"] + xb_off + kb * n1 * 32 + qq * 512
+                got = _kb_unpack(w[base:base + 512])
+                want = codes[row, :, kb * 64:(kb + 1) * 64]
+                assert torch.equal(got, want), f"group {g} pair {qq} row {row} K block {kb}"
+            seen += 1
+    assert seen == int((ids >= 0).sum())
+    rec_x = NT.reconstruct_x(codes, e)
+    amax = x.abs().amax(dim=1, keepdim=True).double()
+    assert ((rec_x - x.double()).abs() <= amax * 2.0 ** -30).all()
 
 
 def test_width_not_multiple_of_64(cuda_ready):
