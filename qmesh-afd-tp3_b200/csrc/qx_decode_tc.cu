@@ -15,28 +15,35 @@
 // the epilogue.
 //
 // Kernels, chained with programmatic dependent launch:
-//   tc_route_kernel    one CTA: unique experts, groups of <= 6 routed pairs of
-//                      one expert, per-group operand buffers, the item counts.
-//   tc_decode_kernel   persistent, one CTA per SM, 7 warps:
-//                      warp 0    producer: claims items from one atomic queue and
-//                                streams each item's weight tile (bulk async copy,
-//                                4 K blocks = 18,432 bytes per stage) and activation
-//                                operand into a shared-memory ring;
+//   tc_prep_kernel     one CTA per (row, 256-element chunk): the reference
+//                      ingest, the row's exponent, the chunk's 16 x terms in the
+//                      row-major operand layout (one 2,048-byte block per row and
+//                      stage); CTA 0 also resets the call's counters and checks the
+//                      ids. Independent of the routing, so it runs while the
+//                      decode kernel starts.
+//   tc_decode_kernel   persistent, one CTA per SM, 7 warps. Every CTA first
+//                      builds the routing tables itself from the ids (unique
+//                      experts, groups of <= 6 routed pairs of one expert, the
+//                      item counts; deterministic, so all CTAs agree), then
+//                      warp 0    producer: streams each item's weight tile (bulk async
+//                                copy, 4 K blocks = 18,432 bytes per stage) and
+//                                activation operand into a shared-memory ring; the
+//                                first item is the CTA's index and its weights are
+//                                in flight before the prep kernel is waited for,
+//                                later items come from one atomic queue;
 //                      warps 1, 6  MMA issuers: each copies its K blocks' scale atoms
 //                                into TMEM and issues one M=128 x N x K=64
 //                                block-scaled MMA per K block (blocks 0-1 / 2-3 of
 //                                every stage) into its own accumulator;
-//                      warps 2-5 first the x terms (every (row, 256-element chunk)
-//                                unit spread over the CTAs, written into each
-//                                routed group's operand), then the epilogue:
-//                                gate/up items -> SwiGLU -> the pair's activation
-//                                terms for the down projection (tile-local
-//                                exponent, fixed up by the group's last tile); down
-//                                items -> y_j = g2 tw_j act.W2 per output row.
+//                      warps 2-5 epilogue: gate/up items -> SwiGLU -> the pair's
+//                                activation terms for the down projection
+//                                (tile-local exponent, fixed up by the group's last
+//                                tile); down items -> y_j = g2 tw_j act.W2 per
+//                                output row.
 //                      Items: gate/up (group, 64-column tile: 64 gate + 64 up rows
 //                      over K = 5120) then down (group, 128-row output tile over
-//                      the slice's columns). A gate/up item waits (bounded) for its
-//                      group's x terms, a down item for its activation terms.
+//                      the slice's columns). A down item waits (bounded) for its
+//                      group's activation terms.
 //   tc_finalize_kernel out = bf16(sum over slots j in order of y_j).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -84,26 +91,23 @@ constexpr int E_LO = -100, E_HI = 100;
 constexpr int XE_LO = -90, XE_HI = 100;
 
 struct Ctl {
-  uint32_t work, status, n_groups, n1, n2, n_valid, b_max;   // b_max: widest activation stage (bytes)
-  uint32_t pad[57];
+  uint32_t work, status;   // dynamic item queue (after the first grid-size items), QX_DEV_* bits
+  uint32_t pad[62];
 };
 static_assert(sizeof(Ctl) == 256, "ctl block is 256 bytes");
 
-struct Group {      // one group: <= GMAX routed pairs of one expert
+struct GroupS {     // one group (<= GMAX routed pairs of one expert), kept in shared memory
   int32_t expert, gsz, pair_off;
-  int32_t n1, sbs1;   // gate/up activation operand: 16 x gsz rows, bytes per stage
+  int32_t n1, sbs1;       // gate/up activation operand: 16 x gsz rows, bytes per stage
   int32_t n2, na2, sbs2;  // down activation operand: round16(8 x gsz) rows, its scale atoms, bytes per stage
-  int64_t xb_off, ab_off;
-  float g13, g2;
-  int32_t pad[2];
-};
-static_assert(sizeof(Group) == 64, "group record is 64 bytes");
-
-struct GroupS {     // the group record each CTA keeps in shared memory
-  int32_t expert, gsz, pair_off, n1, sbs1, n2, na2, sbs2, xb_off, ab_off;
+  int32_t ab_off, pad;    // offset of the group's down operand in the activation-term buffer
   float g13, g2;
 };
 static_assert(sizeof(GroupS) == 48, "shared group record is 48 bytes");
+
+struct RouteHdr {   // call-wide results of the routing, in shared memory
+  int32_t n_groups, n1, n2, b_max;   // groups, gate/up items, down items, widest activation stage
+};
 
 struct PairS {      // per group position: pair index and its routing weight
   int32_t pq;
@@ -132,17 +136,12 @@ struct Params {
   __nv_bfloat16* out;
   int64_t out_stride;
   Ctl* ctl;
-  Group* groups;
-  int32_t* pexp;      // [P] expert of pair q or -1
-  int32_t* pos_pair;  // [P] pair index at group position
   uint32_t* cnt1;     // [P] gate/up tiles finished per group
   uint32_t* ready;    // [P] group activation terms complete
-  uint32_t* xcnt;     // [P] per group: x-term chunks written (complete at 20 x gsz)
-  int32_t* pgrp;      // [P] per pair: (group << 8) | position in the group, or -1
   int32_t* emax;      // [P] per group position: common activation exponent
   int32_t* eloc;      // [P][NT] per group position and tile: tile exponent
   int32_t* xexp;      // [rows]
-  uint8_t* xb;        // per group: 20 stages of sbs1 bytes (x terms, K = 5120)
+  uint8_t* xt;        // [rows][20 stages][2048 bytes]: x terms, row-major
   uint8_t* ab;        // per group: ceil(NT/4) stages of sbs2 bytes (SwiGLU-output terms)
   float* y;           // [P][HID]
   int x_off;          // shared-memory offset of the SwiGLU exchange (2 x gmax x 64 floats)
@@ -172,8 +171,17 @@ __host__ __device__ inline int kbs_of(int n) { return n * 32 + atom_bytes(n); }
 
 // Down-projection activation operand of a group (n = round16(8 gsz) rows):
 // stages of SK K blocks, each K block the n x 32-byte code tile then its scale
-// atoms (atom_bytes(n)). The gate/up operand (16 x gsz rows of x terms) is
-// codes only: K block kb at kb * n1 * 32.
+// atoms (atom_bytes(n)).
+//
+// Gate/up operand (16 x gsz rows of x terms, codes only): each row's terms are
+// kept row-major, one 2,048-byte block per row and stage laid out
+// [row group 2][K block 4][K half 2][8 terms][16 bytes]. A group's stage is its
+// pairs' blocks side by side (pair q at 2,048 q), so operand row group j sits at
+// 1,024 j: one MMA per K block with leading offset 128 and stride 1,024 reads
+// all of the group's rows, and the stage is gsz copies of 2,048 bytes.
+constexpr int XT_STAGE = 2048;                 // x-term bytes per row and stage
+constexpr uint32_t XT_SBO = 1024;              // gate/up operand: row group to row group
+constexpr uint32_t XT_KB = 256;                // gate/up operand: K block to K block
 __host__ __device__ inline int sbs_of(int n) { return SK * kbs_of(n); }
 __host__ __device__ inline size_t b_codes(int n, int sbs, int kb) {
   return (size_t)(kb / SK) * sbs + (size_t)(kb % SK) * kbs_of(n);
@@ -188,7 +196,7 @@ __host__ __device__ inline size_t b_scales(int n, int sbs, int kb, int r) {
 __host__ inline size_t group_bytes_bound(int P, int nkb) { return (size_t)nkb * P * 1536; }
 
 struct WsLayout {
-  size_t ctl, groups, pexp, pos_pair, cnt1, ready, xcnt, pgrp, emax, eloc, xexp, xb, ab, y, total;
+  size_t ctl, cnt1, ready, emax, eloc, xexp, xt, ab, y, total;
 };
 
 __host__ inline WsLayout ws_layout(int rows, int topk, int W) {
@@ -196,17 +204,12 @@ __host__ inline WsLayout ws_layout(int rows, int topk, int W) {
   const int P = rows * topk, NT = (W + 63) / 64;
   size_t o = 0;
   L.ctl = o;      o = al256(o + sizeof(Ctl));
-  L.groups = o;   o = al256(o + (size_t)P * sizeof(Group));
-  L.pexp = o;     o = al256(o + (size_t)P * 4);
-  L.pos_pair = o; o = al256(o + (size_t)P * 4);
   L.cnt1 = o;     o = al256(o + (size_t)P * 4);
   L.ready = o;    o = al256(o + (size_t)P * 4);
-  L.xcnt = o;     o = al256(o + (size_t)P * 4);
-  L.pgrp = o;     o = al256(o + (size_t)P * 4);
   L.emax = o;     o = al256(o + (size_t)P * 4);
   L.eloc = o;     o = al256(o + (size_t)P * NT * 4);
   L.xexp = o;     o = al256(o + (size_t)rows * 4);
-  L.xb = o;       o = al256(o + group_bytes_bound(P, KB1));
+  L.xt = o;       o = al256(o + (size_t)rows * (KB1 / SK) * XT_STAGE);
   L.ab = o;       o = al256(o + group_bytes_bound(P, (NT + SK - 1) / SK * SK));
   L.y = o;        o = al256(o + (size_t)P * HID * 4);
   L.total = o;
@@ -291,242 +294,190 @@ __device__ float row_amax128(const Params& p, const uint8_t* xr, float inv, floa
   return m;
 }
 
-// In-place exclusive scan of v[0..n) (n <= 512) by a 256-thread block; returns
-// the total. All threads must call it.
-__device__ int block_scan_excl(int* v, int n, int* warp_tot) {
-  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
-  const int i0 = 2 * t, i1 = 2 * t + 1;
-  const int a = i0 < n ? v[i0] : 0;
-  const int b = i1 < n ? v[i1] : 0;
-  int s = a + b, inc = s;
+// Exclusive prefix sum over v[0..n) by one warp, in place; returns the total.
+__device__ int warp_scan_excl(int* v, int n, int lane) {
+  int carry = 0;
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int i = i0 + lane;
+    const int x = i < n ? v[i] : 0;
+    int inc = x;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int u = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += u;
-  }
-  if (lane == 31) warp_tot[w] = inc;
-  __syncthreads();
-  if (w == 0) {
-    int x = lane < 8 ? warp_tot[lane] : 0, xi = x;
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
-      const int u = __shfl_up_sync(0xffffffffu, xi, o);
-      if (lane >= o) xi += u;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += u;
     }
-    if (lane < 8) warp_tot[lane] = xi - x;
-    if (lane == 7) warp_tot[8] = xi;
+    if (i < n) v[i] = carry + inc - x;
+    carry += __shfl_sync(0xffffffffu, inc, 31);
   }
-  __syncthreads();
-  const int base = warp_tot[w] + inc - s;
-  if (i0 < n) v[i0] = base;
-  if (i1 < n) v[i1] = base + a;
-  const int total = warp_tot[8];
-  __syncthreads();
-  return total;
+  __syncwarp();
+  return carry;
 }
 
-// Unique experts, groups of <= gmax pairs of one expert, per-group operand
-// geometry and offsets, item counts. Every pair's result is independent of the
-// other pairs sharing its MMA, so the order of pairs inside an expert is free.
-__device__ void route(const Params& p) {
-  __shared__ uint32_t bits[MAXE / 32];
-  __shared__ int wpref[MAXE / 32];
-  __shared__ int cntu[MAXP], offu[MAXP], ngu[MAXP], pu[MAXP], ppos[MAXP];
-  __shared__ int gu[MAXP], gk[MAXP], xsz[MAXP], asz[MAXP], spexp[MAXP], spos[MAXP];
-  __shared__ int wt[9];
-  __shared__ int nmx;
-  const int t = threadIdx.x;
+// Scratch of route_local, in words (placed in the not yet used stage rings).
+constexpr int RT_WORDS = 8 * MAXP + 2 * (MAXE / 32);
+
+// The routing tables of a call, built by one warp of every CTA from the ids
+// (the reference groups the routed pairs by expert the same way for its
+// grouped launch, gx/gx_decode_swz.py:148-179): unique experts in ascending
+// order; an expert's pairs in (row, slot) order, split evenly into groups of at
+// most gmax; per group its operand geometry and the offset of its down operand;
+// gs[g], ps[group position], hdr. Every CTA computes the same tables.
+__device__ void route_local(const Params& p, int* scr, GroupS* gs, PairS* ps, RouteHdr* hdr) {
+  const int lane = threadIdx.x & 31;
+  int* ex = scr;                    // [P] expert of pair q or -1
+  int* pu = ex + MAXP;              // [P] unique index of pair q
+  int* pr = pu + MAXP;              // [P] rank of pair q among its expert's pairs
+  int* cnt = pr + MAXP;             // [U] pairs per unique expert
+  int* off = cnt + MAXP;            // [U] first group position of the unique
+  int* gf = off + MAXP;             // [U] first group of the unique
+  int* uex = gf + MAXP;             // [U] expert id of the unique
+  int* asz = uex + MAXP;            // [G] down-operand bytes of the group
+  uint32_t* bits = reinterpret_cast<uint32_t*>(asz + MAXP);
+  int* wpre = reinterpret_cast<int*>(bits + MAXE / 32);
   const int nw = (p.E + 31) / 32;
   const int gmax = min(GMAX, p.rows);
-  if (t == 0) nmx = 0;
-  for (int i = t; i < MAXE / 32; i += blockDim.x) bits[i] = 0;
-  for (int i = t; i < MAXP; i += blockDim.x) cntu[i] = 0;
-  for (int i = t; i < p.P; i += blockDim.x) {
-    p.cnt1[i] = 0;
-    p.ready[i] = 0;
-    p.xcnt[i] = 0;
-    p.pgrp[i] = -1;
-    p.emax[i] = INT_MIN;
-  }
-  uint32_t* c = reinterpret_cast<uint32_t*>(p.ctl);
-  for (int i = t; i < (int)(sizeof(Ctl) / 4); i += blockDim.x) c[i] = 0;
-  __syncthreads();
-  for (int q = t; q < p.P; q += blockDim.x) {
+  for (int i = lane; i < nw; i += 32) bits[i] = 0;
+  __syncwarp();
+  for (int q = lane; q < p.P; q += 32) {
     const long long id = p.ids64 ? reinterpret_cast<const long long*>(p.ids)[q]
                                  : (long long)reinterpret_cast<const int*>(p.ids)[q];
-    int e = -1;
-    if (id >= 0 && id < p.E) {
-      e = (int)id;
-      atomicOr(&bits[e >> 5], 1u << (e & 31));
-    } else if (id != -1) {
-      atomicOr(&p.ctl->status, (uint32_t)QX_DEV_BAD_ID);
-    }
-    p.pexp[q] = e;
-    spexp[q] = e;
+    const int e = (id >= 0 && id < p.E) ? (int)id : -1;   // other ids: skipped (flagged by the prep kernel)
+    ex[q] = e;
+    if (e >= 0) atomicOr(&bits[e >> 5], 1u << (e & 31));
   }
-  __syncthreads();
-  for (int i = t; i < nw; i += blockDim.x) wpref[i] = __popc(bits[i]);
-  __syncthreads();
-  const int U = block_scan_excl(wpref, nw, wt);
-  // pair rank inside its expert in (row, slot) order: count earlier pairs of the same expert
-  for (int q = t; q < p.P; q += blockDim.x) {
-    const int e = spexp[q];
+  __syncwarp();
+  for (int i = lane; i < nw; i += 32) wpre[i] = __popc(bits[i]);
+  __syncwarp();
+  const int U = warp_scan_excl(wpre, nw, lane);
+  for (int u = lane; u < U; u += 32) cnt[u] = 0;
+  __syncwarp();
+  // rank of each pair among the earlier pairs of its expert, 32 pairs at a time
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int q0 = 0; q0 < p.P; q0 += 32) {
+    const int q = q0 + lane;
+    const int e = q < p.P ? ex[q] : -1;
+    const uint32_t same = __match_any_sync(0xffffffffu, e);
+    int u = -1;
     if (e >= 0) {
-      const int u = wpref[e >> 5] + __popc(bits[e >> 5] & ((1u << (e & 31)) - 1u));
+      u = wpre[e >> 5] + __popc(bits[e >> 5] & ((1u << (e & 31)) - 1u));
       pu[q] = u;
-      ppos[q] = atomicAdd(&cntu[u], 1);   // order inside an expert does not affect any pair's result
+      pr[q] = cnt[u] + __popc(same & lt);
+    }
+    __syncwarp();
+    if (e >= 0 && (same & lt) == 0) {   // the expert's first lane in this chunk
+      cnt[u] += __popc(same);
+      uex[u] = e;
+    }
+    __syncwarp();
+  }
+  for (int u = lane; u < U; u += 32) {
+    off[u] = cnt[u];
+    gf[u] = (cnt[u] + gmax - 1) / gmax;
+  }
+  __syncwarp();
+  warp_scan_excl(off, U, lane);
+  const int G = warp_scan_excl(gf, U, lane);
+  for (int q = lane; q < p.P; q += 32) {
+    if (ex[q] >= 0) {
+      PairS s;
+      s.pq = q;
+      s.tw = p.tw[q];
+      s.pad[0] = s.pad[1] = 0;
+      ps[off[pu[q]] + pr[q]] = s;
     }
   }
-  __syncthreads();
-  for (int u = t; u < U; u += blockDim.x) {
-    offu[u] = cntu[u];
-    ngu[u] = (cntu[u] + gmax - 1) / gmax;
-  }
-  __syncthreads();
-  const int n_valid = block_scan_excl(offu, U, wt);
-  for (int u = t; u < U; u += blockDim.x) gu[u] = ngu[u];
-  __syncthreads();
-  const int G = block_scan_excl(gu, U, wt);   // gu[u] = first group of unique u
-  for (int q = t; q < p.P; q += blockDim.x) {
-    if (spexp[q] >= 0) {
-      p.pos_pair[offu[pu[q]] + ppos[q]] = q;
-      spos[offu[pu[q]] + ppos[q]] = q;
+  int bmx = 0;
+  for (int u = lane; u < U; u += 32) {
+    const int c = cnt[u], ng = (c + gmax - 1) / gmax, e = uex[u];
+    const float g13 = p.g13[e], g2 = p.g2[e];
+    for (int k = 0; k < ng; ++k) {
+      const int lo = k * c / ng, hi = (k + 1) * c / ng, gsz = hi - lo;
+      GroupS d;
+      d.expert = e;
+      d.gsz = gsz;
+      d.pair_off = off[u] + lo;
+      d.n1 = XTERMS * gsz;
+      d.sbs1 = gsz * XT_STAGE;
+      d.n2 = ((TERMS * gsz + 15) / 16) * 16;
+      d.na2 = (d.n2 + 127) / 128;
+      d.sbs2 = sbs_of(d.n2);
+      d.ab_off = 0;
+      d.pad = 0;
+      d.g13 = g13;
+      d.g2 = g2;
+      gs[gf[u] + k] = d;
+      asz[gf[u] + k] = ((p.NT + SK - 1) / SK) * d.sbs2;
+      bmx = max(bmx, max(d.sbs1, d.sbs2));
     }
   }
-  // group -> (unique, index within the unique); even split of the unique's pairs
-  for (int u = t; u < U; u += blockDim.x)
-    for (int k = 0; k < ngu[u]; ++k) {
-      gk[gu[u] + k] = u * 1024 + k;
-    }
-  __syncthreads();
-  for (int g = t; g < G; g += blockDim.x) {
-    const int u = gk[g] >> 10, k = gk[g] & 1023, ng = ngu[u], cnt = cntu[u];
-    const int lo = k * cnt / ng, hi = (k + 1) * cnt / ng;
-    const int gsz = hi - lo;
-    const int n1 = XTERMS * gsz, sbs1 = SK * n1 * 32;
-    const int n2 = ((TERMS * gsz + 15) / 16) * 16;
-    const int na2 = (n2 + 127) / 128;
-    const int sbs2 = sbs_of(n2);
-    atomicMax(&nmx, sbs1 > sbs2 ? sbs1 : sbs2);
-    Group& d = p.groups[g];
-    int e = 0;
-    {
-      // expert id of unique u: the u-th set bit
-      int lo2 = 0, hi2 = nw;
-      while (hi2 - lo2 > 1) {
-        const int mid = (lo2 + hi2) >> 1;
-        if (wpref[mid] <= u) lo2 = mid; else hi2 = mid;
-      }
-      uint32_t w = bits[lo2];
-      for (int s = u - wpref[lo2]; s > 0; --s) w &= w - 1;
-      e = lo2 * 32 + __ffs(w) - 1;
-    }
-    d.expert = e;
-    d.gsz = gsz;
-    d.pair_off = offu[u] + lo;
-    d.n1 = n1;
-    d.sbs1 = sbs1;
-    d.n2 = n2;
-    d.na2 = na2;
-    d.sbs2 = sbs2;
-    d.g13 = p.g13[e];
-    d.g2 = p.g2[e];
-    xsz[g] = (KB1 / SK) * sbs1;
-    asz[g] = ((p.NT + SK - 1) / SK) * sbs2;
-  }
-  __syncthreads();
-  for (int g = t; g < G; g += blockDim.x) {       // pair -> (group, position in the group)
-    const Group& d = p.groups[g];
-    for (int q = 0; q < d.gsz; ++q) p.pgrp[spos[d.pair_off + q]] = (g << 8) | q;
-  }
-  block_scan_excl(xsz, G, wt);
-  block_scan_excl(asz, G, wt);
-  for (int g = t; g < G; g += blockDim.x) {
-    p.groups[g].xb_off = xsz[g];
-    p.groups[g].ab_off = asz[g];
-  }
-  if (t == 0) {
-    p.ctl->n_groups = G;
-    p.ctl->n1 = G * p.NT;
-    p.ctl->n2 = G * HT;
-    p.ctl->n_valid = n_valid;
-    p.ctl->b_max = nmx;
-  }
-}
-
-__global__ void __launch_bounds__(256) tc_route_kernel(Params p) {
-  pdl_launch_dependents();
-  route(p);
-}
-
-// ------------------------------------------------------------------ main kernel
-// Startup duty of the epilogue warps: units (row r, 256-element chunk c),
-// u = blockIdx.x, blockIdx.x + gridDim.x, ... over rows x 20: the reference
-// ingest, the row's exponent E (every unit of the row computes the same), the 16
-// unscaled x terms q_t = rne(r_t / 2^(E - 2t)) of the chunk's elements (two per
-// thread), written straight into the gate/up operand of every group row r is
-// routed to (its position q there owns operand rows 16q .. 16q + 15), then one
-// count per target group on xcnt (a group's operand is complete at 20 x gsz).
-__device__ void x_terms_duty(const Params& p, const GroupS* gs, float* red, int tid) {
-  const int lane = tid & 31;
-  for (int u = blockIdx.x; u < p.rows * NXCH; u += gridDim.x) {
-    const int r = u / NXCH, c = u - r * NXCH;
-    float inv = 1.f;
-    if (p.x_fmt == QX_X_E4M3) inv = p.x_scale[r];
-    else if (p.x_fmt == QX_X_E4M3_POST) inv = p.x_scale[0];
-    const uint8_t* xr = reinterpret_cast<const uint8_t*>(p.x) + (size_t)r * p.x_stride;
-    const int e = x_exponent(row_amax128(p, xr, inv, red, tid));
-    if (c == 0 && tid == 0) p.xexp[r] = e;
-    uint8_t* tgt[QX_MAX_TOPK];
-    int tn1[QX_MAX_TOPK], tgrp[QX_MAX_TOPK];
+  __syncwarp();
+  warp_scan_excl(asz, G, lane);
+  for (int g = lane; g < G; g += 32) gs[g].ab_off = asz[g];
 #pragma unroll
-    for (int j = 0; j < QX_MAX_TOPK; ++j) {
-      tgt[j] = nullptr;
-      tn1[j] = 0;
-      tgrp[j] = -1;
-      if (j < p.topk) {
-        const int pg = p.pgrp[r * p.topk + j];
-        if (pg >= 0) {
-          const GroupS& G = gs[pg >> 8];
-          tgt[j] = p.xb + G.xb_off + (size_t)(pg & 255) * 512;
-          tn1[j] = G.n1;
-          tgrp[j] = pg >> 8;
-        }
-      }
+  for (int o = 16; o > 0; o >>= 1) bmx = max(bmx, __shfl_xor_sync(0xffffffffu, bmx, o));
+  if (lane == 0) {
+    hdr->n_groups = G;
+    hdr->n1 = G * p.NT;
+    hdr->n2 = G * HT;
+    hdr->b_max = bmx;
+  }
+  __syncwarp();
+}
+
+// One CTA per unit (row r, 256-element chunk c = stage c of the gate/up
+// operand): the reference ingest of row r, its exponent E (every unit of the
+// row computes the same), and the chunk's 16 unscaled x terms
+// q_t = rne(r_t / 2^(E - 2t)) (two elements per thread) into the row's stage
+// block. CTA 0 also resets the call's counters and records bad ids.
+__global__ void __launch_bounds__(128) tc_prep_kernel(Params p) {
+  __shared__ float red[4];
+  pdl_launch_dependents();
+  const int tid = threadIdx.x, lane = tid & 31;
+  if (blockIdx.x == 0) {
+    bool bad = false;
+    for (int q = tid; q < p.P; q += 128) {
+      const long long id = p.ids64 ? reinterpret_cast<const long long*>(p.ids)[q]
+                                   : (long long)reinterpret_cast<const int*>(p.ids)[q];
+      bad |= !(id == -1 || (id >= 0 && id < p.E));
+      p.cnt1[q] = 0;
+      p.ready[q] = 0;
+      p.emax[q] = INT_MIN;
     }
-    float v[2];
-    int kb[2], kk[2];
+    bad = __syncthreads_or(bad);
+    uint32_t* c = reinterpret_cast<uint32_t*>(p.ctl);
+    for (int i = tid; i < (int)(sizeof(Ctl) / 4); i += 128) c[i] = 0;
+    __syncthreads();
+    if (tid == 0 && bad) p.ctl->status = (uint32_t)QX_DEV_BAD_ID;
+  }
+  const int r = blockIdx.x / NXCH, c = blockIdx.x - r * NXCH;
+  float inv = 1.f;
+  if (p.x_fmt == QX_X_E4M3) inv = p.x_scale[r];
+  else if (p.x_fmt == QX_X_E4M3_POST) inv = p.x_scale[0];
+  const uint8_t* xr = reinterpret_cast<const uint8_t*>(p.x) + (size_t)r * p.x_stride;
+  float v[2];
+  int kk[2], kbl[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int k = c * XCH + h * 128 + tid;
+    v[h] = ingest_one(p, xr, k, inv);
+    kbl[h] = (k >> 6) & (SK - 1);
+    kk[h] = k & 63;
+  }
+  const int e = x_exponent(row_amax128(p, xr, inv, red, tid));
+  if (c == 0 && tid == 0) p.xexp[r] = e;
+  uint8_t* blk = p.xt + ((size_t)r * NXCH + c) * XT_STAGE;
+#pragma unroll 1
+  for (int tt = 0; tt < XTERMS; ++tt) {
+    const float g = ldexpf(1.f, e - 2 * tt);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int k = c * XCH + h * 128 + tid;
-      v[h] = ingest_one(p, xr, k, inv);
-      kb[h] = k >> 6;
-      kk[h] = k & 63;
-    }
-#pragma unroll 1
-    for (int tt = 0; tt < XTERMS; ++tt) {
-      const float g = ldexpf(1.f, e - 2 * tt);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t code = tc::e2m1_of(v[h], g);    // exact: v / g is a power-of-two rescale
-        v[h] = fmaf(-tc::e2m1_val(code), g, v[h]);
-        const uint32_t w = tc::pack8(code, lane);
-        if ((lane & 7) == 0) {
-          const size_t in_kb = (size_t)(tt >> 3) * 256 + (kk[h] >> 5) * 128 + (tt & 7) * 16 + ((kk[h] & 31) >> 1);
-#pragma unroll
-          for (int j = 0; j < QX_MAX_TOPK; ++j)
-            if (tgt[j]) *reinterpret_cast<uint32_t*>(tgt[j] + (size_t)kb[h] * tn1[j] * 32 + in_kb) = w;
-        }
+      const uint32_t code = tc::e2m1_of(v[h], g);    // exact: v / g is a power-of-two rescale
+      v[h] = fmaf(-tc::e2m1_val(code), g, v[h]);
+      const uint32_t w = tc::pack8(code, lane);
+      if ((lane & 7) == 0) {
+        const int o = (tt >> 3) * 1024 + kbl[h] * 256 + (kk[h] >> 5) * 128 + (tt & 7) * 16 + ((kk[h] & 31) >> 1);
+        *reinterpret_cast<uint32_t*>(blk + o) = w;
       }
-    }
-    // Every thread's stores are made visible before the counts; the counts are
-    // fire-and-forget reductions (the producer acquires them).
-    __threadfence();
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (tid == 0) {
-#pragma unroll
-      for (int j = 0; j < QX_MAX_TOPK; ++j)
-        if (tgrp[j] >= 0) red_add_release_gpu(&p.xcnt[tgrp[j]], 1u);
     }
   }
 }
@@ -571,7 +522,7 @@ struct Smem {       // fixed part of the dynamic shared memory, before the rings
   float amx[GMAX][2];   // per pair, per half: |act| maximum
   int32_t em[GMAX];     // down item: the group's common activation exponents
   int32_t xe[GMAX];     // gate/up item: the group's rows' x exponents
-  float red4[4];        // 4-warp reduction scratch
+  RouteHdr hdr;
 };
 
 // After an abort: wait (bounded) until the copies of the last ring round have
@@ -584,13 +535,13 @@ __device__ void drain_copies(const Params& p, Smem& S, uint32_t sc) {
     mbar_wait_bounded(&S.full[i % p.ns], (i / p.ns) & 1, &S.prod_scratch, 1u, grace);
 }
 
-__device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* gs, volatile uint32_t* status,
-                         uint64_t deadline) {
-  const uint32_t n1 = p.ctl->n1, n2 = p.ctl->n2;
+__device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* gs, const PairS* ps,
+                         const RouteHdr& hdr, volatile uint32_t* status, uint64_t deadline) {
+  const uint32_t n1 = (uint32_t)hdr.n1, n2 = (uint32_t)hdr.n2;
   uint32_t sc = 0, mc = 0;
-  int seen_x = -1, seen_a = -1;       // last group whose x / activation flag was seen set
-  bool ok = true;
-  uint32_t item = atomicAdd(&p.ctl->work, 1u);
+  int seen_a = -1;                    // last group whose activation flag was seen set
+  bool ok = true, prep_seen = false;  // prep_seen: the prep kernel's results are visible
+  uint32_t item = blockIdx.x;         // the first item is static, the rest come from the queue
   for (;;) {
     ItemMeta m = {};
     if (!ok || item >= n1 + n2) {
@@ -618,55 +569,64 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
     mbar_arrive(&S.meta_full[mi]);
     ++mc;
     if (m.kind == 0) {
+      if (!prep_seen) pdl_wait();
       if (!ok) drain_copies(p, S, sc);
       return;
     }
-    const uint32_t next = atomicAdd(&p.ctl->work, 1u);   // the following item, claimed ahead
     const GroupS& gr = gs[m.group];
     const int sbs = m.kind == 1 ? gr.sbs1 : gr.sbs2;
-    const uint8_t* a_src;
-    const uint8_t* b_src;
-    const uint32_t* flag;
-    uint32_t need;
-    bool check;
-    if (m.kind == 1) {
-      a_src = p.w13 + ((size_t)gr.expert * p.NTA + p.tile0 + m.tile) * (size_t)KB1 * A_KB;
-      b_src = p.xb + gr.xb_off;
-      flag = &p.xcnt[m.group];
-      need = (uint32_t)(NXCH * gr.gsz);
-      check = seen_x != m.group;
-    } else {
-      a_src = p.w2 + (((size_t)gr.expert * HT + m.tile) * p.NTA + p.tile0) * (size_t)A_KB;
-      b_src = p.ab + gr.ab_off;
-      flag = &p.ready[m.group];
-      need = 1u + p.dep_extra;
-      check = seen_a != m.group;
+    const uint8_t* a_src = m.kind == 1
+                               ? p.w13 + ((size_t)gr.expert * p.NTA + p.tile0 + m.tile) * (size_t)KB1 * A_KB
+                               : p.w2 + (((size_t)gr.expert * HT + m.tile) * p.NTA + p.tile0) * (size_t)A_KB;
+    // Weights of the CTA's first stages go out before the prep kernel is waited
+    // for: they depend on the routing only (the ring is empty, so every slot is free).
+    const int pre = prep_seen ? 0 : min(m.nst, p.ns);
+    for (int s = 0; s < pre; ++s) {
+      const int nkb = s < m.nst - 1 ? SK : m.nkb_last;
+      mbar_arrive_expect_tx(&S.full[s], (uint32_t)(nkb * A_KB + sbs));
+      bulk_g2s(ring + (size_t)s * A_STAGE, a_src + (size_t)s * SK * A_KB, (uint32_t)(nkb * A_KB), &S.full[s]);
     }
+    if (!prep_seen) {
+      pdl_wait();
+      fence_proxy_async_global();
+      prep_seen = true;
+    }
+    const uint32_t next = gridDim.x + atomicAdd(&p.ctl->work, 1u);   // the following item, claimed ahead
+    bool check = m.kind == 2 && seen_a != m.group;
     for (int s = 0; s < m.nst; ++s, ++sc) {
       const int slot = (int)(sc % (uint32_t)p.ns);
-      // slot (weights + activation operand) free once stage sc - ns completed
-      if (sc >= (uint32_t)p.ns &&
-          !mbar_wait_bounded(&S.empty[slot], ((sc / p.ns) - 1) & 1, status, QX_DEV_TIMEOUT, deadline)) {
-        ok = false;
-        break;
+      if (s >= pre) {
+        // slot (weights + activation operand) free once stage sc - ns completed
+        if (sc >= (uint32_t)p.ns &&
+            !mbar_wait_bounded(&S.empty[slot], ((sc / p.ns) - 1) & 1, status, QX_DEV_TIMEOUT, deadline)) {
+          ok = false;
+          break;
+        }
+        const int nkb = s < m.nst - 1 ? SK : m.nkb_last;
+        mbar_arrive_expect_tx(&S.full[slot], (uint32_t)(nkb * A_KB + sbs));
+        bulk_g2s(ring + (size_t)slot * A_STAGE, a_src + (size_t)s * SK * A_KB, (uint32_t)(nkb * A_KB),
+                 &S.full[slot]);
       }
-      const int nkb = s < m.nst - 1 ? SK : m.nkb_last;
-      uint8_t* dst = ring + (size_t)slot * A_STAGE;
       uint8_t* bdst = ring + p.b_off + (size_t)slot * p.bst;
-      mbar_arrive_expect_tx(&S.full[slot], (uint32_t)(nkb * A_KB + sbs));
-      bulk_g2s(dst, a_src + (size_t)s * SK * A_KB, (uint32_t)(nkb * A_KB), &S.full[slot]);
+      if (m.kind == 1) {
+        // gate/up: each pair's row-major x-term block of this stage
+        for (int q = 0; q < gr.gsz; ++q) {
+          const int row = ps[gr.pair_off + q].pq / p.topk;
+          bulk_g2s(bdst + q * XT_STAGE, p.xt + ((size_t)row * NXCH + s) * XT_STAGE, (uint32_t)XT_STAGE,
+                   &S.full[slot]);
+        }
+        continue;
+      }
       if (check) {
-        // The weights of the first stage are already in flight; the activation
+        // The weights of this stage are already in flight; the activation
         // operand waits for its producer. On a timeout the copy is still issued
         // (of stale bytes) so the stage completes and nothing is left pending.
-        if (!wait_flag(flag, need, status, deadline)) ok = false;
+        if (!wait_flag(&p.ready[m.group], 1u + p.dep_extra, status, deadline)) ok = false;
         fence_proxy_async_global();
         check = false;
-        if (ok) {
-          if (m.kind == 1) seen_x = m.group; else seen_a = m.group;
-        }
+        if (ok) seen_a = m.group;
       }
-      bulk_g2s(bdst, b_src + (size_t)s * sbs, (uint32_t)sbs, &S.full[slot]);
+      bulk_g2s(bdst, p.ab + gr.ab_off + (size_t)s * sbs, (uint32_t)sbs, &S.full[slot]);
       if (!ok) {
         ++sc;
         break;
@@ -692,7 +652,8 @@ __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS
     const GroupS& gr = gs[m.group];
     const bool up = m.kind == 1;                       // gate/up: unscaled x terms, constant B scales
     const uint32_t n = (uint32_t)(up ? gr.n1 : gr.n2);   // down operands have one scale atom (n <= 96)
-    const uint32_t cstride = up ? n * tc::ROWB : (uint32_t)kbs_of((int)n);   // K block to K block in a stage
+    const uint32_t cstride = up ? XT_KB : (uint32_t)kbs_of((int)n);   // K block to K block in a stage
+    const uint32_t bsbo = up ? XT_SBO : tc::SBO;
     const uint32_t idesc = tc::idesc_nvf4(n);
     const int buf = (int)(ic & 1u);
     if (ic >= 2 && !mbar_wait_bounded(&S.acc_empty[buf], ((ic / 2) - 1) & 1, status, QX_DEV_TIMEOUT, deadline))
@@ -722,7 +683,7 @@ __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS
       for (int kb = k0; kb < k1; ++kb) {   // ... then its MMAs
         const uint32_t j = (uint32_t)(kb - k0);
         const uint32_t sa = a0 + kb * A_KB, sbb = b0 + kb * cstride;
-        tc::mma_nvf4(tacc, tc::sdesc(sa, tc::LBO, tc::SBO), tc::sdesc(sbb, tc::LBO, tc::SBO), idesc, bank + 4 * j,
+        tc::mma_nvf4(tacc, tc::sdesc(sa, tc::LBO, tc::SBO), tc::sdesc(sbb, tc::LBO, bsbo), idesc, bank + 4 * j,
                      up ? tbase + TM_ONE : bank + 8 + 4 * j, first ? 0u : 1u);
         first = false;
       }
@@ -753,7 +714,7 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
   const int m = quarter * 32 + lane;               // accumulator row
   const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
 
-  x_terms_duty(p, gs, S.red4, et);
+  pdl_wait();                                       // x exponents, reset counters
 
   uint32_t mc = 0, ic = 0;
   for (;;) {
@@ -766,11 +727,8 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
     if (mt.kind == 0) break;
     const GroupS& gr = gs[mt.group];
     bool ok = true;
-    if (mt.kind == 1 && et < gr.gsz) {
-      // The rows' x exponents (written with the x terms), fetched while the MMAs run.
-      ok = wait_flag(&p.xcnt[mt.group], (uint32_t)(NXCH * gr.gsz), status, deadline);
+    if (mt.kind == 1 && et < gr.gsz)   // the rows' x exponents, fetched while the MMAs run
       S.xe[et] = __ldcg(&p.xexp[ps[gr.pair_off + et].pq / p.topk]);
-    }
     if (mt.kind == 2 && et < gr.gsz) {
       // The group's common exponents, fetched while the MMAs run.
       ok = wait_flag(&p.ready[mt.group], 1u + p.dep_extra, status, deadline);
@@ -903,35 +861,6 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
   }
 }
 
-__device__ void load_tables(const Params& p, GroupS* gs, PairS* ps) {
-  const int G = (int)p.ctl->n_groups, nv = (int)p.ctl->n_valid;
-  for (int i = threadIdx.x; i < G; i += NTHR) {
-    const Group g = p.groups[i];
-    GroupS s;
-    s.expert = g.expert;
-    s.gsz = g.gsz;
-    s.pair_off = g.pair_off;
-    s.n1 = g.n1;
-    s.sbs1 = g.sbs1;
-    s.n2 = g.n2;
-    s.na2 = g.na2;
-    s.sbs2 = g.sbs2;
-    s.xb_off = (int32_t)g.xb_off;
-    s.ab_off = (int32_t)g.ab_off;
-    s.g13 = g.g13;
-    s.g2 = g.g2;
-    gs[i] = s;
-  }
-  for (int i = threadIdx.x; i < nv; i += NTHR) {
-    const int pq = p.pos_pair[i];
-    PairS s;
-    s.pq = pq;
-    s.tw = p.tw[pq];
-    s.pad[0] = s.pad[1] = 0;
-    ps[i] = s;
-  }
-}
-
 __global__ void __launch_bounds__(NTHR, 1) tc_decode_kernel(Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   Smem& S = *reinterpret_cast<Smem*>(smem);
@@ -976,25 +905,30 @@ __global__ void __launch_bounds__(NTHR, 1) tc_decode_kernel(Params p) {
     S.mma_scratch[0] = 0;
     mbar_wait_bounded(&S.init_bar, 0, &S.mma_scratch[0], 1u, globaltimer_ns() + p.timeout_ns);
   }
-  pdl_wait();                // routing tables and row terms are complete
+  // The ids, routing weights and x come from work before the prep kernel, so the
+  // routing needs no wait; the prep kernel's results are waited for by the
+  // threads that read them (producer, epilogue).
+  if (warp == 0) {
+    route_local(p, reinterpret_cast<int*>(ring), gs, ps, &S.hdr);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the ring's next writers are bulk copies
+  }
   pdl_launch_dependents();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
   {
     // Ring geometry from the largest group of this call: every slot holds one
     // weight stage and one activation stage of the widest operand.
-    const int bmx = (int)p.ctl->b_max;
+    const int bmx = S.hdr.b_max;
     p.bst = bmx < 16 ? 16 : bmx;
     int ns = (p.ring_bytes - 512) / (A_STAGE + p.bst);   // 512: slack for the last scale-atom read
     p.ns = ns > MAXNS ? MAXNS : ns;
     p.b_off = p.ns * A_STAGE;
   }
-  load_tables(p, gs, ps);
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
   const uint32_t tbase = S.tmem_base;
   const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
   if (warp == 0) {
-    if ((threadIdx.x & 31) == 0) producer(p, ring, S, gs, status, deadline);
+    if ((threadIdx.x & 31) == 0) producer(p, ring, S, gs, ps, S.hdr, status, deadline);
   } else if (warp == 1 || warp == 6) {
     if ((threadIdx.x & 31) == 0) mma_issuer(p, ring, S, gs, tbase, warp == 1 ? 0 : 1, status, deadline);
   } else {
@@ -1020,7 +954,9 @@ __global__ void __launch_bounds__(256) tc_finalize_kernel(Params p) {
       float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
       if (j < p.topk) {
         const int q = row * p.topk + j;
-        if (p.pexp[q] >= 0) z = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * HID + k));
+        const long long id = p.ids64 ? reinterpret_cast<const long long*>(p.ids)[q]
+                                     : (long long)reinterpret_cast<const int*>(p.ids)[q];
+        if (id >= 0 && id < p.E) z = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * HID + k));
       }
       v[j] = z;
     }
@@ -1155,23 +1091,18 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream)
   p.out_stride = a->out_stride;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
   p.ctl = reinterpret_cast<Ctl*>(ws + L.ctl);
-  p.groups = reinterpret_cast<Group*>(ws + L.groups);
-  p.pexp = reinterpret_cast<int32_t*>(ws + L.pexp);
-  p.pos_pair = reinterpret_cast<int32_t*>(ws + L.pos_pair);
   p.cnt1 = reinterpret_cast<uint32_t*>(ws + L.cnt1);
   p.ready = reinterpret_cast<uint32_t*>(ws + L.ready);
-  p.xcnt = reinterpret_cast<uint32_t*>(ws + L.xcnt);
-  p.pgrp = reinterpret_cast<int32_t*>(ws + L.pgrp);
   p.emax = reinterpret_cast<int32_t*>(ws + L.emax);
   p.eloc = reinterpret_cast<int32_t*>(ws + L.eloc);
   p.xexp = reinterpret_cast<int32_t*>(ws + L.xexp);
-  p.xb = ws + L.xb;
+  p.xt = ws + L.xt;
   p.ab = ws + L.ab;
   p.y = reinterpret_cast<float*>(ws + L.y);
   p.gmax = a->rows < GMAX ? a->rows : GMAX;
   const int nmax = ((8 * p.gmax + 15) / 16) * 16;
   {
-    const int s1 = SK * XTERMS * p.gmax * 32, s2 = sbs_of(nmax);
+    const int s1 = p.gmax * XT_STAGE, s2 = sbs_of(nmax);
     p.bst = s1 > s2 ? s1 : s2;   // the widest possible group, for the shape check
   }
   // shared memory: [Smem][exchange][tables][rings: ns weight stages | ns activation stages]
@@ -1182,13 +1113,14 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream)
   p.ring_off = (int)(((size_t)p.tab_off + tables + 127) & ~size_t(127));
   p.ring_bytes = (int)(SMEM_LIMIT - (size_t)p.ring_off);
   if (p.ring_bytes - 512 < 2 * (A_STAGE + p.bst)) return QX_ERR_SHAPE;   // two slots of the widest group
+  if ((size_t)p.ring_bytes < (size_t)RT_WORDS * 4) return QX_ERR_SHAPE;     // routing scratch
   p.ns = p.b_off = 0;
   p.timeout_ns = timeout_ns();
   p.dep_extra = dep_extra();
   const size_t smem_bytes = SMEM_LIMIT;
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  tc_route_kernel<<<1, 256, 0, st>>>(p);
+  tc_prep_kernel<<<a->rows * NXCH, 128, 0, st>>>(p);
   if (cudaGetLastError() != cudaSuccess) return QX_ERR_LAUNCH;
 
   cudaLaunchAttribute attr[1];

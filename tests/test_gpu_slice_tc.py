@@ -24,26 +24,26 @@ def ws_offsets(rows, topk, width):
     """Byte offsets inside a qx_slice_decode_tc workspace (mirror of its layout)."""
     p, nt = rows * topk, (width + 63) // 64
     o, off = 0, {}
-    for name, size in [("ctl", 256), ("groups", p * 64), ("pexp", p * 4), ("pos_pair", p * 4), ("cnt1", p * 4),
-                       ("ready", p * 4), ("xcnt", p * 4), ("pgrp", p * 4), ("emax", p * 4),
-                       ("eloc", p * nt * 4), ("xexp", rows * 4), ("xb", 0)]:
+    for name, size in [("ctl", 256), ("cnt1", p * 4), ("ready", p * 4), ("emax", p * 4), ("eloc", p * nt * 4),
+                       ("xexp", rows * 4), ("xt", rows * 20 * 2048)]:
         off[name] = o
         o = _al(o + size)
     return off
 
 
-def _kb_unpack(block):
-    """One pair's 512-byte tile of one K block ([row group 2][K half 2][row 8][16 bytes],
-    rows = its 16 terms) -> nibbles [16 terms, 64]."""
-    codes = block.reshape(2, 2, 8, 16)
-    nib = torch.stack([codes & 15, codes >> 4], dim=-1)              # rg, half, row, byte, nibble
+def _kb_unpack(blk, kb):
+    """K block kb of one row's 16 x terms from that row's 2,048-byte stage block
+    ([row group 2][K block 4][K half 2][term 8][16 bytes]) -> nibbles [16 terms, 64]."""
+    b = blk.reshape(2, 4, 2, 8, 16)[:, kb % 4]                        # rg, half, term, byte
+    nib = torch.stack([b & 15, b >> 4], dim=-1)                       # rg, half, term, byte, nibble
     return nib.permute(0, 2, 1, 3, 4).reshape(16, 64)
 
 
 @pytest.mark.parametrize("rows,seed", [(1, 3), (6, 4)])
 def test_x_terms_match_cpu_model(cuda_ready, rows, seed):
-    """Every group's gate/up operand holds, at each pair position, the 16 x terms
-    of that pair's row, bit for bit."""
+    """The prep kernel's x terms of every row, read back in the row-major operand
+    layout, equal the CPU model of the decomposition bit for bit, and the row
+    exponents match."""
     from qmesh_b200.arena import Arena
     from qmesh_b200.expert_slice import alloc_workspace, expert_slice
     dev = cuda_ready
@@ -57,26 +57,16 @@ def test_x_terms_match_cpu_model(cuda_ready, rows, seed):
     torch.cuda.synchronize()
     off = ws_offsets(rows, 6, 256)
     w = ws.cpu()
-    n_groups = int(w[4 * 2:4 * 3].view(torch.int32))                 # ctl.n_groups
     xexp = w[off["xexp"]:off["xexp"] + rows * 4].view(torch.int32)
-    pos_pair = w[off["pos_pair"]:off["pos_pair"] + rows * 6 * 4].view(torch.int32)
     x = H.ingest(q, inv)
     codes, e = NT.decompose_x(x)
     assert torch.equal(xexp, e), (xexp, e)
-    seen = 0
-    for g in range(n_groups):
-        rec = w[off["groups"] + 64 * g:off["groups"] + 64 * (g + 1)]
-        gsz, pair_off, n1 = (int(v) for v in rec[4:16].view(torch.int32))
-        xb_off = int(rec[32:40].view(torch.int64))
-        for qq in range(gsz):
-            row = int(pos_pair[pair_off + qq]) // 6
-            for kb in range(80):
-                base = off["xb"] + xb_off + kb * n1 * 32 + qq * 512
-                got = _kb_unpack(w[base:base + 512])
-                want = codes[row, :, kb * 64:(kb + 1) * 64]
-                assert torch.equal(got, want), f"group {g} pair {qq} row {row} K block {kb}"
-            seen += 1
-    assert seen == int((ids >= 0).sum())
+    for r in range(rows):
+        for kb in range(80):
+            base = off["xt"] + (r * 20 + kb // 4) * 2048
+            got = _kb_unpack(w[base:base + 2048], kb)
+            want = codes[r, :, kb * 64:(kb + 1) * 64]
+            assert torch.equal(got, want), f"row {r} K block {kb}"
     rec_x = NT.reconstruct_x(codes, e)
     amax = x.abs().amax(dim=1, keepdim=True).double()
     assert ((rec_x - x.double()).abs() <= amax * 2.0 ** -30).all()
