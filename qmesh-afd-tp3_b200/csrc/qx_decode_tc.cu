@@ -60,8 +60,7 @@ namespace tcd {
 
 constexpr int HID = QX_HIDDEN;                 // 5120
 constexpr int KB1 = HID / 64;                  // 80 K blocks in a gate/up item
-constexpr int TERMS = 8;                       // SwiGLU-output terms = B rows per pair (down items)
-constexpr int XTERMS = 16;                     // x terms = B rows per pair (gate/up items)
+constexpr int XTERMS = 16;                     // activation terms = B rows per pair (both item kinds)
 constexpr int GMAX = 6;                        // routed pairs per group (gate/up N = 16 x 6 = 96)
 constexpr int SK = 4;                          // K blocks per stage
 constexpr int A_KB = 128 * tc::ROWB + tc::SF_ATOM;  // 4608 weight bytes per K block
@@ -85,10 +84,9 @@ constexpr int NTHR = 224;                      // producer, issuer 0, 4 epilogue
 //   MMAs do not read, so no MMA waits on the copy just before it.
 constexpr uint32_t TM_COLS = 512, TM_SLOT = 128, TM_ONE = 96, TM_SF = 224, TM_BANK = 16;
 constexpr int NISS = 2, KB_PER_ISS = SK / NISS;
-static_assert(GMAX * TERMS <= 128, "a down operand keeps one scale atom per K block");
-static_assert(GMAX * XTERMS <= 96 && ((GMAX * TERMS + 15) / 16) * 16 <= 96, "an accumulator fits its slot");
-constexpr int E_LO = -100, E_HI = 100;
-constexpr int XE_LO = -90, XE_HI = 100;
+static_assert(GMAX * XTERMS <= 96, "an accumulator fits its slot");
+constexpr int XE_LO = -90, XE_HI = 100;      // x exponents
+constexpr int AE_LO = -90, AE_HI = 100;      // SwiGLU-output exponents (even)
 
 struct Ctl {
   uint32_t work, status;   // dynamic item queue (after the first grid-size items), QX_DEV_* bits
@@ -98,12 +96,11 @@ static_assert(sizeof(Ctl) == 256, "ctl block is 256 bytes");
 
 struct GroupS {     // one group (<= GMAX routed pairs of one expert), kept in shared memory
   int32_t expert, gsz, pair_off;
-  int32_t n1, sbs1;       // gate/up activation operand: 16 x gsz rows, bytes per stage
-  int32_t n2, na2, sbs2;  // down activation operand: round16(8 x gsz) rows, its scale atoms, bytes per stage
-  int32_t ab_off, pad;    // offset of the group's down operand in the activation-term buffer
+  int32_t n, sbs;         // activation operand of either item kind: 16 x gsz rows, bytes per stage
+  int32_t ab_off;         // offset of the group's down operand in the activation-term buffer
   float g13, g2;
 };
-static_assert(sizeof(GroupS) == 48, "shared group record is 48 bytes");
+static_assert(sizeof(GroupS) == 32, "shared group record is 32 bytes");
 
 struct RouteHdr {   // call-wide results of the routing, in shared memory
   int32_t n_groups, n1, n2, b_max;   // groups, gate/up items, down items, widest activation stage
@@ -142,7 +139,7 @@ struct Params {
   int32_t* eloc;      // [P][NT] per group position and tile: tile exponent
   int32_t* xexp;      // [rows]
   uint8_t* xt;        // [rows][20 stages][2048 bytes]: x terms, row-major
-  uint8_t* ab;        // per group: ceil(NT/4) stages of sbs2 bytes (SwiGLU-output terms)
+  uint8_t* ab;        // per group: ceil(NT/4) stages of sbs bytes (SwiGLU-output terms)
   float* y;           // [P][HID]
   int x_off;          // shared-memory offset of the SwiGLU exchange (2 x gmax x 64 floats)
   int tab_off;        // shared-memory offset of the group and pair tables
@@ -162,38 +159,17 @@ struct ItemMeta {
 
 __host__ __device__ inline size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// Scale-atom bytes of one K block of an n-row activation operand: rows < 32 use
-// only the first 4 bytes of their line, so n <= 32 rows need n lines of 16
-// bytes (the 512-byte copy into TMEM reads past them; those lanes are rows the
-// MMA does not have); otherwise one 512-byte atom per 128 rows.
-__host__ __device__ inline int atom_bytes(int n) { return n <= 32 ? n * 16 : ((n + 127) / 128) * 512; }
-__host__ __device__ inline int kbs_of(int n) { return n * 32 + atom_bytes(n); }
-
-// Down-projection activation operand of a group (n = round16(8 gsz) rows):
-// stages of SK K blocks, each K block the n x 32-byte code tile then its scale
-// atoms (atom_bytes(n)).
-//
-// Gate/up operand (16 x gsz rows of x terms, codes only): each row's terms are
-// kept row-major, one 2,048-byte block per row and stage laid out
-// [row group 2][K block 4][K half 2][8 terms][16 bytes]. A group's stage is its
-// pairs' blocks side by side (pair q at 2,048 q), so operand row group j sits at
-// 1,024 j: one MMA per K block with leading offset 128 and stride 1,024 reads
-// all of the group's rows, and the stage is gsz copies of 2,048 bytes.
-constexpr int XT_STAGE = 2048;                 // x-term bytes per row and stage
-constexpr uint32_t XT_SBO = 1024;              // gate/up operand: row group to row group
-constexpr uint32_t XT_KB = 256;                // gate/up operand: K block to K block
-__host__ __device__ inline int sbs_of(int n) { return SK * kbs_of(n); }
-__host__ __device__ inline size_t b_codes(int n, int sbs, int kb) {
-  return (size_t)(kb / SK) * sbs + (size_t)(kb % SK) * kbs_of(n);
-}
-__host__ __device__ inline size_t b_scales(int n, int sbs, int kb, int r) {
-  return b_codes(n, sbs, kb) + (size_t)n * 32 + (size_t)(r >> 7) * tc::SF_ATOM + tc::sf_off((uint32_t)(r & 127), 0);
-}
-
-// Upper bound of a call's per-group operand bytes for P routed pairs and nkb K
-// blocks: per pair and K block at most 16 x 32 code bytes (gate/up) or
-// 256 + 256 + 1024 (down: codes, padding pair, scale atoms).
-__host__ inline size_t group_bytes_bound(int P, int nkb) { return (size_t)nkb * P * 1536; }
+// Activation operands (16 x gsz rows of e2m1 terms, codes only; the B-side
+// scales are the constant 1.0 atom). x terms are kept row-major, one 2,048-byte
+// block per row and stage laid out [row group 2][K block 4][K half 2][8 terms]
+// [16 bytes]. A group's stage is its pairs' blocks side by side (pair q at
+// 2,048 q), so operand row group j sits at 1,024 j: one MMA per K block with
+// leading offset 128 and stride 1,024 reads all of the group's rows, and the
+// gate/up stage is gsz copies of 2,048 bytes. The SwiGLU-output terms of a group
+// (down items) use the same stage layout, one copy of gsz x 2,048 bytes.
+constexpr int XT_STAGE = 2048;                 // term bytes per pair (row) and stage
+constexpr uint32_t XT_SBO = 1024;              // row group to row group
+constexpr uint32_t XT_KB = 256;                // K block to K block
 
 struct WsLayout {
   size_t ctl, cnt1, ready, emax, eloc, xexp, xt, ab, y, total;
@@ -210,22 +186,26 @@ __host__ inline WsLayout ws_layout(int rows, int topk, int W) {
   L.eloc = o;     o = al256(o + (size_t)P * NT * 4);
   L.xexp = o;     o = al256(o + (size_t)rows * 4);
   L.xt = o;       o = al256(o + (size_t)rows * (KB1 / SK) * XT_STAGE);
-  L.ab = o;       o = al256(o + group_bytes_bound(P, (NT + SK - 1) / SK * SK));
+  L.ab = o;       o = al256(o + (size_t)P * ((NT + SK - 1) / SK) * XT_STAGE);
   L.y = o;        o = al256(o + (size_t)P * HID * 4);
   L.total = o;
   return L;
 }
 
 // ------------------------------------------------------------------ prologue
-// Smallest E with 2688 * 2^E >= amax (0 for amax == 0), clamped to [-100, 100].
-__device__ __forceinline__ int term_exponent(float amax) {
-  if (!(amax > 0.f)) return 0;
+// SwiGLU-output exponent of one pair over one 64-column tile: the smallest EVEN
+// E with 6 * 2^E >= amax, clamped to [-90, 100] (-90 for amax == 0, so an
+// all-zero tile never raises the pair's common exponent). Even, so that moving
+// a tile to a larger common exponent is a shift of whole terms.
+__device__ __forceinline__ int act_exponent(float amax) {
+  if (!(amax > 0.f)) return AE_LO;
   int ex;
   frexpf(amax, &ex);
-  int e = ex - 12;
-  while (e > E_LO && ldexpf(2688.f, e - 1) >= amax) --e;
-  while (e < E_HI && ldexpf(2688.f, e) < amax) ++e;
-  return e;
+  int e = ex - 3;
+  while (e > AE_LO && ldexpf(6.f, e - 1) >= amax) --e;
+  while (e < AE_HI && ldexpf(6.f, e) < amax) ++e;
+  e += e & 1;
+  return e > AE_HI ? AE_HI : e;
 }
 
 // Smallest E with 6 * 2^E >= amax (0 for amax == 0), clamped to [-90, 100]:
@@ -396,18 +376,14 @@ __device__ void route_local(const Params& p, int* scr, GroupS* gs, PairS* ps, Ro
       d.expert = e;
       d.gsz = gsz;
       d.pair_off = off[u] + lo;
-      d.n1 = XTERMS * gsz;
-      d.sbs1 = gsz * XT_STAGE;
-      d.n2 = ((TERMS * gsz + 15) / 16) * 16;
-      d.na2 = (d.n2 + 127) / 128;
-      d.sbs2 = sbs_of(d.n2);
+      d.n = XTERMS * gsz;
+      d.sbs = gsz * XT_STAGE;
       d.ab_off = 0;
-      d.pad = 0;
       d.g13 = g13;
       d.g2 = g2;
       gs[gf[u] + k] = d;
-      asz[gf[u] + k] = ((p.NT + SK - 1) / SK) * d.sbs2;
-      bmx = max(bmx, max(d.sbs1, d.sbs2));
+      asz[gf[u] + k] = ((p.NT + SK - 1) / SK) * d.sbs;
+      bmx = max(bmx, d.sbs);
     }
   }
   __syncwarp();
@@ -574,7 +550,7 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
       return;
     }
     const GroupS& gr = gs[m.group];
-    const int sbs = m.kind == 1 ? gr.sbs1 : gr.sbs2;
+    const int sbs = gr.sbs;
     const uint8_t* a_src = m.kind == 1
                                ? p.w13 + ((size_t)gr.expert * p.NTA + p.tile0 + m.tile) * (size_t)KB1 * A_KB
                                : p.w2 + (((size_t)gr.expert * HT + m.tile) * p.NTA + p.tile0) * (size_t)A_KB;
@@ -650,11 +626,7 @@ __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS
     ++mc;
     if (m.kind == 0) break;
     const GroupS& gr = gs[m.group];
-    const bool up = m.kind == 1;                       // gate/up: unscaled x terms, constant B scales
-    const uint32_t n = (uint32_t)(up ? gr.n1 : gr.n2);   // down operands have one scale atom (n <= 96)
-    const uint32_t cstride = up ? XT_KB : (uint32_t)kbs_of((int)n);   // K block to K block in a stage
-    const uint32_t bsbo = up ? XT_SBO : tc::SBO;
-    const uint32_t idesc = tc::idesc_nvf4(n);
+    const uint32_t idesc = tc::idesc_nvf4((uint32_t)gr.n);
     const int buf = (int)(ic & 1u);
     if (ic >= 2 && !mbar_wait_bounded(&S.acc_empty[buf], ((ic / 2) - 1) & 1, status, QX_DEV_TIMEOUT, deadline))
       break;
@@ -675,16 +647,12 @@ __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS
       const uint32_t a0 = smem_u32(ring + (size_t)slot * A_STAGE);
       const uint32_t b0 = smem_u32(ring + p.b_off + (size_t)slot * p.bst);
       const uint32_t bank = sfbase + (sc & 1u) * TM_BANK;
-      for (int kb = k0; kb < k1; ++kb) {   // this issuer's scale atoms of the stage first ...
-        const uint32_t j = (uint32_t)(kb - k0);
-        tc::cp_sf_atom(bank + 4 * j, a0 + kb * A_KB + 128 * tc::ROWB);
-        if (!up) tc::cp_sf_atom(bank + 8 + 4 * j, b0 + kb * cstride + n * tc::ROWB);
-      }
-      for (int kb = k0; kb < k1; ++kb) {   // ... then its MMAs
-        const uint32_t j = (uint32_t)(kb - k0);
-        const uint32_t sa = a0 + kb * A_KB, sbb = b0 + kb * cstride;
-        tc::mma_nvf4(tacc, tc::sdesc(sa, tc::LBO, tc::SBO), tc::sdesc(sbb, tc::LBO, bsbo), idesc, bank + 4 * j,
-                     up ? tbase + TM_ONE : bank + 8 + 4 * j, first ? 0u : 1u);
+      for (int kb = k0; kb < k1; ++kb)     // this issuer's weight scale atoms of the stage first ...
+        tc::cp_sf_atom(bank + 4 * (uint32_t)(kb - k0), a0 + kb * A_KB + 128 * tc::ROWB);
+      for (int kb = k0; kb < k1; ++kb) {   // ... then its MMAs (activation scales: the constant atom)
+        const uint32_t sa = a0 + kb * A_KB, sbb = b0 + kb * XT_KB;
+        tc::mma_nvf4(tacc, tc::sdesc(sa, tc::LBO, tc::SBO), tc::sdesc(sbb, tc::LBO, XT_SBO), idesc,
+                     bank + 4 * (uint32_t)(kb - k0), tbase + TM_ONE, first ? 0u : 1u);
         first = false;
       }
       tc::commit(&S.empty[slot]);          // arrives when this issuer's work on the stage is done
@@ -765,8 +733,8 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       if (lane == 0) mbar_arrive(&S.acc_empty[buf]);
       asm volatile("bar.sync 1, 128;" ::: "memory");
       const int col0 = mt.tile * 64;
-      uint8_t* ab = p.ab + gr.ab_off;
-      const size_t cb = b_codes(gr.n2, gr.sbs2, mt.tile);
+      const int kbl = mt.tile % SK;                   // the tile is K block kbl of down stage tile / 4
+      uint8_t* ab = p.ab + gr.ab_off + (size_t)(mt.tile / SK) * gr.sbs;
       if (!up) {
         // SwiGLU per pair, |act| maxima per half tile
         const int half = warp & 1;   // quarters 0, 1 <-> columns 0..31, 32..63
@@ -785,26 +753,25 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
           if (lane == 0) S.amx[q][half] = mx;
         }
         asm volatile("bar.sync 2, 64;" ::: "memory");
+        // 16 unscaled e2m1 terms per pair with the tile's own even exponent:
+        // act = sum_t 2^(el - 2t) q_t (the same digit rule as the x terms).
         for (int q = 0; q < gr.gsz; ++q) {
-          const int el = term_exponent(fmaxf(S.amx[q][0], S.amx[q][1]));
+          const int el = act_exponent(fmaxf(S.amx[q][0], S.amx[q][1]));
           float r = xg[q * 64 + c];
+          uint8_t* blk = ab + (size_t)q * XT_STAGE + kbl * XT_KB + (c >> 5) * 128 + ((c & 31) >> 1);
 #pragma unroll 1
-          for (int t = 0; t < TERMS; ++t) {
-            uint32_t sb;
-            const uint32_t code = tc::term_step(r, ldexpf(1.f, el - 2 * t), &sb);
+          for (int t = 0; t < XTERMS; ++t) {
+            const float g = ldexpf(1.f, el - 2 * t);
+            const uint32_t code = tc::e2m1_of(r, g);
+            r = fmaf(-tc::e2m1_val(code), g, r);
             const uint32_t w = tc::pack8(code, lane);
-            const int n = 8 * q + t;
-            if ((lane & 7) == 0)
-              *reinterpret_cast<uint32_t*>(ab + cb + q * 256 + half * 128 + t * 16 + (lane >> 3) * 4) = w;
-            if ((lane & 15) == 0) ab[b_scales(gr.n2, gr.sbs2, mt.tile, n) + (c >> 4)] = (uint8_t)sb;
+            if ((lane & 7) == 0) *reinterpret_cast<uint32_t*>(blk + (t >> 3) * XT_SBO + (t & 7) * 16) = w;
           }
           if (c == 0) {
             p.eloc[(size_t)(gr.pair_off + q) * p.NT + mt.tile] = el;
             atomicMax(&p.emax[gr.pair_off + q], el);
           }
         }
-        if (gr.n2 > TERMS * gr.gsz && c < TERMS)       // padding pair of the down operand: zero scales
-          *reinterpret_cast<uint32_t*>(ab + b_scales(gr.n2, gr.sbs2, mt.tile, TERMS * gr.gsz + c)) = 0u;
         __threadfence();
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -814,20 +781,44 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (S.last_flag) {
-        // Last tile of the group: bring every tile's scales to the common exponent.
-        uint8_t* ab0 = p.ab + gr.ab_off;
-        for (int i = et; i < p.NT * gr.gsz; i += 128) {
+        // Last tile of the group: bring every tile to the pair's common exponent
+        // em by moving its terms d = (em - el) / 2 places down (term t becomes
+        // term t + d; the last d terms, below the common precision, drop out).
+        // Shifts of all (tile, pair) items first (into the exchange area, free
+        // now; NT x gsz <= 64 gmax), then one item per warp and lane = (K half,
+        // term) owning 16 code bytes, four items in flight per warp.
+        int* dsh = reinterpret_cast<int*>(xg);
+        const int nit = p.NT * gr.gsz;
+        for (int i = et; i < nit; i += 128) {
           const int tile = i / gr.gsz, q = i - tile * gr.gsz;
-          const int sh = __ldcg(&p.emax[gr.pair_off + q]) - __ldcg(&p.eloc[(size_t)(gr.pair_off + q) * p.NT + tile]);
-          if (sh <= 0) continue;
-          for (int t = 0; t < TERMS; ++t) {
-            const int n = 8 * q + t;
-            uint32_t* w = reinterpret_cast<uint32_t*>(ab0 + b_scales(gr.n2, gr.sbs2, tile, n));
-            const uint32_t b = __ldcg(w);
-            uint32_t nb = 0;
+          dsh[i] = (__ldcg(&p.emax[gr.pair_off + q]) - __ldcg(&p.eloc[(size_t)(gr.pair_off + q) * p.NT + tile])) >> 1;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const int ew = et >> 5, t = lane & 15, kh = lane >> 4;
+        for (int i0 = 4 * ew; i0 < nit; i0 += 16) {
+          int dd[4];
+          uint4* wp[4];
+          uint4 v[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) nb |= tc::e4m3_shift((b >> (8 * j)) & 0xFFu, sh) << (8 * j);
-            *w = nb;
+          for (int j = 0; j < 4; ++j) {
+            const int i = i0 + j;
+            dd[j] = i < nit ? dsh[i] : 0;
+            const int tile = i / gr.gsz, q = i - tile * gr.gsz;
+            wp[j] = reinterpret_cast<uint4*>(p.ab + gr.ab_off + (size_t)(tile / SK) * gr.sbs + (size_t)q * XT_STAGE +
+                                             (t >> 3) * XT_SBO + (tile % SK) * XT_KB + kh * 128 + (t & 7) * 16);
+            if (dd[j] > 0) v[j] = __ldcg(wp[j]);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (dd[j] <= 0) continue;          // warp-uniform
+            const int d = dd[j];
+            uint4 nv;
+            nv.x = __shfl_up_sync(0xffffffffu, v[j].x, d & 15, 16);
+            nv.y = __shfl_up_sync(0xffffffffu, v[j].y, d & 15, 16);
+            nv.z = __shfl_up_sync(0xffffffffu, v[j].z, d & 15, 16);
+            nv.w = __shfl_up_sync(0xffffffffu, v[j].w, d & 15, 16);
+            if (t < d) nv = make_uint4(0u, 0u, 0u, 0u);
+            __stcg(wp[j], nv);
           }
         }
         __threadfence();
@@ -838,19 +829,19 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       // ---- down tile: output rows [128 tile, 128 tile + 128)
       const int h = mt.tile * 128 + m;
       for (int q = 0; q < gr.gsz; ++q) {
-        float v[8];
-        tc::ld8(tacc + 8 * q, v);
+        float v[16];
+        tc::ld16(tacc + XTERMS * q, v);
         if (two) {
-          float v1[8];
-          tc::ld8(tacc + TM_SLOT + 8 * q, v1);
+          float v1[16];
+          tc::ld16(tacc + TM_SLOT + XTERMS * q, v1);
 #pragma unroll
-          for (int t = 0; t < TERMS; ++t) v[t] += v1[t];
+          for (int t = 0; t < XTERMS; ++t) v[t] += v1[t];
         }
         const PairS pr = ps[gr.pair_off + q];
         const int ea = S.em[q];
         float s = 0.f;
 #pragma unroll
-        for (int t = 0; t < TERMS; ++t) s += v[t] * term_scale(ea, t);
+        for (int t = XTERMS - 1; t >= 0; --t) s += v[t] * term_scale(ea, t);   // smallest terms first
         p.y[(size_t)pr.pq * HID + h] = s * (gr.g2 * pr.tw);
       }
       tc::fence_before_sync();
@@ -1048,6 +1039,7 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream)
   if (a->x_fmt < QX_X_E4M3 || a->x_fmt > QX_X_BF16) return QX_ERR_ARG;
   if (a->rows < 1 || a->rows > QX_MAX_ROWS || a->topk < 1 || a->topk > QX_MAX_TOPK) return QX_ERR_SHAPE;
   if (arena->n_experts < 1 || arena->n_experts > MAXE) return QX_ERR_SHAPE;
+  if (a->c1 - a->c0 > 64 * 64) return QX_ERR_SHAPE;   // at most 64 column tiles per slice
   if (arena->a0 % 32 || arena->a1 % 32 || arena->a1 <= arena->a0) return QX_ERR_SHAPE;
   if ((a->c0 - arena->a0) % 64 || a->c1 % 32 || a->c0 < arena->a0 || a->c1 > arena->a1 || a->c1 <= a->c0)
     return QX_ERR_SHAPE;
@@ -1100,10 +1092,8 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream)
   p.ab = ws + L.ab;
   p.y = reinterpret_cast<float*>(ws + L.y);
   p.gmax = a->rows < GMAX ? a->rows : GMAX;
-  const int nmax = ((8 * p.gmax + 15) / 16) * 16;
   {
-    const int s1 = p.gmax * XT_STAGE, s2 = sbs_of(nmax);
-    p.bst = s1 > s2 ? s1 : s2;   // the widest possible group, for the shape check
+    p.bst = p.gmax * XT_STAGE;   // the widest possible group, for the shape check
   }
   // shared memory: [Smem][exchange][tables][rings: ns weight stages | ns activation stages]
   const size_t tables = (size_t)p.P * (sizeof(GroupS) + sizeof(PairS));
