@@ -38,9 +38,9 @@ INTER = 2304
 N_EXPERTS = 384
 TOPK = 6
 EXPERT_BYTES = 2 * INTER * (HIDDEN // 2 + HIDDEN // 16) + HIDDEN * (INTER // 2 + INTER // 16)  # 19,906,560
-# DRAM bytes (read + write) per unique expert per launch of qx_decode_kernel, from the ncu capture in
-# profiles/qx_decode_kernel_rows6.md (545.86 MB over 27 unique experts, full 2304 columns).
-DRAM_BYTES_PER_UNIQUE = 545.86e6 / 27
+# DRAM bytes (read + write) per unique expert per launch of tc_decode_kernel, from the ncu capture in
+# profiles/tc_decode_kernel_config1.md (544.78 MB over 27 unique experts, full 2304 columns).
+DRAM_BYTES_PER_UNIQUE = 544.78e6 / 27
 METRIC = "MoE-layer decode µs (6 rows) & NVFP4 weight GB/s vs HBM peak, 1/2/4/8 GPU"
 
 
@@ -257,7 +257,7 @@ def run_ours(args) -> dict | None:
                        "routing_draws": args.draws, "mean_unique_experts": round(mean_u, 2),
                        "l2": "inputs larger than L2: ~%.0f MB of expert weights per step" % (mean_u * EXPERT_BYTES / 1e6),
                        "parallelism": f"column-split tp{world}",
-                       "kernel": "tcgen05 mxf4nvf4 (8-term NVFP4 activations)" if args.layout == "tc"
+                       "kernel": "tcgen05 mxf4nvf4 (16-term e2m1 activations)" if args.layout == "tc"
                        else "register dequant + mma.sync"},
             "tokens_per_s": round(rows / (us_layer * 1e-6), 1),
             "weight_gbs": round(gbs, 1),
