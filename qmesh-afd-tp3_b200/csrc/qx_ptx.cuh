@@ -1,6 +1,6 @@
 // Inline-PTX helpers for sm_100a: mbarriers, bulk async copies (TMA engine),
 // proxy fences, acquire/release atomics, e2m1/e4m3 converts and the
-// mixed-precision FMA. Nothing here issues a multicast copy.
+// mixed-precision FMA. Every bulk copy here lands in the issuing CTA only.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -68,7 +68,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 
 // ---- bulk async copy global -> shared (TMA engine, no tensor map) ------------
 // dst, src 16-byte aligned, bytes a multiple of 16. Completion is signalled on
-// `bar` as transaction bytes. CTA-local destination (no cluster multicast).
+// `bar` as transaction bytes. CTA-local destination.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
