@@ -69,8 +69,13 @@ constexpr int HT = HID / 128;                  // 40 output-row tiles in a down 
 constexpr int MAXP = QX_MAX_ROWS * QX_MAX_TOPK;
 constexpr int MAXE = 4096;
 constexpr int MAXNS = 12;                      // ring slots
-constexpr int NI = MAXNS + 2;
-constexpr int NTHR = 224;                      // producer, issuer 0, 4 epilogue warps, issuer 1
+constexpr int NI = MAXNS + 2;                 // even: an epilogue group reuses its own meta entries
+static_assert(NI % 2 == 0, "epilogue groups alternate meta entries");
+// Warps: 0 producer, 1 and 6 MMA issuers, 2-5 and 7-10 two epilogue warpgroups
+// (group g takes the items of accumulator buffer g, so a long gate/up epilogue
+// never holds up the next item's accumulator).
+constexpr int NTHR = 352;
+constexpr int NEPI = 2;                        // epilogue warpgroups
 // Two MMA issuer warps split every stage: K blocks 0-1 go to issuer 0, 2-3 to
 // issuer 1, each into its own accumulator (summed in the epilogue); one thread
 // cannot issue block-scaled MMAs as fast as the tensor pipe executes them.
@@ -141,7 +146,7 @@ struct Params {
   uint8_t* xt;        // [rows][20 stages][2048 bytes]: x terms, row-major
   uint8_t* ab;        // per group: ceil(NT/4) stages of sbs bytes (SwiGLU-output terms)
   float* y;           // [P][HID]
-  int x_off;          // shared-memory offset of the SwiGLU exchange (2 x gmax x 64 floats)
+  int x_off;          // shared-memory offset of the SwiGLU exchanges (per epilogue group 2 x gmax x 64 floats)
   int tab_off;        // shared-memory offset of the group and pair tables
   int ring_off, ring_bytes;  // shared-memory span of the stage rings
   int gmax;           // pairs per group at most
@@ -430,31 +435,20 @@ __global__ void __launch_bounds__(128) tc_prep_kernel(Params p) {
   if (p.x_fmt == QX_X_E4M3) inv = p.x_scale[r];
   else if (p.x_fmt == QX_X_E4M3_POST) inv = p.x_scale[0];
   const uint8_t* xr = reinterpret_cast<const uint8_t*>(p.x) + (size_t)r * p.x_stride;
-  float v[2];
-  int kk[2], kbl[2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int k = c * XCH + h * 128 + tid;
-    v[h] = ingest_one(p, xr, k, inv);
-    kbl[h] = (k >> 6) & (SK - 1);
-    kk[h] = k & 63;
-  }
+  // Thread tid owns elements k, k + 1 (k = 256 c + 2 tid): warp w is K block w
+  // of the stage, lane l its columns 2l, 2l + 1.
+  const int k = c * XCH + 2 * tid;
+  float v0 = ingest_one(p, xr, k, inv), v1 = ingest_one(p, xr, k + 1, inv);
   const int e = x_exponent(row_amax128(p, xr, inv, red, tid));
   if (c == 0 && tid == 0) p.xexp[r] = e;
-  uint8_t* blk = p.xt + ((size_t)r * NXCH + c) * XT_STAGE;
+  uint8_t* blk = p.xt + ((size_t)r * NXCH + c) * XT_STAGE + (tid >> 5) * XT_KB + (lane >> 4) * 128 + (lane & 12);
+  float g = tc::exp2i(e), ig = tc::exp2i(-e);
 #pragma unroll 1
   for (int tt = 0; tt < XTERMS; ++tt) {
-    const float g = ldexpf(1.f, e - 2 * tt);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t code = tc::e2m1_of(v[h], g);    // exact: v / g is a power-of-two rescale
-      v[h] = fmaf(-tc::e2m1_val(code), g, v[h]);
-      const uint32_t w = tc::pack8(code, lane);
-      if ((lane & 7) == 0) {
-        const int o = (tt >> 3) * 1024 + kbl[h] * 256 + (kk[h] >> 5) * 128 + (tt & 7) * 16 + ((kk[h] & 31) >> 1);
-        *reinterpret_cast<uint32_t*>(blk + o) = w;
-      }
-    }
+    const uint32_t w = tc::pack4(tc::digit2(v0, v1, g, ig), lane);
+    if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(blk + (tt >> 3) * XT_SBO + (tt & 7) * 16) = w;
+    g *= 0.25f;
+    ig *= 4.f;
   }
 }
 
@@ -494,10 +488,11 @@ struct Smem {       // fixed part of the dynamic shared memory, before the rings
   ItemMeta meta[NI];
   uint64_t drain[NISS];
   uint64_t init_bar;
-  uint32_t tmem_base, last_flag, prod_scratch, mma_scratch[NISS];   // scratch: status words of drain waits
-  float amx[GMAX][2];   // per pair, per half: |act| maximum
-  int32_t em[GMAX];     // down item: the group's common activation exponents
-  int32_t xe[GMAX];     // gate/up item: the group's rows' x exponents
+  uint32_t tmem_base, prod_scratch, mma_scratch[NISS];   // scratch: status words of drain waits
+  uint32_t last_flag[NEPI];
+  float amx[NEPI][GMAX][2];   // per epilogue group, pair, half: |act| maximum
+  int32_t em[NEPI][GMAX];     // down item: the group's common activation exponents
+  int32_t xe[NEPI][GMAX];     // gate/up item: the group's rows' x exponents
   RouteHdr hdr;
 };
 
@@ -545,6 +540,13 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
     mbar_arrive(&S.meta_full[mi]);
     ++mc;
     if (m.kind == 0) {
+      // A second end marker: the epilogue groups take alternate entries.
+      const int mi2 = (int)(mc % NI);
+      if (mc < (uint32_t)NI ||
+          mbar_wait_bounded(&S.meta_empty[mi2], ((mc / NI) - 1) & 1, status, QX_DEV_TIMEOUT, deadline)) {
+        S.meta[mi2] = m;
+        mbar_arrive(&S.meta_full[mi2]);
+      }
       if (!prep_seen) pdl_wait();
       if (!ok) drain_copies(p, S, sc);
       return;
@@ -670,41 +672,47 @@ __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS
 // Whether issuer 1 wrote its accumulator for an item (it owns K blocks 2-3 of each stage).
 __device__ __forceinline__ bool second_acc(const ItemMeta& m) { return m.nst > 1 || m.nkb_last > KB_PER_ISS; }
 
-// Scale of term t for exponent e: 2^(e - 2t), exact.
-__device__ __forceinline__ float term_scale(int e, int t) { return ldexpf(1.f, e - 2 * t); }
 
+// Epilogue warpgroup eg (warps 2-5 or 7-10): the items of accumulator buffer
+// eg, i.e. every other item. Named barriers 1 + 2 eg (its 128 threads) and
+// 2 + 2 eg (its gate half).
 __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, const PairS* ps, uint32_t tbase,
-                         volatile uint32_t* status, uint64_t deadline) {
+                         int eg, volatile uint32_t* status, uint64_t deadline) {
+  xg += eg * 2 * p.gmax * 64;
   float* xu = xg + p.gmax * 64;                  // gate and up values of a gate/up item, [pair][column]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int et = threadIdx.x - 64;                 // 0..127
+  const int et = threadIdx.x - (eg ? 224 : 64);    // 0..127
+  const int B1 = 1 + 2 * eg;                       // this group's 128-thread barrier
   const int quarter = warp & 3;                    // TMEM lane quarter this warp may read
   const int m = quarter * 32 + lane;               // accumulator row
   const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
 
   pdl_wait();                                       // x exponents, reset counters
 
-  uint32_t mc = 0, ic = 0;
-  for (;;) {
+  uint32_t* last_flag = &S.last_flag[eg];
+  float(*amx)[2] = S.amx[eg];
+  int32_t* em = S.em[eg];
+  int32_t* xe_s = S.xe[eg];
+  for (uint32_t ic = (uint32_t)eg;; ic += NEPI) {   // item ic = meta entry ic
+    const uint32_t mc = ic;
     const int mi = (int)(mc % NI);
     const bool got = mbar_wait_bounded(&S.meta_full[mi], (mc / NI) & 1, status, QX_DEV_TIMEOUT, deadline);
     const ItemMeta mt = S.meta[mi];
-    if (!bar_and(1, 128, got)) break;
+    if (!bar_and(B1, 128, got)) break;
     if (et == 0) mbar_arrive(&S.meta_empty[mi]);
-    ++mc;
     if (mt.kind == 0) break;
     const GroupS& gr = gs[mt.group];
     bool ok = true;
     if (mt.kind == 1 && et < gr.gsz)   // the rows' x exponents, fetched while the MMAs run
-      S.xe[et] = __ldcg(&p.xexp[ps[gr.pair_off + et].pq / p.topk]);
+      xe_s[et] = __ldcg(&p.xexp[ps[gr.pair_off + et].pq / p.topk]);
     if (mt.kind == 2 && et < gr.gsz) {
       // The group's common exponents, fetched while the MMAs run.
       ok = wait_flag(&p.ready[mt.group], 1u + p.dep_extra, status, deadline);
-      S.em[et] = __ldcg(&p.emax[gr.pair_off + et]);
+      em[et] = __ldcg(&p.emax[gr.pair_off + et]);
     }
-    const int buf = (int)(ic & 1u);
+    const int buf = eg;
     ok = mbar_wait_bounded(&S.acc_full[buf], (ic / 2) & 1, status, QX_DEV_TIMEOUT, deadline) && ok;
-    if (!bar_and(1, 128, ok)) break;
+    if (!bar_and(B1, 128, ok)) break;
     tc::fence_after_sync();
     const uint32_t tacc = tbase + lanes + (uint32_t)buf * 2u * TM_SLOT;   // issuer 1's at + TM_SLOT
     const bool two = second_acc(mt);
@@ -713,25 +721,17 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       const bool up = m >= 64;
       const int c = m & 63;
       for (int q = 0; q < gr.gsz; ++q) {
-        float v[16];
-        tc::ld16(tacc + XTERMS * q, v);
-        if (two) {
-          float v1[16];
-          tc::ld16(tacc + TM_SLOT + XTERMS * q, v1);
+        float v[16], v1[16];
+        tc::ld16x2(tacc + XTERMS * q, tacc + TM_SLOT + XTERMS * q, v, v1);   // v1 holds data only if two
 #pragma unroll
-          for (int t = 0; t < XTERMS; ++t) v[t] += v1[t];
-        }
-        const int xe = S.xe[q];
-        float s = 0.f;
-#pragma unroll
-        for (int t = XTERMS - 1; t >= 0; --t) s += v[t] * term_scale(xe, t);   // smallest terms first
-        s *= gr.g13;
+        for (int t = 0; t < XTERMS; ++t) v[t] += two ? v1[t] : 0.f;
+        const float s = tc::term_sum16(v, xe_s[q]) * gr.g13;
         if (up) xu[q * 64 + c] = s; else xg[q * 64 + c] = s;
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.acc_empty[buf]);
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
       const int col0 = mt.tile * 64;
       const int kbl = mt.tile % SK;                   // the tile is K block kbl of down stage tile / 4
       uint8_t* ab = p.ab + gr.ab_off + (size_t)(mt.tile / SK) * gr.sbs;
@@ -750,37 +750,39 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
           float mx = fabsf(a);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-          if (lane == 0) S.amx[q][half] = mx;
+          if (lane == 0) amx[q][half] = mx;
         }
-        asm volatile("bar.sync 2, 64;" ::: "memory");
-        // 16 unscaled e2m1 terms per pair with the tile's own even exponent:
-        // act = sum_t 2^(el - 2t) q_t (the same digit rule as the x terms).
-        for (int q = 0; q < gr.gsz; ++q) {
-          const int el = act_exponent(fmaxf(S.amx[q][0], S.amx[q][1]));
-          float r = xg[q * 64 + c];
-          uint8_t* blk = ab + (size_t)q * XT_STAGE + kbl * XT_KB + (c >> 5) * 128 + ((c & 31) >> 1);
-#pragma unroll 1
-          for (int t = 0; t < XTERMS; ++t) {
-            const float g = ldexpf(1.f, el - 2 * t);
-            const uint32_t code = tc::e2m1_of(r, g);
-            r = fmaf(-tc::e2m1_val(code), g, r);
-            const uint32_t w = tc::pack8(code, lane);
-            if ((lane & 7) == 0) *reinterpret_cast<uint32_t*>(blk + (t >> 3) * XT_SBO + (t & 7) * 16) = w;
-          }
-          if (c == 0) {
-            p.eloc[(size_t)(gr.pair_off + q) * p.NT + mt.tile] = el;
-            atomicMax(&p.emax[gr.pair_off + q], el);
-          }
-        }
-        __threadfence();
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
+      // 16 unscaled e2m1 terms per pair with the tile's own even exponent el:
+      // act = sum_t 2^(el - 2t) q_t (the digit rule of the x terms). Warp w of
+      // the group takes pairs w, w + 4; lane l the columns 2l, 2l + 1.
+      for (int q = et >> 5; q < gr.gsz; q += 4) {
+        const int el = act_exponent(fmaxf(amx[q][0], amx[q][1]));
+        float r0 = xg[q * 64 + 2 * lane], r1 = xg[q * 64 + 2 * lane + 1];
+        uint8_t* blk = ab + (size_t)q * XT_STAGE + kbl * XT_KB + (lane >> 4) * 128 + (lane & 12);
+        float g = tc::exp2i(el), ig = tc::exp2i(-el);
+#pragma unroll 1
+        for (int t = 0; t < XTERMS; ++t) {
+          const uint32_t w = tc::pack4(tc::digit2(r0, r1, g, ig), lane);
+          if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(blk + (t >> 3) * XT_SBO + (t & 7) * 16) = w;
+          g *= 0.25f;
+          ig *= 4.f;
+        }
+        if (lane == 0) {
+          p.eloc[(size_t)(gr.pair_off + q) * p.NT + mt.tile] = el;
+          atomicMax(&p.emax[gr.pair_off + q], el);
+        }
+      }
+      // The group's stores are ordered before thread 0's release (acq_rel) by the
+      // barrier; the group's last tile acquires them through the same counter.
+      asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
       if (et == 0) {
         const uint32_t old = atom_add_acq_rel_gpu(&p.cnt1[mt.group], 1u);
-        S.last_flag = (old == (uint32_t)p.NT - 1u) ? 1u : 0u;
+        *last_flag = (old == (uint32_t)p.NT - 1u) ? 1u : 0u;
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (S.last_flag) {
+      asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
+      if (*last_flag) {
         // Last tile of the group: bring every tile to the pair's common exponent
         // em by moving its terms d = (em - el) / 2 places down (term t becomes
         // term t + d; the last d terms, below the common precision, drop out).
@@ -793,7 +795,7 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
           const int tile = i / gr.gsz, q = i - tile * gr.gsz;
           dsh[i] = (__ldcg(&p.emax[gr.pair_off + q]) - __ldcg(&p.eloc[(size_t)(gr.pair_off + q) * p.NT + tile])) >> 1;
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
         const int ew = et >> 5, t = lane & 15, kh = lane >> 4;
         for (int i0 = 4 * ew; i0 < nit; i0 += 16) {
           int dd[4];
@@ -821,34 +823,24 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
             __stcg(wp[j], nv);
           }
         }
-        __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
         if (et == 0) st_release_gpu(&p.ready[mt.group], 1u);
       }
     } else {
       // ---- down tile: output rows [128 tile, 128 tile + 128)
       const int h = mt.tile * 128 + m;
       for (int q = 0; q < gr.gsz; ++q) {
-        float v[16];
-        tc::ld16(tacc + XTERMS * q, v);
-        if (two) {
-          float v1[16];
-          tc::ld16(tacc + TM_SLOT + XTERMS * q, v1);
+        float v[16], v1[16];
+        tc::ld16x2(tacc + XTERMS * q, tacc + TM_SLOT + XTERMS * q, v, v1);   // v1 holds data only if two
 #pragma unroll
-          for (int t = 0; t < XTERMS; ++t) v[t] += v1[t];
-        }
+        for (int t = 0; t < XTERMS; ++t) v[t] += two ? v1[t] : 0.f;
         const PairS pr = ps[gr.pair_off + q];
-        const int ea = S.em[q];
-        float s = 0.f;
-#pragma unroll
-        for (int t = XTERMS - 1; t >= 0; --t) s += v[t] * term_scale(ea, t);   // smallest terms first
-        p.y[(size_t)pr.pq * HID + h] = s * (gr.g2 * pr.tw);
+        p.y[(size_t)pr.pq * HID + h] = tc::term_sum16(v, em[q]) * (gr.g2 * pr.tw);
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.acc_empty[buf]);
     }
-    ++ic;
   }
 }
 
@@ -923,7 +915,7 @@ __global__ void __launch_bounds__(NTHR, 1) tc_decode_kernel(Params p) {
   } else if (warp == 1 || warp == 6) {
     if ((threadIdx.x & 31) == 0) mma_issuer(p, ring, S, gs, tbase, warp == 1 ? 0 : 1, status, deadline);
   } else {
-    epilogue(p, S, xg, gs, ps, tbase, status, deadline);
+    epilogue(p, S, xg, gs, ps, tbase, warp < 6 ? 0 : 1, status, deadline);
   }
   // The producer drained its copies and the issuers their tensor-core work (all
   // bounded) before returning; the epilogue's last TMEM reads are complete.
@@ -1097,7 +1089,7 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream)
   }
   // shared memory: [Smem][exchange][tables][rings: ns weight stages | ns activation stages]
   const size_t tables = (size_t)p.P * (sizeof(GroupS) + sizeof(PairS));
-  const size_t xchg = (size_t)2 * p.gmax * 64 * sizeof(float);
+  const size_t xchg = (size_t)NEPI * 2 * p.gmax * 64 * sizeof(float);
   p.x_off = (int)((sizeof(Smem) + 15) & ~size_t(15));
   p.tab_off = (int)(((size_t)p.x_off + xchg + 15) & ~size_t(15));
   p.ring_off = (int)(((size_t)p.tab_off + tables + 127) & ~size_t(127));

@@ -123,6 +123,27 @@ __device__ __forceinline__ void ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Two ld16 loads (e.g. the two issuers' accumulators) behind one wait.
+__device__ __forceinline__ void ld16x2(uint32_t ta, uint32_t tb, float (&v)[16], float (&w)[16]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%32];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31}, [%33];\n\ttcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(ta), "r"(tb)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    v[i] = __uint_as_float(r[i]);
+    w[i] = __uint_as_float(r[16 + i]);
+  }
+}
+
 // As ld16, 8 columns.
 __device__ __forceinline__ void ld8(uint32_t taddr, float (&v)[8]) {
   uint32_t r[8];
@@ -188,6 +209,49 @@ __device__ __forceinline__ uint32_t term_step(float& r, float g, uint32_t* sb) {
   r = fmaf(-e2m1_val(code), sg, r);
   *sb = b;
   return code;
+}
+
+// e2m1 codes of two values (|v| <= 6), round to nearest with ties to the even
+// code (the hardware conversion), packed as one byte: lo in bits 0-3, hi in 4-7.
+__device__ __forceinline__ uint32_t e2m1x2_of(float lo, float hi) {
+  uint32_t r;
+  asm("{ .reg .b8 b; cvt.rn.satfinite.e2m1x2.f32 b, %1, %2; cvt.u32.u8 %0, b; }" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// 2^e as a float for -126 <= e <= 127 (exact, no library call).
+__device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
+
+// One digit step of the unscaled term decomposition for two values held by one
+// thread: the byte of their e2m1 codes at scale g (ig = 1/g, both powers of two,
+// so r * ig is exact) and the exact residual update r -= code * g.
+__device__ __forceinline__ uint32_t digit2(float& r0, float& r1, float g, float ig) {
+  const uint32_t byte = e2m1x2_of(r0 * ig, r1 * ig);
+  const uint32_t h2 = e2m1x2_to_f16x2(byte);
+  r0 = fmaf(-f16lo_to_f32(h2), g, r0);
+  r1 = fmaf(-f16hi_to_f32(h2), g, r1);
+  return byte;
+}
+
+// Packs the bytes of 4 consecutive lanes into one word (lane 4j + i -> byte i);
+// the word is valid in every lane of the group.
+__device__ __forceinline__ uint32_t pack4(uint32_t byte, int lane) {
+  uint32_t w = byte << (8 * (lane & 3));
+  w |= __shfl_xor_sync(0xffffffffu, w, 1);
+  w |= __shfl_xor_sync(0xffffffffu, w, 2);
+  return w;
+}
+
+// Sum of 16 term accumulators, sum_t v[t] 2^(e - 2t), smallest term first
+// (-90 <= e <= 100, so every scale is a normal float).
+__device__ __forceinline__ float term_sum16(const float (&v)[16], int e) {
+  float g = exp2i(e - 30), s = 0.f;
+#pragma unroll
+  for (int t = 15; t >= 0; --t) {
+    s = fmaf(v[t], g, s);
+    g *= 4.f;
+  }
+  return s;
 }
 
 // Packs the codes of 8 consecutive lanes into one word (lane 8j + i -> nibble i);
