@@ -15,9 +15,9 @@
 // the epilogue.
 //
 // Kernels, chained with programmatic dependent launch:
-//   tc_prep_kernel     one CTA per (row, 256-element chunk): the reference
+//   tc_prep_kernel     one CTA per (row, 512-element chunk): the reference
 //                      ingest, the row's exponent, the chunk's 16 x terms in the
-//                      row-major operand layout (one 2,048-byte block per row and
+//                      row-major operand layout (one 4,096-byte block per row and
 //                      stage); CTA 0 also resets the call's counters and checks the
 //                      ids. Independent of the routing, so it runs while the
 //                      decode kernel starts.
@@ -26,14 +26,14 @@
 //                      experts, groups of <= 6 routed pairs of one expert, the
 //                      item counts; deterministic, so all CTAs agree), then
 //                      warp 0    producer: streams each item's weight tile (bulk async
-//                                copy, 4 K blocks = 18,432 bytes per stage) and
+//                                copy, 8 K blocks = 36,864 bytes per stage) and
 //                                activation operand into a shared-memory ring; the
 //                                first item is the CTA's index and its weights are
 //                                in flight before the prep kernel is waited for,
 //                                later items come from one atomic queue;
 //                      warps 1, 6  MMA issuers: each copies its K blocks' scale atoms
 //                                into TMEM and issues one M=128 x N x K=64
-//                                block-scaled MMA per K block (blocks 0-1 / 2-3 of
+//                                block-scaled MMA per K block (blocks 0-3 / 4-7 of
 //                                every stage) into its own accumulator;
 //                      warps 2-5 epilogue: gate/up items -> SwiGLU -> the pair's
 //                                activation terms for the down projection
@@ -62,9 +62,9 @@ constexpr int HID = QX_HIDDEN;                 // 5120
 constexpr int KB1 = HID / 64;                  // 80 K blocks in a gate/up item
 constexpr int XTERMS = 16;                     // activation terms = B rows per pair (both item kinds)
 constexpr int GMAX = 6;                        // routed pairs per group (gate/up N = 16 x 6 = 96)
-constexpr int SK = 4;                          // K blocks per stage
+constexpr int SK = 8;                          // K blocks per stage (36,864-byte weight copies)
 constexpr int A_KB = 128 * tc::ROWB + tc::SF_ATOM;  // 4608 weight bytes per K block
-constexpr int A_STAGE = SK * A_KB;             // 18432
+constexpr int A_STAGE = SK * A_KB;             // 36864
 constexpr int HT = HID / 128;                  // 40 output-row tiles in a down item set
 constexpr int MAXP = QX_MAX_ROWS * QX_MAX_TOPK;
 constexpr int MAXE = 4096;
@@ -76,19 +76,21 @@ static_assert(NI % 2 == 0, "epilogue groups alternate meta entries");
 // never holds up the next item's accumulator).
 constexpr int NTHR = 352;
 constexpr int NEPI = 2;                        // epilogue warpgroups
-// Two MMA issuer warps split every stage: K blocks 0-1 go to issuer 0, 2-3 to
+// Two MMA issuer warps split every stage: K blocks 0-3 go to issuer 0, 4-7 to
 // issuer 1, each into its own accumulator (summed in the epilogue); one thread
 // cannot issue block-scaled MMAs as fast as the tensor pipe executes them.
 // TMEM columns, in four 128-column slots (accumulators use the first 96):
 //   accumulator (buffer b, issuer i) at 256 b + 128 i;
-//   in the 32-column gaps: the constant all-1.0 scale atom of every gate/up
-//   MMA (two atoms: operand rows 0..127, 128..255) at 96; the scale atoms of
-//   issuer i's K blocks of a stage, in two banks alternating by stage (weights
-//   at +0/+4, down activations at +8/+12) at 224 + 128 i + 16 bank. A stage's
-//   scale copies are issued before its MMAs into the bank the previous stage's
-//   MMAs do not read, so no MMA waits on the copy just before it.
+//   in the 32-column gaps: the constant all-1.0 scale atom of every activation
+//   operand at 96 (two atoms: operand rows 0..127, 128..255); the weight scale
+//   atoms of issuer i's 4 K blocks of a stage (4 columns each), in two banks
+//   alternating by stage, at 224 + 128 i + 16 bank. A stage's scale copies are
+//   issued before its MMAs into the bank the previous stage's MMAs do not read,
+//   so no MMA waits on the copy just before it. Every scale operand starts on a
+//   4-column boundary, as block-scaled MMAs require.
 constexpr uint32_t TM_COLS = 512, TM_SLOT = 128, TM_ONE = 96, TM_SF = 224, TM_BANK = 16;
 constexpr int NISS = 2, KB_PER_ISS = SK / NISS;
+static_assert(KB_PER_ISS * 4 <= (int)TM_BANK, "a stage's scale atoms fit one bank");
 static_assert(GMAX * XTERMS <= 96, "an accumulator fits its slot");
 constexpr int XE_LO = -90, XE_HI = 100;      // x exponents
 constexpr int AE_LO = -90, AE_HI = 100;      // SwiGLU-output exponents (even)
@@ -143,7 +145,7 @@ struct Params {
   int32_t* emax;      // [P] per group position: common activation exponent
   int32_t* eloc;      // [P][NT] per group position and tile: tile exponent
   int32_t* xexp;      // [rows]
-  uint8_t* xt;        // [rows][20 stages][2048 bytes]: x terms, row-major
+  uint8_t* xt;        // [rows][10 stages][4096 bytes]: x terms, row-major
   uint8_t* ab;        // per group: ceil(NT/4) stages of sbs bytes (SwiGLU-output terms)
   float* y;           // [P][HID]
   int x_off;          // shared-memory offset of the SwiGLU exchanges (per epilogue group 2 x gmax x 64 floats)
@@ -165,15 +167,15 @@ struct ItemMeta {
 __host__ __device__ inline size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
 
 // Activation operands (16 x gsz rows of e2m1 terms, codes only; the B-side
-// scales are the constant 1.0 atom). x terms are kept row-major, one 2,048-byte
-// block per row and stage laid out [row group 2][K block 4][K half 2][8 terms]
+// scales are the constant 1.0 atom). x terms are kept row-major, one 4,096-byte
+// block per row and stage laid out [row group 2][K block 8][K half 2][8 terms]
 // [16 bytes]. A group's stage is its pairs' blocks side by side (pair q at
-// 2,048 q), so operand row group j sits at 1,024 j: one MMA per K block with
-// leading offset 128 and stride 1,024 reads all of the group's rows, and the
-// gate/up stage is gsz copies of 2,048 bytes. The SwiGLU-output terms of a group
-// (down items) use the same stage layout, one copy of gsz x 2,048 bytes.
-constexpr int XT_STAGE = 2048;                 // term bytes per pair (row) and stage
-constexpr uint32_t XT_SBO = 1024;              // row group to row group
+// 4,096 q), so operand row group j sits at 2,048 j: one MMA per K block with
+// leading offset 128 and stride 2,048 reads all of the group's rows, and the
+// gate/up stage is gsz copies of 4,096 bytes. The SwiGLU-output terms of a group
+// (down items) use the same stage layout, one copy of gsz x 4,096 bytes.
+constexpr int XT_STAGE = SK * 512;             // term bytes per pair (row) and stage
+constexpr uint32_t XT_SBO = SK * 256;          // row group to row group
 constexpr uint32_t XT_KB = 256;                // K block to K block
 
 struct WsLayout {
@@ -225,8 +227,9 @@ __device__ __forceinline__ int x_exponent(float amax) {
   return e;
 }
 
-constexpr int XCH = 256;                 // activation elements per x-term unit
-constexpr int NXCH = HID / XCH;          // 20 units per row
+constexpr int XCH = SK * 64;             // activation elements per x-term unit (one stage)
+constexpr int NXCH = HID / XCH;          // 10 units per row
+constexpr int PREP_THR = XCH / 2;        // prep threads per unit: two elements each
 
 // The reference's bf16 activation value of element k (gx/gx_ingest.py:151-154).
 __device__ __forceinline__ float ingest_one(const Params& p, const uint8_t* xr, int k, float inv) {
@@ -235,12 +238,12 @@ __device__ __forceinline__ float ingest_one(const Params& p, const uint8_t* xr, 
   return __bfloat162float(__float2bfloat16_rn(__fmul_rn(f16lo_to_f32(f2), inv)));
 }
 
-// max |x| over one row, by the 128 epilogue threads (5 KB of L2 reads); red: 4 floats
-// of shared memory. Every thread gets the result.
-__device__ float row_amax128(const Params& p, const uint8_t* xr, float inv, float* red, int tid) {
+// max |x| over one row (5 KB of L2 reads) by the PREP_THR threads of a prep
+// CTA; red: PREP_THR / 32 floats of shared memory. Every thread gets the result.
+__device__ float row_amax(const Params& p, const uint8_t* xr, float inv, float* red, int tid) {
   float amax = 0.f;
   if (p.x_fmt == QX_X_BF16) {
-    for (int u = tid; u < HID / 8; u += 128) {
+    for (int u = tid; u < HID / 8; u += PREP_THR) {
       const uint4 w = *reinterpret_cast<const uint4*>(xr + (size_t)u * 16);
       const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -250,14 +253,15 @@ __device__ float row_amax128(const Params& p, const uint8_t* xr, float inv, floa
       }
     }
   } else {
-    uint4 wv[3];                            // all loads first (320 units over 128 threads)
+    constexpr int NW = (HID / 16 + PREP_THR - 1) / PREP_THR;
+    uint4 wv[NW];                           // all loads first
 #pragma unroll
-    for (int i = 0; i < 3; ++i) {
-      const int u = tid + 128 * i;
+    for (int i = 0; i < NW; ++i) {
+      const int u = tid + PREP_THR * i;
       wv[i] = u < HID / 16 ? *reinterpret_cast<const uint4*>(xr + (size_t)u * 16) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < NW; ++i) {
       const uint32_t ww[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -273,9 +277,10 @@ __device__ float row_amax128(const Params& p, const uint8_t* xr, float inv, floa
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   if ((tid & 31) == 0) red[tid >> 5] = amax;
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  const float m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  asm volatile("bar.sync 1, 128;" ::: "memory");   // red may be reused after this
+  __syncthreads();
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < PREP_THR / 32; ++i) m = fmaxf(m, red[i]);
   return m;
 }
 
@@ -405,18 +410,18 @@ __device__ void route_local(const Params& p, int* scr, GroupS* gs, PairS* ps, Ro
   __syncwarp();
 }
 
-// One CTA per unit (row r, 256-element chunk c = stage c of the gate/up
+// One CTA per unit (row r, 512-element chunk c = stage c of the gate/up
 // operand): the reference ingest of row r, its exponent E (every unit of the
 // row computes the same), and the chunk's 16 unscaled x terms
 // q_t = rne(r_t / 2^(E - 2t)) (two elements per thread) into the row's stage
 // block. CTA 0 also resets the call's counters and records bad ids.
-__global__ void __launch_bounds__(128) tc_prep_kernel(Params p) {
-  __shared__ float red[4];
+__global__ void __launch_bounds__(PREP_THR) tc_prep_kernel(Params p) {
+  __shared__ float red[PREP_THR / 32];
   pdl_launch_dependents();
   const int tid = threadIdx.x, lane = tid & 31;
   if (blockIdx.x == 0) {
     bool bad = false;
-    for (int q = tid; q < p.P; q += 128) {
+    for (int q = tid; q < p.P; q += PREP_THR) {
       const long long id = p.ids64 ? reinterpret_cast<const long long*>(p.ids)[q]
                                    : (long long)reinterpret_cast<const int*>(p.ids)[q];
       bad |= !(id == -1 || (id >= 0 && id < p.E));
@@ -426,7 +431,7 @@ __global__ void __launch_bounds__(128) tc_prep_kernel(Params p) {
     }
     bad = __syncthreads_or(bad);
     uint32_t* c = reinterpret_cast<uint32_t*>(p.ctl);
-    for (int i = tid; i < (int)(sizeof(Ctl) / 4); i += 128) c[i] = 0;
+    for (int i = tid; i < (int)(sizeof(Ctl) / 4); i += PREP_THR) c[i] = 0;
     __syncthreads();
     if (tid == 0 && bad) p.ctl->status = (uint32_t)QX_DEV_BAD_ID;
   }
@@ -435,11 +440,11 @@ __global__ void __launch_bounds__(128) tc_prep_kernel(Params p) {
   if (p.x_fmt == QX_X_E4M3) inv = p.x_scale[r];
   else if (p.x_fmt == QX_X_E4M3_POST) inv = p.x_scale[0];
   const uint8_t* xr = reinterpret_cast<const uint8_t*>(p.x) + (size_t)r * p.x_stride;
-  // Thread tid owns elements k, k + 1 (k = 256 c + 2 tid): warp w is K block w
+  // Thread tid owns elements k, k + 1 (k = XCH c + 2 tid): warp w is K block w
   // of the stage, lane l its columns 2l, 2l + 1.
   const int k = c * XCH + 2 * tid;
   float v0 = ingest_one(p, xr, k, inv), v1 = ingest_one(p, xr, k + 1, inv);
-  const int e = x_exponent(row_amax128(p, xr, inv, red, tid));
+  const int e = x_exponent(row_amax(p, xr, inv, red, tid));
   if (c == 0 && tid == 0) p.xexp[r] = e;
   uint8_t* blk = p.xt + ((size_t)r * NXCH + c) * XT_STAGE + (tid >> 5) * XT_KB + (lane >> 4) * 128 + (lane & 12);
   float g = tc::exp2i(e), ig = tc::exp2i(-e);
@@ -733,7 +738,7 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       if (lane == 0) mbar_arrive(&S.acc_empty[buf]);
       asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
       const int col0 = mt.tile * 64;
-      const int kbl = mt.tile % SK;                   // the tile is K block kbl of down stage tile / 4
+      const int kbl = mt.tile % SK;                   // the tile is K block kbl of down stage tile / SK
       uint8_t* ab = p.ab + gr.ab_off + (size_t)(mt.tile / SK) * gr.sbs;
       if (!up) {
         // SwiGLU per pair, |act| maxima per half tile
@@ -1102,7 +1107,7 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream)
   const size_t smem_bytes = SMEM_LIMIT;
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  tc_prep_kernel<<<a->rows * NXCH, 128, 0, st>>>(p);
+  tc_prep_kernel<<<a->rows * NXCH, PREP_THR, 0, st>>>(p);
   if (cudaGetLastError() != cudaSuccess) return QX_ERR_LAUNCH;
 
   cudaLaunchAttribute attr[1];

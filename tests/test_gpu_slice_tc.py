@@ -25,16 +25,16 @@ def ws_offsets(rows, topk, width):
     p, nt = rows * topk, (width + 63) // 64
     o, off = 0, {}
     for name, size in [("ctl", 256), ("cnt1", p * 4), ("ready", p * 4), ("emax", p * 4), ("eloc", p * nt * 4),
-                       ("xexp", rows * 4), ("xt", rows * 20 * 2048)]:
+                       ("xexp", rows * 4), ("xt", rows * 10 * 4096)]:
         off[name] = o
         o = _al(o + size)
     return off
 
 
 def _kb_unpack(blk, kb):
-    """K block kb of one row's 16 x terms from that row's 2,048-byte stage block
-    ([row group 2][K block 4][K half 2][term 8][16 bytes]) -> nibbles [16 terms, 64]."""
-    b = blk.reshape(2, 4, 2, 8, 16)[:, kb % 4]                        # rg, half, term, byte
+    """K block kb of one row's 16 x terms from that row's 4,096-byte stage block
+    ([row group 2][K block 8][K half 2][term 8][16 bytes]) -> nibbles [16 terms, 64]."""
+    b = blk.reshape(2, 8, 2, 8, 16)[:, kb % 8]                        # rg, half, term, byte
     nib = torch.stack([b & 15, b >> 4], dim=-1)                       # rg, half, term, byte, nibble
     return nib.permute(0, 2, 1, 3, 4).reshape(16, 64)
 
@@ -63,8 +63,8 @@ def test_x_terms_match_cpu_model(cuda_ready, rows, seed):
     assert torch.equal(xexp, e), (xexp, e)
     for r in range(rows):
         for kb in range(80):
-            base = off["xt"] + (r * 20 + kb // 4) * 2048
-            got = _kb_unpack(w[base:base + 2048], kb)
+            base = off["xt"] + (r * 10 + kb // 8) * 4096
+            got = _kb_unpack(w[base:base + 4096], kb)
             want = codes[r, :, kb * 64:(kb + 1) * 64]
             assert torch.equal(got, want), f"row {r} K block {kb}"
     rec_x = NT.reconstruct_x(codes, e)
