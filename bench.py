@@ -124,7 +124,7 @@ def run_ours(args) -> dict | None:
     from qmesh_b200.arena import Arena
     from qmesh_b200.combine import combine_ordered
     from qmesh_b200.expert_slice import alloc_workspace, launch
-    from qmesh_b200.shard import combine_across_ranks, shard_range
+    from qmesh_b200.shard import P2PExchange, combine_across_ranks, shard_range
     build.build()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -149,7 +149,13 @@ def run_ours(args) -> dict | None:
     uniq = [len(set(ids.flatten().tolist())) for _, _, ids, _ in draws]
     ws = alloc_workspace(rows, TOPK, a0, a1, dev, args.layout)
     part = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
-    gathered = [torch.empty_like(part) for _ in range(world)] if world > 1 else None
+    gathered = [torch.empty_like(part) for _ in range(world)] if world > 1 and args.xchg == "nccl" else None
+    xchg = P2PExchange(rows_max=rows, dst=0, device=dev) if world > 1 and args.xchg == "p2p" else None
+
+    def exchange(p: torch.Tensor) -> torch.Tensor | None:
+        if xchg is not None:
+            return xchg.combine(p, out=out)
+        return combine_across_ranks(p, dst=0, out=out, combine=combine_ordered, gathered=gathered)
     out = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
     views = [ar.view(li) for li in range(layers)]
     stream = torch.cuda.current_stream(dev)
@@ -159,7 +165,7 @@ def run_ours(args) -> dict | None:
         launch(views[i % layers], q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=stream.cuda_stream,
                layout=args.layout)
         if world > 1:
-            combine_across_ranks(part, dst=0, out=out, combine=combine_ordered, gathered=gathered)
+            exchange(part)
 
     for i in range(args.warmup):
         step(i)
@@ -198,7 +204,7 @@ def run_ours(args) -> dict | None:
         launch(views[i % layers], dev_in[0], dev_in[2], dev_in[3], part, a0, a1, ws, x_scale=dev_in[1],
                stream=stream.cuda_stream, layout=args.layout)
         if world > 1:
-            if combine_across_ranks(part, dst=0, out=out, combine=combine_ordered, gathered=gathered) is not None:
+            if exchange(part) is not None:
                 out_h.copy_(out, non_blocking=True)
         else:
             out_h.copy_(part, non_blocking=True)
@@ -257,6 +263,9 @@ def run_ours(args) -> dict | None:
                        "routing_draws": args.draws, "mean_unique_experts": round(mean_u, 2),
                        "l2": "inputs larger than L2: ~%.0f MB of expert weights per step" % (mean_u * EXPERT_BYTES / 1e6),
                        "parallelism": f"column-split tp{world}",
+                       "exchange": None if world == 1 else (
+                           "one-shot NVLink store + rank-ordered FP32 sum kernel" if args.xchg == "p2p"
+                           else "NCCL all-gather + rank-ordered FP32 sum kernel"),
                        "kernel": "tcgen05 mxf4nvf4 (16-term e2m1 activations)" if args.layout == "tc"
                        else "register dequant + mma.sync"},
             "tokens_per_s": round(rows / (us_layer * 1e-6), 1),
@@ -274,6 +283,8 @@ def run_ours(args) -> dict | None:
         if world == 1 and not args.no_cpu:
             res["cpu_baseline"] = cpu_baseline(draws, ar, rows, a0, a1, args.cpu_layers)
     if world > 1:
+        if xchg is not None:
+            xchg.close()
         dist.barrier()
         dist.destroy_process_group()
     return res
@@ -350,6 +361,8 @@ def main() -> int:
     ap.add_argument("--draws", type=int, default=16)
     ap.add_argument("--cpu-layers", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--xchg", default="p2p", choices=["p2p", "nccl"],
+                    help="N>1 combine: one-shot NVLink kernel (p2p) or NCCL all-gather + combine kernel")
     ap.add_argument("--layout", default="tc", choices=["tc", "frag"],
                     help="arena layout / kernel: tc = tcgen05 block-scaled MMA, frag = register dequant + mma.sync")
     args = ap.parse_args()

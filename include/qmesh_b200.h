@@ -136,6 +136,41 @@ int qx_combine_ordered(const uint16_t* const* parts, int32_t n_parts, int64_t pa
                        void* out, int64_t out_stride, int32_t out_f32, int32_t rows,
                        void* stream);
 
+/* ---- one-shot combine over peer memory (NVLink) ------------------------------
+ * Replaces the reference's RDMA seam (native/qmesh_afd_seam.cu:309-361,
+ * qmesh_afd_edge/peer transport) inside one box: every rank's BF16 partial is
+ * stored straight into the output rank's receive slot over NVLink, and the
+ * output rank sums the partials in FP32 in rank order (then `shared`, if given)
+ * with one BF16 rounding. Setup: each rank allocates its exchange buffer
+ * (qx_xchg_alloc, zero-filled), exports it (qx_ipc_handle), the ranks swap the
+ * 64-byte handles (e.g. torch.distributed.all_gather_object) and open the
+ * others' buffers (qx_ipc_open). Every rank then calls qx_combine_p2p once per
+ * step with the same rank order, on its own stream; calls are graph-capturable.
+ * Waits on peers are bounded (QX_TIMEOUT_MS); a timeout sets QX_DEV_TIMEOUT in
+ * *status and leaves the exchange unusable (recreate it). */
+#define QX_XCHG_MAX_RANKS 8
+#define QX_IPC_HANDLE_BYTES 64
+
+typedef struct QxXchgArgs {
+  void*        bufs[QX_XCHG_MAX_RANKS]; /* every rank's exchange buffer in this process (own included) */
+  const void*  part;        /* this rank's BF16 partial [rows, 5120] */
+  int64_t      part_stride; /* elements */
+  const void*  shared;      /* output rank only, optional: BF16 [rows, 5120] added after the ranks */
+  int64_t      shared_stride;
+  void*        out;         /* output rank only: BF16 [rows, 5120] */
+  int64_t      out_stride;
+  uint32_t*    status;      /* device word: QX_DEV_TIMEOUT on a wait that ran out */
+  int32_t      rank, world, dst, rows, rows_max;
+} QxXchgArgs;
+
+size_t qx_xchg_bytes(int32_t rows_max);
+int qx_xchg_alloc(int32_t rows_max, void** buf);
+int qx_xchg_free(void* buf);
+int qx_ipc_handle(const void* buf, void* handle);   /* handle: QX_IPC_HANDLE_BYTES bytes */
+int qx_ipc_open(const void* handle, void** buf);
+int qx_ipc_close(void* buf);
+int qx_combine_p2p(const QxXchgArgs* args, void* stream);
+
 /* Read the device status words of a workspace (host copy, synchronous on
  * `stream`): bit set of QX_DEV_*. */
 int qx_status_read(const void* workspace, uint32_t* status, void* stream);
@@ -145,8 +180,9 @@ int qx_status_read(const void* workspace, uint32_t* status, void* stream);
  * layout: w13 [E][ceil(W/64)][80][4608 B], w2 [E][40][ceil(W/64)][4608 B] for
  * arena width W = a1 - a0 (each 4608-byte K block = a 128-row x 64-element
  * operand tile, then its 512-byte scale atom; columns past a1 are zero). The
- * activations enter the MMA as eight residual NVFP4 terms, so results stay
- * within the same tolerance of the reference's FP32 arithmetic. Requires
+ * activations enter the MMA as 16 residual e2m1 terms (to 2^-30 of their
+ * maximum), so results stay within the same tolerance of the reference's FP32
+ * arithmetic. Requires
  * (c0 - a0) % 64 == 0 and c1 % 32 == 0. Replaces the same reference body as
  * qx_slice_decode (gx/kernels/ext_variant.cu:11-24). */
 size_t qx_arena_tc_w13_bytes(int32_t n_experts, int32_t width);

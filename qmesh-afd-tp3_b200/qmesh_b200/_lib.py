@@ -80,6 +80,28 @@ class QxSliceArgs(ctypes.Structure):
     ]
 
 
+XCHG_MAX_RANKS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class QxXchgArgs(ctypes.Structure):
+    _fields_ = [
+        ("bufs", ctypes.c_void_p * XCHG_MAX_RANKS),
+        ("part", ctypes.c_void_p),
+        ("part_stride", ctypes.c_int64),
+        ("shared", ctypes.c_void_p),
+        ("shared_stride", ctypes.c_int64),
+        ("out", ctypes.c_void_p),
+        ("out_stride", ctypes.c_int64),
+        ("status", ctypes.c_void_p),
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("dst", ctypes.c_int32),
+        ("rows", ctypes.c_int32),
+        ("rows_max", ctypes.c_int32),
+    ]
+
+
 # (name, restype, argtypes) of every exported entry point in include/qmesh_b200.h
 SIGNATURES = [
     ("qx_arena_w13_bytes", ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32]),
@@ -104,6 +126,13 @@ SIGNATURES = [
     ("qx_diag_nvf4_tile", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
       ctypes.c_void_p, ctypes.c_void_p]),
+    ("qx_xchg_bytes", ctypes.c_size_t, [ctypes.c_int32]),
+    ("qx_xchg_alloc", ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p)]),
+    ("qx_xchg_free", ctypes.c_int, [ctypes.c_void_p]),
+    ("qx_ipc_handle", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    ("qx_ipc_open", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    ("qx_ipc_close", ctypes.c_int, [ctypes.c_void_p]),
+    ("qx_combine_p2p", ctypes.c_int, [ctypes.POINTER(QxXchgArgs), ctypes.c_void_p]),
     ("qx_version", ctypes.c_char_p, []),
 ]
 

@@ -56,3 +56,97 @@ def combine_across_ranks(part: torch.Tensor, group=None, dst: int = 0, shared: t
     if shared is not None:
         parts = list(parts) + [shared]
     return combine(parts, out=out)
+
+
+class P2PExchange:
+    """One-shot rank-ordered combine over NVLink peer memory (`qx_combine_p2p`).
+
+    The B200 replacement of the reference's RDMA seam between the column-split
+    nodes (native/qmesh_afd_seam.cu:309-361): each rank's BF16 partial is stored
+    straight into the output rank's receive slot, and the output rank sums the
+    partials in FP32 in rank order (then `shared`) with one BF16 rounding, the
+    same result as `combine_across_ranks`. Setup exchanges CUDA IPC handles
+    through `torch.distributed` (one collective); each step is one kernel per
+    rank and no collective. Every rank must call `combine` once per step, in
+    the same order; `close` (collective) releases the mappings.
+    """
+
+    def __init__(self, rows_max: int, group=None, dst: int = 0, device: torch.device | None = None):
+        import ctypes
+
+        from . import _lib
+        self._ct = ctypes
+        self._lib = _lib.load()
+        self._L = _lib
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.dst = dst
+        self.rows_max = rows_max
+        if self.world > _lib.XCHG_MAX_RANKS:
+            raise ValueError(f"at most {_lib.XCHG_MAX_RANKS} ranks")
+        if not 0 <= dst < self.world:
+            raise ValueError(f"output rank {dst} outside world {self.world}")
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        own = ctypes.c_void_p()
+        _lib.check(self._lib.qx_xchg_alloc(rows_max, ctypes.byref(own)), "qx_xchg_alloc")
+        self._own = own.value
+        handle = (ctypes.c_char * _lib.IPC_HANDLE_BYTES)()
+        _lib.check(self._lib.qx_ipc_handle(ctypes.c_void_p(self._own), handle), "qx_ipc_handle")
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened: list[int] = []
+        bufs = []
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                bufs.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            _lib.check(self._lib.qx_ipc_open(hb, ctypes.byref(p)), "qx_ipc_open")
+            bufs.append(p.value)
+            self._opened.append(p.value)
+        self._args = _lib.QxXchgArgs()
+        for r, b in enumerate(bufs):
+            self._args.bufs[r] = b
+        self._args.rank, self._args.world, self._args.dst = self.rank, self.world, dst
+        self._args.rows_max = rows_max
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._args.status = self.status.data_ptr()
+        dist.barrier(group=group)   # every rank has mapped every buffer before the first step
+
+    def combine(self, part: torch.Tensor, out: torch.Tensor | None = None, shared: torch.Tensor | None = None,
+                stream=None) -> torch.Tensor | None:
+        """Sends this rank's partial; on the output rank returns bf16(p0 + ... [+ shared])."""
+        if part.dtype != torch.bfloat16 or part.dim() != 2 or part.shape[1] != self._L.HIDDEN or part.stride(1) != 1:
+            raise TypeError("partial must be bf16 [rows, 5120] with unit column stride")
+        rows = part.shape[0]
+        if not 1 <= rows <= self.rows_max:
+            raise ValueError(f"rows {rows} outside 1..{self.rows_max}")
+        a = self._args
+        a.part, a.part_stride, a.rows = part.data_ptr(), part.stride(0), rows
+        a.shared, a.shared_stride, a.out, a.out_stride = None, 0, None, 0
+        if self.rank == self.dst:
+            if out is None:
+                out = torch.empty(rows, self._L.HIDDEN, dtype=torch.bfloat16, device=part.device)
+            a.out, a.out_stride = out.data_ptr(), out.stride(0)
+            if shared is not None:
+                if shared.dtype != torch.bfloat16 or shared.shape != part.shape or shared.stride(1) != 1:
+                    raise TypeError("shared partial must be bf16 like the partial")
+                a.shared, a.shared_stride = shared.data_ptr(), shared.stride(0)
+        if stream is None:
+            stream = torch.cuda.current_stream(part.device).cuda_stream
+        self._L.check(self._lib.qx_combine_p2p(self._ct.byref(a), self._ct.c_void_p(stream)), "qx_combine_p2p")
+        return out if self.rank == self.dst else None
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers, then free this rank's own."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            self._L.check(self._lib.qx_ipc_close(self._ct.c_void_p(p)), "qx_ipc_close")
+        self._opened = []
+        dist.barrier(group=self.group)
+        self._L.check(self._lib.qx_xchg_free(self._ct.c_void_p(self._own)), "qx_xchg_free")
+        self._own = None
