@@ -16,6 +16,13 @@ third-party function it calls) on the CPU; nothing is restated here:
 * ingest.npz    gx/gx_ingest.py ``_ingest`` Triton kernel run by Triton's CPU
                 interpreter: e4m3 slab * header inv -> bf16 x, id sanitising.
 * arena.json    gx/gx_expert_worker.py ``Arena.bytes_per_layer`` for CP=896.
+* prefill_quant.npz
+                vLLM ``ref_nvfp4_quant`` (nvfp4_emulation_utils.py): the NVFP4
+                activation quantiser of the reference's W4A4 prefill body
+                (scaled_fp4_experts_quant, gx/gx_ingest.py:225-237), on rows with
+                zero blocks, ties and a range of magnitudes and global scales; and
+                ``SiluAndMulWithClamp.forward_native`` (the clamp SwiGLU of
+                gx/gx_ingest.py:235) on bf16 gate/up values.
 """
 
 from __future__ import annotations
@@ -72,6 +79,8 @@ def main(ref: str) -> None:
     sw = gxw.swiglu(h.to(torch.bfloat16), 64)
     np.savez_compressed(HERE / "swiglu.npz", h=h.to(torch.bfloat16).float().numpy(), out=sw.numpy())
 
+    make_prefill_fixture(torch.Generator().manual_seed(17))
+
     # ---- arena size accounting -------------------------------------------------------
     a = gxw.Arena.__new__(gxw.Arena)
     a.cp = gxw.CP
@@ -82,6 +91,32 @@ def main(ref: str) -> None:
     import subprocess
     env = dict(os.environ, TRITON_INTERPRET="1")
     subprocess.run([sys.executable, __file__, ref, "--ingest"], env=env, check=True)
+
+
+def make_prefill_fixture(g) -> None:
+    import types
+
+    import torch
+    from vllm.model_executor.layers.activation import SiluAndMulWithClamp
+    from vllm.model_executor.layers.quantization.utils.nvfp4_emulation_utils import ref_nvfp4_quant
+    x = torch.randn(6, 256, generator=g)
+    x[0] *= 1e-3
+    x[1] *= 40.0
+    x[2, :16] = 0.0                                            # an all-zero block
+    x[3, :16] = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0] * 2)   # grid midpoints
+    x[4] = torch.randn(256, generator=g).to(torch.bfloat16).float()
+    x[5] = torch.exp(torch.randn(256, generator=g) * 3) * torch.sign(torch.randn(256, generator=g))
+    out = {"x": x.numpy()}
+    for i, gs in enumerate([3.0, 6.0 / float(x.abs().max()), 0.02, 1e4]):
+        codes, scale = ref_nvfp4_quant(x, torch.tensor(gs, dtype=torch.float32), 16)
+        out[f"gs{i}"] = np.float32(gs)
+        out[f"codes{i}"] = codes.numpy()                        # e2m1 values (float32)
+        out[f"scale{i}"] = scale.numpy()                        # e4m3 values (float32)
+    h = (torch.randn(7, 2 * 64, generator=g) * 6).to(torch.bfloat16)
+    sw = SiluAndMulWithClamp.forward_native(types.SimpleNamespace(swiglu_limit=10.0), h.float())
+    out["swiglu_h"] = h.float().numpy()
+    out["swiglu_out"] = sw.numpy()
+    np.savez_compressed(HERE / "prefill_quant.npz", **out)
 
 
 def make_ingest_fixture(ref: str) -> None:
@@ -122,5 +157,8 @@ if __name__ == "__main__":
     _ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     if "--ingest" in sys.argv:
         make_ingest_fixture(_ref)
+    elif "--prefill" in sys.argv:
+        import torch
+        make_prefill_fixture(torch.Generator().manual_seed(17))
     else:
         main(_ref)
