@@ -136,6 +136,21 @@ int qx_combine_ordered(const uint16_t* const* parts, int32_t n_parts, int64_t pa
                        void* out, int64_t out_stride, int32_t out_f32, int32_t rows,
                        void* stream);
 
+/* ---- prefill slice (W4A4 grouped tcgen05 block-scaled GEMM) -------------------
+ * The reference's prefill body (gx/gx_ingest.py:190-246, cutlass_body_clamped:
+ * scaled_fp4_experts_quant + cutlass_fp4_moe_mm + silu_and_mul_with_clamp):
+ * x (FP8 rows + scale, or BF16) is quantised to NVFP4 with a1g = bf16(6 / max|x|),
+ * both GEMMs run as `tcgen05.mma.kind::mxf4nvf4` over the tensor-core arena,
+ * the clamp SwiGLU output is quantised to NVFP4 with the caller's calibrated
+ * a2 (device FP32 [n_experts], gx/gx_expert_worker.py:250-283), and
+ * out = bf16(sum_j bf16(c3_j * bf16(tw_j))). Arena in the tensor-core layout;
+ * rows up to QX_PREFILL_MAX_ROWS, n_experts up to 1024; workspace from
+ * qx_prefill_workspace_bytes (256-byte aligned). Same column-range rules and
+ * status codes as qx_slice_decode_tc. */
+#define QX_PREFILL_MAX_ROWS 8192
+size_t qx_prefill_workspace_bytes(int32_t rows, int32_t topk, int32_t c0, int32_t c1, int32_t n_experts);
+int qx_slice_prefill_tc(const QxArena* arena, const QxSliceArgs* args, const float* a2, void* stream);
+
 /* ---- one-shot combine over peer memory (NVLink) ------------------------------
  * Replaces the reference's RDMA seam (native/qmesh_afd_seam.cu:309-361,
  * qmesh_afd_edge/peer transport) inside one box: every rank's BF16 partial is

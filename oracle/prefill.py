@@ -18,7 +18,7 @@ nvfp4(v, gs) is vLLM's reference NVFP4 activation quantiser
 nvfp4_emulation_utils.py, vLLM 0.22.0 in this image; the reference ran
 0.24.0): per 16 elements scale = e4m3(min(gs * (amax * f32(1/6)), 448)),
 code = e2m1_rne(clamp(v * 1/(scale * 1/gs), -6, 6)), every step in FP32 with
-correctly rounded reciprocals. Pinned by tests/golden (prefill_quant.pt).
+correctly rounded reciprocals. Pinned by tests/golden/prefill_quant.npz.
 
 The GEMM products code*scale are exact; the oracle sums them in float64 and
 rounds the scaled result once to FP32 then BF16, so it differs from any FP32
@@ -77,7 +77,7 @@ def silu_clamp(c1g: torch.Tensor, c1u: torch.Tensor, limit: float, has_limit: bo
 
 
 def slice_w4a4(x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, layer: dict, c0: int, c1: int,
-               a2, limit: float = 10.0, has_limit: bool = True) -> torch.Tensor:
+               a2, limit: float = 10.0, has_limit: bool = True, stats: dict | None = None) -> torch.Tensor:
     """BF16 partial [T, H] of the W4A4 prefill body over intermediate columns [c0, c1).
 
     x: bf16-valued float32 [T, H]; ids int [T, k] (-1 = no expert); tw float32
@@ -92,6 +92,7 @@ def slice_w4a4(x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, layer: dict
     xq = act_dequant_unscaled(xn, xs).to(torch.float64)
     a2 = torch.as_tensor(a2, dtype=torch.float32)
     y = torch.zeros(t, k, hid, dtype=torch.float32)
+    c2max = 0.0
     for e in torch.unique(ids[ids >= 0]).tolist():
         sel = (ids == e).nonzero().tolist()
         rows = [p[0] for p in sel]
@@ -103,6 +104,7 @@ def slice_w4a4(x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, layer: dict
         cg = q4.bf16_round((alpha1.double() * (xr @ wg.T)).to(torch.float32))
         cu = q4.bf16_round((alpha1.double() * (xr @ wu.T)).to(torch.float32))
         c2 = silu_clamp(cg, cu, limit, has_limit)
+        c2max = max(c2max, float(c2.abs().max()))
         an, as_ = act_quant(c2, a2e)
         aq = act_dequant_unscaled(an, as_).to(torch.float64)
         w2 = q4.dequant(layer["c2"][e][:, c0 // 2:c1 // 2], layer["s2"][e][:, c0 // 16:c1 // 16], 1.0)
@@ -114,4 +116,6 @@ def slice_w4a4(x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, layer: dict
     out = y[:, 0].clone()
     for j in range(1, k):
         out = out + y[:, j]
+    if stats is not None:
+        stats["c2_amax"] = c2max      # what the reference's a2 calibration estimates (gx_expert_worker.py:250-283)
     return q4.bf16_round(out)

@@ -41,6 +41,7 @@ QX_X_BF16 = 2
 HIDDEN = 5120
 MAX_ROWS = 64
 MAX_TOPK = 8
+PREFILL_MAX_ROWS = 8192
 STATIC_MAX_ROWS = 8
 STATIC_MAX_TOPK = 8
 STATIC_MAX_WIDTH = 2304
@@ -126,6 +127,10 @@ SIGNATURES = [
     ("qx_diag_nvf4_tile", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
       ctypes.c_void_p, ctypes.c_void_p]),
+    ("qx_prefill_workspace_bytes", ctypes.c_size_t,
+     [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+    ("qx_slice_prefill_tc", ctypes.c_int,
+     [ctypes.POINTER(QxArena), ctypes.POINTER(QxSliceArgs), ctypes.c_void_p, ctypes.c_void_p]),
     ("qx_xchg_bytes", ctypes.c_size_t, [ctypes.c_int32]),
     ("qx_xchg_alloc", ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p)]),
     ("qx_xchg_free", ctypes.c_int, [ctypes.c_void_p]),

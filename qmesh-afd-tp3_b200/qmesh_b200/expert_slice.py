@@ -46,12 +46,7 @@ def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
     return ctypes.c_void_p(t.data_ptr() if t is not None else 0)
 
 
-def launch(view: _lib.QxArena, x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, out: torch.Tensor,
-           c0: int, c1: int, workspace: torch.Tensor, x_scale: torch.Tensor | None = None,
-           swiglu_limit: float = SWIGLU_LIMIT, has_limit: bool = True, stream=None, layout: str = "tc") -> None:
-    """Validate and launch one slice call (no allocation, no host sync). `layout` is
-    the arena's: "tc" runs qx_slice_decode_tc, "frag" qx_slice_decode."""
-    lib = _lib.load()
+def _slice_args(x, ids, tw, out, c0, c1, workspace, x_scale, swiglu_limit, has_limit) -> _lib.QxSliceArgs:
     rows = x.shape[0]
     if x.dtype == torch.bfloat16:
         fmt = _lib.QX_X_BF16
@@ -76,11 +71,20 @@ def launch(view: _lib.QxArena, x: torch.Tensor, ids: torch.Tensor, tw: torch.Ten
         raise ValueError(f"hidden size must be {_lib.HIDDEN}")
     if not (ids.is_contiguous() and tw.is_contiguous()) or x.stride(1) != 1 or out.stride(1) != 1:
         raise ValueError("ids/tw must be contiguous and x/out rows unit-stride")
-    args = _lib.QxSliceArgs(
+    return _lib.QxSliceArgs(
         _ptr(x), _ptr(x_scale), x.stride(0) * esz, fmt,
         _ptr(ids), 1 if ids.dtype == torch.int64 else 0, _ptr(tw),
         rows, ids.shape[1], c0, c1, float(swiglu_limit), 1 if has_limit else 0,
         _ptr(out), out.stride(0), _ptr(workspace), workspace.numel())
+
+
+def launch(view: _lib.QxArena, x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, out: torch.Tensor,
+           c0: int, c1: int, workspace: torch.Tensor, x_scale: torch.Tensor | None = None,
+           swiglu_limit: float = SWIGLU_LIMIT, has_limit: bool = True, stream=None, layout: str = "tc") -> None:
+    """Validate and launch one slice call (no allocation, no host sync). `layout` is
+    the arena's: "tc" runs qx_slice_decode_tc, "frag" qx_slice_decode."""
+    lib = _lib.load()
+    args = _slice_args(x, ids, tw, out, c0, c1, workspace, x_scale, swiglu_limit, has_limit)
     if stream is None:
         stream = torch.cuda.current_stream(x.device).cuda_stream
     name = "qx_slice_decode_tc" if layout == "tc" else "qx_slice_decode"
@@ -140,3 +144,51 @@ def make_body(arena: Arena, swiglu_limit: float, max_rows: int = 16, topk: int =
         launch(arena.view(li), x[:r], ids[:r], tw[:r], out[:r], arena.a0, arena.a1, ws,
                swiglu_limit=limit, has_limit=has_limit, layout=arena.layout)
     return body
+
+
+# ---------------------------------------------------------------- prefill (W4A4)
+
+def prefill_workspace_bytes(rows: int, topk: int, c0: int, c1: int, n_experts: int) -> int:
+    n = _lib.load().qx_prefill_workspace_bytes(rows, topk, c0, c1, n_experts)
+    if n == 0:
+        raise ValueError(f"no prefill workspace for rows={rows} topk={topk} columns [{c0}, {c1}) E={n_experts}")
+    return n
+
+
+def alloc_prefill_workspace(rows: int, topk: int, c0: int, c1: int, n_experts: int, device) -> torch.Tensor:
+    return torch.empty(prefill_workspace_bytes(rows, topk, c0, c1, n_experts), dtype=torch.uint8, device=device)
+
+
+def launch_prefill(view: _lib.QxArena, x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, a2: torch.Tensor,
+                   out: torch.Tensor, c0: int, c1: int, workspace: torch.Tensor, x_scale: torch.Tensor | None = None,
+                   swiglu_limit: float = SWIGLU_LIMIT, has_limit: bool = True, stream=None) -> None:
+    """One W4A4 prefill slice call (qx_slice_prefill_tc): the reference's CUTLASS
+    prefill body (gx/gx_ingest.py:190-246) on the tensor-core arena. `a2` is the
+    layer's calibrated FP32 activation scale per expert ([n_experts], device)."""
+    lib = _lib.load()
+    if a2.dtype != torch.float32 or a2.dim() != 1 or a2.device != x.device:
+        raise TypeError("a2 must be a float32 [n_experts] tensor on the activations' device")
+    args = _slice_args(x, ids, tw, out, c0, c1, workspace, x_scale, swiglu_limit, has_limit)
+    if stream is None:
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+    rc = lib.qx_slice_prefill_tc(ctypes.byref(view), ctypes.byref(args), _ptr(a2), ctypes.c_void_p(stream))
+    _lib.check(rc, "qx_slice_prefill_tc")
+
+
+def prefill_slice(arena: Arena, li: int, x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, a2: torch.Tensor,
+                  c0: int | None = None, c1: int | None = None, x_scale: torch.Tensor | None = None,
+                  out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                  swiglu_limit: float = SWIGLU_LIMIT) -> torch.Tensor:
+    """BF16 [rows, 5120] partial of a prefill chunk over columns [c0, c1) (W4A4)."""
+    if arena.layout != "tc":
+        raise ValueError("the prefill slice needs a tensor-core layout arena")
+    c0 = arena.a0 if c0 is None else c0
+    c1 = arena.a1 if c1 is None else c1
+    rows = x.shape[0]
+    if out is None:
+        out = torch.empty(rows, _lib.HIDDEN, dtype=torch.bfloat16, device=x.device)
+    if workspace is None:
+        workspace = alloc_prefill_workspace(rows, ids.shape[1], c0, c1, arena.n_experts, x.device)
+    launch_prefill(arena.view(li), x, ids, tw, a2, out, c0, c1, workspace, x_scale=x_scale,
+                   swiglu_limit=max(swiglu_limit, 0.0), has_limit=swiglu_limit > 0)
+    return out
