@@ -349,6 +349,156 @@ def run_reference(args) -> dict | None:
             "e2e": {"value": round(us, 1), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+PREFILL_TOKENS = 2048
+PREFILL_A2 = 0.25   # stands in for the reference's calibrated a2 (6 / (1.5 max|c2|) on this synthetic layer)
+PREFILL_METRIC = "MoE-layer prefill µs (2048 tokens, W4A4) & NVFP4 weight GB/s, tensor TFLOP/s"
+
+
+def run_prefill(args) -> dict | None:
+    """Config 4: one prefill chunk of 2048 tokens through the W4A4 grouped tcgen05
+    GEMM (qx_slice_prefill_tc), 384 experts, uniform top-6 routing, seed 4."""
+    import torch.distributed as dist
+    from qmesh_b200 import build
+    from qmesh_b200.arena import Arena
+    from qmesh_b200.combine import combine_ordered
+    from qmesh_b200.expert_slice import alloc_prefill_workspace, launch_prefill
+    from qmesh_b200.shard import combine_across_ranks, shard_range
+    from qmesh_b200.synth import make_activation, routing
+    build.build()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+    T, E = args.tokens, args.experts
+    a0, a1 = shard_range(rank, world)
+    width = a1 - a0
+    ar = Arena(dev, 1, E, a0, a1, layout="tc")
+    ar.fill_synthetic(0, 4)
+    gen = torch.Generator().manual_seed(4)
+    ids, tw = routing(torch.randn(T, E, generator=gen), TOPK)
+    q, inv = make_activation(T, gen)
+    a2 = torch.full((E,), PREFILL_A2, dtype=torch.float32, device=dev)
+    dq, dinv, dids, dtw = q.to(dev), inv.to(dev), ids.to(dev), tw.to(dev)
+    ws = alloc_prefill_workspace(T, TOPK, a0, a1, E, dev)
+    part = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device=dev)
+    out = torch.empty_like(part)
+    gathered = [torch.empty_like(part) for _ in range(world)] if world > 1 else None
+    view = ar.view(0)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(x, xs, i_, t_) -> None:
+        launch_prefill(view, x, i_, t_, a2, part, a0, a1, ws, x_scale=xs, stream=stream.cuda_stream)
+        if world > 1:
+            combine_across_ranks(part, dst=0, out=out, combine=combine_ordered, gathered=gathered)
+
+    for _ in range(args.warmup):
+        step(dq, dinv, dids, dtw)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step(dq, dinv, dids, dtw)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    us = ms * 1e3 / args.steps
+    # end to end: H2D of the chunk's inputs from pinned memory, D2H of the output
+    host = [t_.pin_memory() for t_ in (q, inv, ids, tw)]
+    dev_in = [torch.empty_like(t_, device=dev) for t_ in host]
+    out_h = torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t_.numel() * t_.element_size() for t_ in host)
+    d2h = out_h.numel() * out_h.element_size()
+
+    def e2e_step() -> None:
+        for d_, h_ in zip(dev_in, host):
+            d_.copy_(h_, non_blocking=True)
+        step(dev_in[0], dev_in[1], dev_in[2], dev_in[3])
+        if rank == 0:
+            out_h.copy_(out if world > 1 else part, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    us_e2e = ms_e2e * 1e3 / args.steps
+    uniq = len(set(ids.flatten().tolist()))
+    alg_bytes = uniq * EXPERT_BYTES * width / INTER + T * HIDDEN + T * HIDDEN * 2
+    n_pairs = T * TOPK
+    flops = 2.0 * n_pairs * (2 * width * HIDDEN + HIDDEN * width)
+    peak, peak_kind = peaks()
+    res = None
+    if rank == 0:
+        res = {
+            "metric": PREFILL_METRIC, "value": round(us, 1), "unit": "us/layer", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 4),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "nvfp4-w/nvfp4-x (W4A4)/fp32-acc",
+            "data": "synthetic (seeded NVFP4 weights from N(0,0.02); FP8 activations from N(0,1))",
+            "config": {"workload": "config4-prefill", "experts": E, "hidden": HIDDEN, "intermediate": INTER,
+                       "tokens": T, "topk": TOPK, "columns_per_rank": width, "unique_experts": uniq,
+                       "a2": PREFILL_A2, "l2": f"inputs larger than L2: {alg_bytes / 1e9:.2f} GB of expert weights per step",
+                       "parallelism": f"column-split tp{world}",
+                       "kernel": "grouped tcgen05 mxf4nvf4 (NVFP4 x NVFP4, TMEM accumulators)"},
+            "tokens_per_s": round(T / (us * 1e-6), 1),
+            "weight_gbs": round(alg_bytes / (us * 1e-6) / 1e9, 1),
+            "tensor_tflops": round(flops / (us * 1e-6) / 1e12, 2),
+            "roofline": {"bound": "hbm", "achieved": round(alg_bytes / (us * 1e-6) / 1e9, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(alg_bytes / (us * 1e-6) / 1e9 / peak, 4),
+                         "peak_kind": peak_kind, "traffic": None, "kernel_us": round(us, 1),
+                         "alg_bytes_per_launch": int(alg_bytes), "flops_per_launch": int(flops)},
+            "e2e": {"value": round(us_e2e, 1), "unit": "us/layer", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * 6 + (args.steps if world > 1 else 0),
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu:
+            res["cpu_baseline"] = prefill_cpu_baseline(ar, q, inv, ids, tw, uniq)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res
+
+
+def prefill_cpu_baseline(ar, q, inv, ids, tw, uniq: int, n_experts: int = 3) -> dict:
+    """The W4A4 prefill body restated on the host cores (oracle.prefill), timed on
+    the pairs of a few experts and scaled by the unique experts of the chunk."""
+    from oracle import moe, nvfp4 as oq, prefill as opf
+    n = moe.cpu_threads()
+    experts = sorted(set(ids.flatten().tolist()))[:n_experts]
+    pack = ar.expert_pack(0, experts)
+    remap = {e: i for i, e in enumerate(experts)}
+    local = torch.tensor([remap.get(e, -1) for e in ids.flatten().tolist()], dtype=torch.int32).view_as(ids)
+    x = oq.fp8_ingest(q, inv)
+    t0 = time.perf_counter()
+    opf.slice_w4a4(x, local, tw, pack, 0, ar.width, torch.full((len(experts),), PREFILL_A2))
+    dt = time.perf_counter() - t0
+    us = dt / len(experts) * uniq * 1e6
+    return {"value": round(us, 1), "unit": "us/layer", "cores": n, "kind": "port",
+            "sample": f"the pairs of {len(experts)} of the chunk's {uniq} experts ({dt:.1f} s), scaled by {uniq}/{len(experts)}"}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -363,12 +513,22 @@ def main() -> int:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--xchg", default="p2p", choices=["p2p", "nccl"],
                     help="N>1 combine: one-shot NVLink kernel (p2p) or NCCL all-gather + combine kernel")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: BASELINE configs 1/2 (default); prefill: config 4 (2048-token W4A4 chunk)")
+    ap.add_argument("--tokens", type=int, default=PREFILL_TOKENS)
     ap.add_argument("--layout", default="tc", choices=["tc", "frag"],
                     help="arena layout / kernel: tc = tcgen05 block-scaled MMA, frag = register dequant + mma.sync")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    res = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if args.workload == "prefill":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the prefill reference arm is the CPU baseline "
+                              "inside the ours line (cpu_baseline)"}), flush=True)
+            return 0
+        res = run_prefill(args)
+    else:
+        res = run_reference(args) if args.impl == "reference" else run_ours(args)
     if res is not None:
         print(json.dumps(res), flush=True)
     return 0
