@@ -105,13 +105,18 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_inputs(n_draws: int, rows: int, seed: int, n_experts: int):
-    """Seeded routing (softmax top-6 of N(0,1) logits) and FP8 activations per draw."""
-    from qmesh_b200.synth import make_activation, routing
+def make_inputs(n_draws: int, rows: int, seed: int, n_experts: int, zipf: float = 0.0):
+    """Seeded routing (softmax top-6 of N(0,1) logits, plus a Zipf(s) per-expert
+    bias -s ln(rank) over a seeded permutation when zipf > 0) and FP8 activations
+    per draw."""
+    from qmesh_b200.synth import make_activation, routing, zipf_bias
     gen = torch.Generator().manual_seed(seed)
+    bias = zipf_bias(n_experts, zipf, gen) if zipf > 0 else None
     draws = []
     for _ in range(n_draws):
         logits = torch.randn(rows, n_experts, generator=gen)
+        if bias is not None:
+            logits = logits + bias
         ids, tw = routing(logits, TOPK)
         q, inv = make_activation(rows, gen)
         draws.append((q, inv, ids, tw))
@@ -144,9 +149,13 @@ def run_ours(args) -> dict | None:
     for li in range(layers):
         ar.fill_synthetic(li, seed=1000 + li)
     torch.cuda.synchronize()
-    draws = make_inputs(args.draws, rows, seed=1, n_experts=n_exp)
+    draws = make_inputs(args.draws, rows, seed=args.seed, n_experts=n_exp, zipf=args.zipf)
     dq = [(q.to(dev), inv.to(dev), ids.to(dev), tw.to(dev)) for q, inv, ids, tw in draws]
     uniq = [len(set(ids.flatten().tolist())) for _, _, ids, _ in draws]
+    if args.zipf > 0 or rows > 6:
+        workload = f"config3-spec-decode-rows{rows}" + (f"-zipf{args.zipf}" if args.zipf > 0 else "")
+    else:
+        workload = "config1-decode" if world == 1 else "config2-column-split"
     ws = alloc_workspace(rows, TOPK, a0, a1, dev, args.layout)
     part = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
     gathered = [torch.empty_like(part) for _ in range(world)] if world > 1 and args.xchg == "nccl" else None
@@ -257,10 +266,11 @@ def run_ours(args) -> dict | None:
             "vs_baseline": None,
             "dtype": "nvfp4-w/fp8-x/fp32-acc",
             "data": "synthetic (seeded NVFP4 weights from N(0,0.02); FP8 activations from N(0,1))",
-            "config": {"workload": "config1-decode" if world == 1 else "config2-column-split",
+            "config": {"workload": workload,
                        "experts": n_exp, "hidden": HIDDEN, "intermediate": INTER, "rows": rows,
                        "topk": TOPK, "columns_per_rank": width, "resident_layers": layers,
                        "routing_draws": args.draws, "mean_unique_experts": round(mean_u, 2),
+                       "zipf_s": args.zipf, "seed": args.seed,
                        "l2": "inputs larger than L2: ~%.0f MB of expert weights per step" % (mean_u * EXPERT_BYTES / 1e6),
                        "parallelism": f"column-split tp{world}",
                        "exchange": None if world == 1 else (
@@ -516,6 +526,9 @@ def main() -> int:
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
                     help="decode: BASELINE configs 1/2 (default); prefill: config 4 (2048-token W4A4 chunk)")
     ap.add_argument("--tokens", type=int, default=PREFILL_TOKENS)
+    ap.add_argument("--zipf", type=float, default=0.0,
+                    help="Zipf(s) expert bias of the routing logits (config 3: --rows 48 --zipf 1.1 --seed 3)")
+    ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--layout", default="tc", choices=["tc", "frag"],
                     help="arena layout / kernel: tc = tcgen05 block-scaled MMA, frag = register dequant + mma.sync")
     args = ap.parse_args()
