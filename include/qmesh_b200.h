@@ -40,7 +40,8 @@ enum {
 enum {
   QX_DEV_BAD_ID = 1,       /* an id outside {-1} U [0, E): that slot was skipped */
   QX_DEV_TIMEOUT = 2,      /* a bounded device wait ran out; the output is invalid */
-  QX_DEV_OVERFLOW = 4      /* more routed pairs than the workspace was sized for */
+  QX_DEV_OVERFLOW = 4,     /* more routed pairs than the workspace was sized for */
+  QX_DEV_NONFINITE = 8     /* qx_quant_fp8: a non-finite maximum; those bytes were not written */
 };
 
 /* Activation formats. */
@@ -150,6 +151,23 @@ int qx_combine_ordered(const uint16_t* const* parts, int32_t n_parts, int64_t pa
 #define QX_PREFILL_MAX_ROWS 8192
 size_t qx_prefill_workspace_bytes(int32_t rows, int32_t topk, int32_t c0, int32_t c1, int32_t n_experts);
 int qx_slice_prefill_tc(const QxArena* arena, const QxSliceArgs* args, const float* a2, void* stream);
+
+/* ---- producer side: FP8 activation quantisation and the routing front end ----
+ * qx_quant_fp8 replaces the seam's post quantiser (native/qmesh_afd_seam.cu:9-16,
+ * seam_amax_kernel / seam_finish / seam_pack_kernel :88-176): BF16 x [rows, 5120]
+ * -> e4m3 q with m = max|x|, mc = max(m, bf16(1e-6)), s = (float)(448 / (double)mc),
+ * inv = (float)(1 / (448 / (double)mc)), q = e4m3_rne_satfinite(clamp(bf16_rn(x s),
+ * +-448)); per row (inv [rows], per_post = 0) or per post (inv [1], the
+ * reference's form; `work` is one device word of scratch). A non-finite maximum
+ * leaves those bytes unwritten, sets inv = 1 and QX_DEV_NONFINITE in *status.
+ * qx_route_topk: softmax of FP32 logits [rows, n_experts], the top-k experts
+ * (larger probability first, lower id first among equals), weights renormalised
+ * to sum 1 (the router output the reference posts with each layer,
+ * afd_session.py:211-252). */
+int qx_quant_fp8(const void* x, int64_t x_stride, int32_t rows, int32_t per_post, void* q, int64_t q_stride,
+                 float* inv, uint32_t* work, uint32_t* status, void* stream);
+int qx_route_topk(const float* logits, int64_t logits_stride, int32_t rows, int32_t n_experts, int32_t topk,
+                  int32_t* ids, float* tw, void* stream);
 
 /* ---- one-shot combine over peer memory (NVLink) ------------------------------
  * Replaces the reference's RDMA seam (native/qmesh_afd_seam.cu:309-361,

@@ -150,6 +150,21 @@ def fp8_quant_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return q, inv
 
 
+def fp8_quant_post(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """The same transport with ONE scale for all rows of a post, the reference's
+    form (p7/afd_overlay/afd_session.py:106-107: scale = 448 / amax over the
+    post's rows; native/qmesh_afd_seam.cu:88-176 on the device). Returns
+    (q uint8 [R,K], inv float32 [1])."""
+    x = x.to(torch.float32)
+    m = x.abs().amax().to(torch.float64)
+    mc = torch.clamp(m, min=BF16_FLOOR)
+    sd = 448.0 / mc
+    s = sd.to(torch.float32)
+    inv = (1.0 / sd).to(torch.float32)
+    q = e4m3_encode(bf16_round(x * s))
+    return q, inv.reshape(1)
+
+
 def fp8_ingest(q: torch.Tensor, inv: torch.Tensor) -> torch.Tensor:
     """Consumer side, gx/gx_ingest.py:151-154: x = bf16(float(e4m3) * inv)."""
     v = e4m3_decode(q)

@@ -131,6 +131,12 @@ SIGNATURES = [
      [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     ("qx_slice_prefill_tc", ctypes.c_int,
      [ctypes.POINTER(QxArena), ctypes.POINTER(QxSliceArgs), ctypes.c_void_p, ctypes.c_void_p]),
+    ("qx_quant_fp8", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
+      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    ("qx_route_topk", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+      ctypes.c_void_p, ctypes.c_void_p]),
     ("qx_xchg_bytes", ctypes.c_size_t, [ctypes.c_int32]),
     ("qx_xchg_alloc", ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p)]),
     ("qx_xchg_free", ctypes.c_int, [ctypes.c_void_p]),

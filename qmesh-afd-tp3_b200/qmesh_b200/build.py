@@ -15,7 +15,7 @@ from ._lib import LIB_PATH, PKG_ROOT
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES = ["csrc/qx_decode.cu", "csrc/qx_decode_tc.cu", "csrc/qx_nvf4_tile.cu", "csrc/qx_xchg.cu",
-           "csrc/qx_prefill_tc.cu"]
+           "csrc/qx_prefill_tc.cu", "csrc/qx_front.cu"]
 HEADERS = ["csrc/qx_ptx.cuh", "csrc/qx_tc.cuh"]
 INCLUDE = PKG_ROOT.parent / "include"
 
