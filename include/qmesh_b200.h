@@ -169,6 +169,14 @@ int qx_quant_fp8(const void* x, int64_t x_stride, int32_t rows, int32_t per_post
 int qx_route_topk(const float* logits, int64_t logits_stride, int32_t rows, int32_t n_experts, int32_t topk,
                   int32_t* ids, float* tw, void* stream);
 
+/* Bounded device wait for a round driver (the counterpart of gx/gx_spin.py's
+ * spin kernel): one thread waits until the 32-bit sequence cell (host-mapped or
+ * device memory) reaches *need (a device word read when the wait runs, so one
+ * captured round graph serves every round; wrap-around order), or until
+ * timeout_ns passes, then sets QX_DEV_TIMEOUT in *status; work queued after it
+ * on the stream runs either way. */
+int qx_wait_cell(const uint32_t* cell, const uint32_t* need, uint64_t timeout_ns, uint32_t* status, void* stream);
+
 /* ---- one-shot combine over peer memory (NVLink) ------------------------------
  * Replaces the reference's RDMA seam (native/qmesh_afd_seam.cu:309-361,
  * qmesh_afd_edge/peer transport) inside one box: every rank's BF16 partial is

@@ -191,6 +191,31 @@ __global__ void __launch_bounds__(THR) route_kernel(const float* logits, int64_t
   }
 }
 
+// Round driver support: one thread waits until the sequence cell (host-mapped
+// or device memory, written by whoever publishes the layer's inputs) reaches
+// *need_p (read at run time, so a captured graph serves every round), or the
+// time limit passes; then records QX_DEV_TIMEOUT and returns, so the stream
+// (and a captured round graph) always moves on.
+__global__ void wait_cell_kernel(const uint32_t* cell, const uint32_t* need_p, uint64_t timeout_ns, uint32_t* status) {
+  const uint32_t need = *need_p;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (uint32_t it = 0;; ++it) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(cell) : "memory");
+    if ((int32_t)(v - need) >= 0) return;
+    if ((it & 31u) == 31u) {
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > timeout_ns) {
+        atomicOr(status, (uint32_t)QX_DEV_TIMEOUT);
+        return;
+      }
+    }
+    __nanosleep(256);
+  }
+}
+
 }  // namespace front
 }  // namespace qx
 
@@ -215,6 +240,12 @@ int qx_quant_fp8(const void* x, int64_t x_stride, int32_t rows, int32_t per_post
     post_amax_kernel<<<rows, THR, 0, st>>>(xb, x_stride, work);
     post_pack_kernel<<<rows, THR, 0, st>>>(xb, x_stride, qb, q_stride, work, inv, status);
   }
+  return cudaGetLastError() == cudaSuccess ? QX_OK : QX_ERR_LAUNCH;
+}
+
+int qx_wait_cell(const uint32_t* cell, const uint32_t* need, uint64_t timeout_ns, uint32_t* status, void* stream) {
+  if (!cell || !need || !status || timeout_ns == 0) return QX_ERR_ARG;
+  wait_cell_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(cell, need, timeout_ns, status);
   return cudaGetLastError() == cudaSuccess ? QX_OK : QX_ERR_LAUNCH;
 }
 

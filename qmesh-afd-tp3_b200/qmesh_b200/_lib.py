@@ -137,6 +137,8 @@ SIGNATURES = [
     ("qx_route_topk", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
       ctypes.c_void_p, ctypes.c_void_p]),
+    ("qx_wait_cell", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]),
     ("qx_xchg_bytes", ctypes.c_size_t, [ctypes.c_int32]),
     ("qx_xchg_alloc", ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p)]),
     ("qx_xchg_free", ctypes.c_int, [ctypes.c_void_p]),
