@@ -192,3 +192,81 @@ def prefill_slice(arena: Arena, li: int, x: torch.Tensor, ids: torch.Tensor, tw:
     launch_prefill(arena.view(li), x, ids, tw, a2, out, c0, c1, workspace, x_scale=x_scale,
                    swiglu_limit=max(swiglu_limit, 0.0), has_limit=swiglu_limit > 0)
     return out
+
+
+# ---------------------------------------------------------------- host-buffer calls
+
+def _al16(n: int) -> int:
+    return (n + 15) & ~15
+
+
+class HostSlice:
+    """Slice calls whose inputs and output live in host memory.
+
+    For a caller that receives a layer's activations and routing on the host (a
+    transport that lands in host memory, or a test harness): each call packs
+    x (FP8 e4m3 [rows, 5120]), its per-row FP32 scale, ids and tw into one pinned
+    staging buffer, moves them with ONE host-to-device copy, runs the slice on
+    views of the device copy and brings the BF16 output back with one
+    device-to-host copy, all on one stream and without synchronising the host.
+    Two staging slots alternate, each guarded by an event, so the host can pack
+    call k+1 while call k runs. The returned host tensor belongs to that call's
+    slot and stays valid until the call after next; read it after
+    `torch.cuda.current_stream().synchronize()` (or `done(out)`).
+    """
+
+    def __init__(self, arena: Arena, rows: int, topk: int = 6, c0: int | None = None, c1: int | None = None,
+                 swiglu_limit: float = SWIGLU_LIMIT, slots: int = 2):
+        self.arena = arena
+        self.rows, self.topk = rows, topk
+        self.c0 = arena.a0 if c0 is None else c0
+        self.c1 = arena.a1 if c1 is None else c1
+        self.limit = float(max(swiglu_limit, 0.0))
+        self.has_limit = swiglu_limit > 0
+        dev = arena.dev
+        self.o_x = 0
+        self.o_s = _al16(rows * _lib.HIDDEN)
+        self.o_i = self.o_s + _al16(rows * 4)
+        self.o_t = self.o_i + _al16(rows * topk * 4)
+        self.nbytes = self.o_t + _al16(rows * topk * 4)
+        self.host = [torch.empty(self.nbytes, dtype=torch.uint8).pin_memory() for _ in range(slots)]
+        self.dev = [torch.empty(self.nbytes, dtype=torch.uint8, device=dev) for _ in range(slots)]
+        self.out_d = [torch.empty(rows, _lib.HIDDEN, dtype=torch.bfloat16, device=dev) for _ in range(slots)]
+        self.out_h = [torch.empty(rows, _lib.HIDDEN, dtype=torch.bfloat16).pin_memory() for _ in range(slots)]
+        self.events = [torch.cuda.Event() for _ in range(slots)]
+        self.used = [False] * slots
+        self.ws = alloc_workspace(rows, topk, self.c0, self.c1, dev, arena.layout)
+        self.k = 0
+
+    def _views(self, buf: torch.Tensor, n: int):
+        x = buf[self.o_x:self.o_x + n * _lib.HIDDEN].view(n, _lib.HIDDEN)
+        s = buf[self.o_s:self.o_s + n * 4].view(torch.float32)
+        i = buf[self.o_i:self.o_i + n * self.topk * 4].view(torch.int32).view(n, self.topk)
+        t = buf[self.o_t:self.o_t + n * self.topk * 4].view(torch.float32).view(n, self.topk)
+        return x, s, i, t
+
+    def __call__(self, li: int, x: torch.Tensor, x_scale: torch.Tensor, ids: torch.Tensor,
+                 tw: torch.Tensor) -> torch.Tensor:
+        n = x.shape[0]
+        if not 1 <= n <= self.rows or ids.shape != (n, self.topk) or tw.shape != (n, self.topk):
+            raise ValueError(f"call of {n} rows / ids {tuple(ids.shape)} outside this HostSlice ({self.rows} x {self.topk})")
+        k = self.k
+        self.k = (k + 1) % len(self.host)
+        if self.used[k]:
+            self.events[k].synchronize()              # the slot's previous call has left it
+        hx, hs, hi, ht = self._views(self.host[k], n)
+        hx.copy_(x.view(torch.uint8) if x.dtype != torch.uint8 else x)
+        hs.copy_(x_scale.reshape(-1))
+        hi.copy_(ids)
+        ht.copy_(tw)
+        stream = torch.cuda.current_stream(self.arena.dev)
+        used = self.o_t + _al16(n * self.topk * 4) if n == self.rows else self.nbytes
+        self.dev[k][:used].copy_(self.host[k][:used], non_blocking=True)
+        dx, ds, di, dt = self._views(self.dev[k], n)
+        launch(self.arena.view(li), dx.view(torch.float8_e4m3fn), di, dt, self.out_d[k][:n], self.c0, self.c1,
+               self.ws, x_scale=ds, swiglu_limit=self.limit, has_limit=self.has_limit, stream=stream.cuda_stream,
+               layout=self.arena.layout)
+        self.out_h[k][:n].copy_(self.out_d[k][:n], non_blocking=True)
+        self.events[k].record(stream)
+        self.used[k] = True
+        return self.out_h[k][:n]

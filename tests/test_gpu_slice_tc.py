@@ -92,3 +92,24 @@ def test_width_not_multiple_of_64(cuda_ready):
     torch.cuda.synchronize()
     H.assert_parity(out2, H.oracle_out(H.ingest(q, inv), ids, tw, layer, 288, 416), "[288, 416)")
     _ = oq
+
+
+def test_host_slice_matches_device_call(cuda_ready):
+    """HostSlice (host inputs, one packed copy each way) returns the device call's
+    output, over more calls than it has staging slots and with a short call."""
+    from qmesh_b200.arena import Arena
+    from qmesh_b200.expert_slice import HostSlice, expert_slice
+    dev = cuda_ready
+    layer = H.small_layer(33, 8, inter=256)
+    ar = Arena(dev, 1, 8, 0, 256, layout="tc")
+    ar.load_layer(0, layer)
+    hs = HostSlice(ar, 6)
+    outs = []
+    for step, rows in enumerate([6, 6, 3, 6]):
+        ids, tw = H.random_routing(rows, 8, 50 + step)
+        _, q, inv = H.activations(rows, 50 + step)
+        got = hs(0, q, inv, ids, tw)
+        want = expert_slice(ar, 0, q.to(dev), ids.to(dev), tw.to(dev), x_scale=inv.to(dev))
+        outs.append((got, want))
+        torch.cuda.synchronize()
+        assert torch.equal(got, want.cpu()), f"call {step}"
