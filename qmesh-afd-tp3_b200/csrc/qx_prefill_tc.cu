@@ -158,11 +158,34 @@ __device__ __forceinline__ long long id_of(const Params& p, int q) {
   return p.ids64 ? reinterpret_cast<const long long*>(p.ids)[q] : (long long)reinterpret_cast<const int*>(p.ids)[q];
 }
 
-// The reference's bf16 activation value of element k (gx/gx_ingest.py:151-154).
-__device__ __forceinline__ float ingest_one(const Params& p, const uint8_t* xr, int k, float inv) {
-  if (p.x_fmt == QX_X_BF16) return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(xr)[k] << 16);
-  const uint32_t f2 = e4m3x2_to_f16x2(xr[k]);
-  return __bfloat162float(__float2bfloat16_rn(__fmul_rn(f16lo_to_f32(f2), inv)));
+// The reference's bf16 activation values (gx/gx_ingest.py:151-154) of elements
+// k0 .. k0 + 15 (k0 % 16 == 0) of a row, from 16-byte loads.
+__device__ __forceinline__ void ingest16(const Params& p, const uint8_t* xr, int k0, float inv, float (&v)[16]) {
+  if (p.x_fmt == QX_X_BF16) {
+    const uint4* src = reinterpret_cast<const uint4*>(xr + (size_t)k0 * 2);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 u = src[h];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[8 * h + 2 * i] = __uint_as_float(w[i] << 16);
+        v[8 * h + 2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      }
+    }
+    return;
+  }
+  const uint4 u = *reinterpret_cast<const uint4*>(xr + k0);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t f2 = e4m3x2_to_f16x2(w[i] >> (16 * h));
+      v[4 * i + 2 * h] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(f16lo_to_f32(f2), inv)));
+      v[4 * i + 2 * h + 1] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(f16hi_to_f32(f2), inv)));
+    }
+  }
 }
 
 __device__ __forceinline__ float row_inv(const Params& p, int r) {
@@ -203,7 +226,12 @@ __global__ void __launch_bounds__(256) pf_prep_kernel(Params p) {
   const float inv = row_inv(p, r);
   const uint8_t* xr = reinterpret_cast<const uint8_t*>(p.x) + (size_t)r * p.x_stride;
   float amax = 0.f;
-  for (int k = t; k < HID; k += 256) amax = fmaxf(amax, fabsf(ingest_one(p, xr, k, inv)));
+  for (int k0 = t * 16; k0 < HID; k0 += 256 * 16) {
+    float v[16];
+    ingest16(p, xr, k0, inv, v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   if ((t & 31) == 0) atomicMax(&p.ctl->amax_bits, __float_as_uint(amax));   // amax >= 0: bits order as values
@@ -348,8 +376,7 @@ __global__ void __launch_bounds__(XQ_THR) pf_xquant_kernel(Params p) {
   const uint8_t* xr = reinterpret_cast<const uint8_t*>(p.x) + (size_t)t * p.x_stride;
   const int b = threadIdx.x;                     // 16-element block
   float v[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = ingest_one(p, xr, b * 16 + i, inv);
+  ingest16(p, xr, b * 16, inv, v);
   uint32_t w[2];
   const uint32_t sb = quant16(v, p.ctl->a1g, w);
   const int s = b >> 5, kb = (b >> 2) & (SK - 1), j = b & 3;
