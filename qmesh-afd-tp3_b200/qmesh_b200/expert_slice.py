@@ -24,6 +24,7 @@ import torch
 
 from . import _lib
 from .arena import Arena
+from .trace import rng
 
 SWIGLU_LIMIT = 10.0
 
@@ -88,7 +89,8 @@ def launch(view: _lib.QxArena, x: torch.Tensor, ids: torch.Tensor, tw: torch.Ten
     if stream is None:
         stream = torch.cuda.current_stream(x.device).cuda_stream
     name = "qx_slice_decode_tc" if layout == "tc" else "qx_slice_decode"
-    rc = getattr(lib, name)(ctypes.byref(view), ctypes.byref(args), ctypes.c_void_p(stream))
+    with rng("qx.slice"):
+        rc = getattr(lib, name)(ctypes.byref(view), ctypes.byref(args), ctypes.c_void_p(stream))
     _lib.check(rc, name)
 
 
@@ -171,7 +173,8 @@ def launch_prefill(view: _lib.QxArena, x: torch.Tensor, ids: torch.Tensor, tw: t
     args = _slice_args(x, ids, tw, out, c0, c1, workspace, x_scale, swiglu_limit, has_limit)
     if stream is None:
         stream = torch.cuda.current_stream(x.device).cuda_stream
-    rc = lib.qx_slice_prefill_tc(ctypes.byref(view), ctypes.byref(args), _ptr(a2), ctypes.c_void_p(stream))
+    with rng("qx.prefill"):
+        rc = lib.qx_slice_prefill_tc(ctypes.byref(view), ctypes.byref(args), _ptr(a2), ctypes.c_void_p(stream))
     _lib.check(rc, "qx_slice_prefill_tc")
 
 
@@ -254,19 +257,22 @@ class HostSlice:
         self.k = (k + 1) % len(self.host)
         if self.used[k]:
             self.events[k].synchronize()              # the slot's previous call has left it
-        hx, hs, hi, ht = self._views(self.host[k], n)
-        hx.copy_(x.view(torch.uint8) if x.dtype != torch.uint8 else x)
-        hs.copy_(x_scale.reshape(-1))
-        hi.copy_(ids)
-        ht.copy_(tw)
+        with rng("qx.host_stage"):
+            hx, hs, hi, ht = self._views(self.host[k], n)
+            hx.copy_(x.view(torch.uint8) if x.dtype != torch.uint8 else x)
+            hs.copy_(x_scale.reshape(-1))
+            hi.copy_(ids)
+            ht.copy_(tw)
         stream = torch.cuda.current_stream(self.arena.dev)
         used = self.o_t + _al16(n * self.topk * 4) if n == self.rows else self.nbytes
-        self.dev[k][:used].copy_(self.host[k][:used], non_blocking=True)
+        with rng("qx.h2d"):
+            self.dev[k][:used].copy_(self.host[k][:used], non_blocking=True)
         dx, ds, di, dt = self._views(self.dev[k], n)
         launch(self.arena.view(li), dx.view(torch.float8_e4m3fn), di, dt, self.out_d[k][:n], self.c0, self.c1,
                self.ws, x_scale=ds, swiglu_limit=self.limit, has_limit=self.has_limit, stream=stream.cuda_stream,
                layout=self.arena.layout)
-        self.out_h[k][:n].copy_(self.out_d[k][:n], non_blocking=True)
+        with rng("qx.d2h"):
+            self.out_h[k][:n].copy_(self.out_d[k][:n], non_blocking=True)
         self.events[k].record(stream)
         self.used[k] = True
         return self.out_h[k][:n]

@@ -135,7 +135,9 @@ class P2PExchange:
                 a.shared, a.shared_stride = shared.data_ptr(), shared.stride(0)
         if stream is None:
             stream = torch.cuda.current_stream(part.device).cuda_stream
-        self._L.check(self._lib.qx_combine_p2p(self._ct.byref(a), self._ct.c_void_p(stream)), "qx_combine_p2p")
+        from .trace import rng
+        with rng("qx.combine_p2p"):
+            self._L.check(self._lib.qx_combine_p2p(self._ct.byref(a), self._ct.c_void_p(stream)), "qx_combine_p2p")
         return out if self.rank == self.dst else None
 
     def close(self) -> None:
