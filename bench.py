@@ -294,7 +294,8 @@ def run_ours(args) -> dict | None:
                          "kernel_us": round(k_mean, 3), "alg_bytes_per_launch": int(alg_bytes)},
             "e2e": {"value": round(us_e2e, 3), "unit": "us/layer", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * 3 + (args.steps if world > 1 else 0),
+            # prep + decode (tc) or prologue + main + finalize (frag) per step, + the combine kernel for N > 1
+            "gpu_launches": args.steps * (2 if args.layout == "tc" else 3) + (args.steps if world > 1 else 0),
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu:

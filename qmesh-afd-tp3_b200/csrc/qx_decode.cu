@@ -839,6 +839,7 @@ __global__ void __launch_bounds__(NTHR, 1) qx_decode_kernel(Params p) {
     }
     for (int i = threadIdx.x; i < p.rows; i += blockDim.x) tb.xs[i] = p.xscale[i];
   }
+  __syncwarp();   // warp 0 reconverges after its lane 0's set-up: one arrival per warp
   __syncthreads();
   const int warp = threadIdx.x >> 5;
   if (warp == NCW) {

@@ -33,8 +33,9 @@
 //                                later items come from one atomic queue;
 //                      warps 1, 6  MMA issuers: each copies its K blocks' scale atoms
 //                                into TMEM and issues one M=128 x N x K=64
-//                                block-scaled MMA per K block (blocks 0-3 / 4-7 of
-//                                every stage) into its own accumulator;
+//                                block-scaled MMA per K block (the lower / upper
+//                                half of every stage's K blocks) into its own
+//                                accumulator;
 //                      warps 2-5 epilogue: gate/up items -> SwiGLU -> the pair's
 //                                activation terms for the down projection
 //                                (tile-local exponent, fixed up by the group's last
@@ -43,8 +44,11 @@
 //                      Items: gate/up (group, 64-column tile: 64 gate + 64 up rows
 //                      over K = 5120) then down (group, 128-row output tile over
 //                      the slice's columns). A down item waits (bounded) for its
-//                      group's activation terms.
-//   tc_finalize_kernel out = bf16(sum over slots j in order of y_j).
+//                      group's activation terms. Every down item counts its
+//                      pairs into its 128-row output tile's counter; after its
+//                      items each epilogue group finalizes some (output tile,
+//                      4-row block) units, out = bf16(sum over slots j in order
+//                      of y_j), once their tile's counter is complete.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <limits.h>
@@ -76,9 +80,10 @@ static_assert(NI % 2 == 0, "epilogue groups alternate meta entries");
 // never holds up the next item's accumulator).
 constexpr int NTHR = 352;
 constexpr int NEPI = 2;                        // epilogue warpgroups
-// Two MMA issuer warps split every stage: K blocks 0-3 go to issuer 0, 4-7 to
-// issuer 1, each into its own accumulator (summed in the epilogue); one thread
-// cannot issue block-scaled MMAs as fast as the tensor pipe executes them.
+// Two MMA issuer warps split every stage: of its nkb K blocks, the first
+// ceil(nkb / 2) go to issuer 0, the rest to issuer 1, each into its own
+// accumulator (summed in the epilogue); one thread cannot issue block-scaled
+// MMAs as fast as the tensor pipe executes them.
 // TMEM columns, in four 128-column slots (accumulators use the first 96):
 //   accumulator (buffer b, issuer i) at 256 b + 128 i;
 //   in the 32-column gaps: the constant all-1.0 scale atom of every activation
@@ -105,20 +110,20 @@ struct GroupS {     // one group (<= GMAX routed pairs of one expert), kept in s
   int32_t expert, gsz, pair_off;
   int32_t n, sbs;         // activation operand of either item kind: 16 x gsz rows, bytes per stage
   int32_t ab_off;         // offset of the group's down operand in the activation-term buffer
-  float g13, g2;
+  int32_t pad[2];
 };
 static_assert(sizeof(GroupS) == 32, "shared group record is 32 bytes");
 
 struct RouteHdr {   // call-wide results of the routing, in shared memory
   int32_t n_groups, n1, n2, b_max;   // groups, gate/up items, down items, widest activation stage
+  int32_t n_pairs;                   // routed pairs with a valid expert
+  int32_t pad[3];
 };
 
-struct PairS {      // per group position: pair index and its routing weight
+struct PairS {      // per group position: pair index (row * topk + slot)
   int32_t pq;
-  float tw;
-  int32_t pad[2];
 };
-static_assert(sizeof(PairS) == 16, "shared pair record is 16 bytes");
+static_assert(sizeof(PairS) == 4, "shared pair record is 4 bytes");
 
 struct Params {
   const void* x;
@@ -142,6 +147,7 @@ struct Params {
   Ctl* ctl;
   uint32_t* cnt1;     // [P] gate/up tiles finished per group
   uint32_t* ready;    // [P] group activation terms complete
+  uint32_t* fcnt;     // [HT] routed pairs whose y is written, per 128-row output tile
   int32_t* emax;      // [P] per group position: common activation exponent
   int32_t* eloc;      // [P][NT] per group position and tile: tile exponent
   int32_t* xexp;      // [rows]
@@ -179,7 +185,7 @@ constexpr uint32_t XT_SBO = SK * 256;          // row group to row group
 constexpr uint32_t XT_KB = 256;                // K block to K block
 
 struct WsLayout {
-  size_t ctl, cnt1, ready, emax, eloc, xexp, xt, ab, y, total;
+  size_t ctl, cnt1, ready, fcnt, emax, eloc, xexp, xt, ab, y, total;
 };
 
 __host__ inline WsLayout ws_layout(int rows, int topk, int W) {
@@ -189,6 +195,7 @@ __host__ inline WsLayout ws_layout(int rows, int topk, int W) {
   L.ctl = o;      o = al256(o + sizeof(Ctl));
   L.cnt1 = o;     o = al256(o + (size_t)P * 4);
   L.ready = o;    o = al256(o + (size_t)P * 4);
+  L.fcnt = o;     o = al256(o + (size_t)HT * 4);
   L.emax = o;     o = al256(o + (size_t)P * 4);
   L.eloc = o;     o = al256(o + (size_t)P * NT * 4);
   L.xexp = o;     o = al256(o + (size_t)rows * 4);
@@ -284,27 +291,21 @@ __device__ float row_amax(const Params& p, const uint8_t* xr, float inv, float* 
   return m;
 }
 
-// Exclusive prefix sum over v[0..n) by one warp, in place; returns the total.
-__device__ int warp_scan_excl(int* v, int n, int lane) {
-  int carry = 0;
-  for (int i0 = 0; i0 < n; i0 += 32) {
-    const int i = i0 + lane;
-    const int x = i < n ? v[i] : 0;
-    int inc = x;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int u = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += u;
-    }
-    if (i < n) v[i] = carry + inc - x;
-    carry += __shfl_sync(0xffffffffu, inc, 31);
-  }
-  __syncwarp();
-  return carry;
-}
+constexpr int IDR = MAXP / 32;   // expert ids per lane of the routing warp
 
-// Scratch of route_local, in words (placed in the not yet used stage rings).
-constexpr int RT_WORDS = 8 * MAXP + 2 * (MAXE / 32);
+// Lane `lane`'s expert ids (pairs lane + 32 i); ids outside [0, E) (the -1
+// sentinel, or bad ids that the prep kernel flags) become -1 and are skipped.
+__device__ __forceinline__ void load_ids(const Params& p, int lane, int (&idr)[IDR]) {
+#pragma unroll
+  for (int i = 0; i < IDR; ++i) {
+    const int q = lane + 32 * i;
+    long long id = -1;
+    if (q < p.P)
+      id = p.ids64 ? __ldg(reinterpret_cast<const long long*>(p.ids) + q)
+                   : (long long)__ldg(reinterpret_cast<const int*>(p.ids) + q);
+    idr[i] = (id >= 0 && id < p.E) ? (int)id : -1;
+  }
+}
 
 // The routing tables of a call, built by one warp of every CTA from the ids
 // (the reference groups the routed pairs by expert the same way for its
@@ -312,102 +313,168 @@ constexpr int RT_WORDS = 8 * MAXP + 2 * (MAXE / 32);
 // order; an expert's pairs in (row, slot) order, split evenly into groups of at
 // most gmax; per group its operand geometry and the offset of its down operand;
 // gs[g], ps[group position], hdr. Every CTA computes the same tables.
-__device__ void route_local(const Params& p, int* scr, GroupS* gs, PairS* ps, RouteHdr* hdr) {
+//
+// The warp sorts the keys (expert << 9 | pair) of its 32 K slots (pair
+// lane + 32 j, no pair = all ones, sorted last) with a bitonic network, element
+// i = K lane + j after the sort; an expert's pairs are then a run of the sorted
+// order, and scans over the order give each pair its run's start and end, its
+// rank in the run and its group. A group's pairs are contiguous in the order,
+// so its down operand sits at (its first position) x (bytes per pair).
+// Compare-exchange of this lane's slots j and j | S (S < K) towards ascending
+// order where bit k of the element index K lane + j is clear.
+template <int K, int S>
+__device__ __forceinline__ void cx_lane(uint32_t (&v)[K], int k, int lane) {
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    if ((j & S) == 0) {
+      const bool asc = ((K * lane + j) & k) == 0;
+      const uint32_t a = v[j], b = v[j | S];
+      v[j] = asc ? min(a, b) : max(a, b);
+      v[j | S] = asc ? max(a, b) : min(a, b);
+    }
+  }
+}
+
+// floor(a / b) for 0 <= a < 2^22, 1 <= b < 2^22: a float quotient corrected by one step.
+__device__ __forceinline__ int div_small(int a, int b) {
+  int q = __float2int_rz(__fdividef((float)a, (float)b));
+  if (q * b > a) --q;
+  else if ((q + 1) * b <= a) ++q;
+  return q;
+}
+
+template <int K>
+__device__ void route_sort(const Params& p, const int (&idr)[IDR], GroupS* gs, PairS* ps, RouteHdr* hdr) {
+  static_assert(K <= IDR && (K & (K - 1)) == 0, "keys per lane");
+  constexpr uint32_t FULL = 0xffffffffu, NONE = 0xffffffffu;
+  constexpr int N = 32 * K;
   const int lane = threadIdx.x & 31;
-  int* ex = scr;                    // [P] expert of pair q or -1
-  int* pu = ex + MAXP;              // [P] unique index of pair q
-  int* pr = pu + MAXP;              // [P] rank of pair q among its expert's pairs
-  int* cnt = pr + MAXP;             // [U] pairs per unique expert
-  int* off = cnt + MAXP;            // [U] first group position of the unique
-  int* gf = off + MAXP;             // [U] first group of the unique
-  int* uex = gf + MAXP;             // [U] expert id of the unique
-  int* asz = uex + MAXP;            // [G] down-operand bytes of the group
-  uint32_t* bits = reinterpret_cast<uint32_t*>(asz + MAXP);
-  int* wpre = reinterpret_cast<int*>(bits + MAXE / 32);
-  const int nw = (p.E + 31) / 32;
   const int gmax = min(GMAX, p.rows);
-  for (int i = lane; i < nw; i += 32) bits[i] = 0;
-  __syncwarp();
-  for (int q = lane; q < p.P; q += 32) {
-    const long long id = p.ids64 ? reinterpret_cast<const long long*>(p.ids)[q]
-                                 : (long long)reinterpret_cast<const int*>(p.ids)[q];
-    const int e = (id >= 0 && id < p.E) ? (int)id : -1;   // other ids: skipped (flagged by the prep kernel)
-    ex[q] = e;
-    if (e >= 0) atomicOr(&bits[e >> 5], 1u << (e & 31));
+  uint32_t v[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const int q = lane + 32 * j;
+    v[j] = (q < p.P && idr[j] >= 0) ? ((uint32_t)idr[j] << 9) | (uint32_t)q : NONE;
   }
-  __syncwarp();
-  for (int i = lane; i < nw; i += 32) wpre[i] = __popc(bits[i]);
-  __syncwarp();
-  const int U = warp_scan_excl(wpre, nw, lane);
-  for (int u = lane; u < U; u += 32) cnt[u] = 0;
-  __syncwarp();
-  // rank of each pair among the earlier pairs of its expert, 32 pairs at a time
-  const uint32_t lt = (1u << lane) - 1u;
-  for (int q0 = 0; q0 < p.P; q0 += 32) {
-    const int q = q0 + lane;
-    const int e = q < p.P ? ex[q] : -1;
-    const uint32_t same = __match_any_sync(0xffffffffu, e);
-    int u = -1;
-    if (e >= 0) {
-      u = wpre[e >> 5] + __popc(bits[e >> 5] & ((1u << (e & 31)) - 1u));
-      pu[q] = u;
-      pr[q] = cnt[u] + __popc(same & lt);
-    }
-    __syncwarp();
-    if (e >= 0 && (same & lt) == 0) {   // the expert's first lane in this chunk
-      cnt[u] += __popc(same);
-      uex[u] = e;
-    }
-    __syncwarp();
-  }
-  for (int u = lane; u < U; u += 32) {
-    off[u] = cnt[u];
-    gf[u] = (cnt[u] + gmax - 1) / gmax;
-  }
-  __syncwarp();
-  warp_scan_excl(off, U, lane);
-  const int G = warp_scan_excl(gf, U, lane);
-  for (int q = lane; q < p.P; q += 32) {
-    if (ex[q] >= 0) {
-      PairS s;
-      s.pq = q;
-      s.tw = p.tw[q];
-      s.pad[0] = s.pad[1] = 0;
-      ps[off[pu[q]] + pr[q]] = s;
+  // The network's stages run as loops (unrolled only for 2 slots per lane): a
+  // fully unrolled network of 512 keys is thousands of instructions that every
+  // SM fetches once at its start.
+#pragma unroll(K == 2 ? 8 : 1)
+  for (int k = 2; k <= N; k <<= 1) {
+#pragma unroll(K == 2 ? 8 : 1)
+    for (int s = k >> 1; s > 0; s >>= 1) {
+      if (s >= K) {                        // partner in lane ^ (s / K), same slot
+        const bool keep_min = ((lane & (k / K)) == 0) == ((lane & (s / K)) == 0);
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+          const uint32_t o = __shfl_xor_sync(FULL, v[j], s / K);
+          v[j] = keep_min ? min(v[j], o) : max(v[j], o);
+        }
+      } else if (s == 1) {                 // partner in this lane's slot j ^ s
+        cx_lane<K, 1>(v, k, lane);
+      } else if (s == 2) {
+        if constexpr (K > 2) cx_lane<K, 2>(v, k, lane);
+      } else if (s == 4) {
+        if constexpr (K > 4) cx_lane<K, 4>(v, k, lane);
+      } else {
+        if constexpr (K > 8) cx_lane<K, 8>(v, k, lane);
+      }
     }
   }
+  // runs: f = first pair of an expert; st = run start (inclusive max scan of
+  // the starts), en = next run's start (suffix min), or the valid-pair count
+  int Pv = 0, e[K];
+  bool f[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    e[j] = v[j] == NONE ? -1 : (int)(v[j] >> 9);
+    Pv += __popc(__ballot_sync(FULL, v[j] != NONE));
+  }
+  const int prev = __shfl_up_sync(FULL, e[K - 1], 1);
+#pragma unroll
+  for (int j = 0; j < K; ++j) f[j] = e[j] >= 0 && (j ? e[j - 1] != e[j] : (lane == 0 || prev != e[0]));
+  int st[K], en[K], run = -1, nx = INT_MAX;
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    if (f[j]) run = K * lane + j;
+    st[j] = run;
+  }
+#pragma unroll
+  for (int j = K - 1; j >= 0; --j) {
+    en[j] = nx;
+    if (f[j]) nx = K * lane + j;
+  }
+  int lmax = run, lmin = nx;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a = __shfl_up_sync(FULL, lmax, o), b = __shfl_down_sync(FULL, lmin, o);
+    if (lane >= o) lmax = max(lmax, a);
+    if (lane + o < 32) lmin = min(lmin, b);
+  }
+  // (every lane takes part in each shuffle; the edge lanes' values are replaced after)
+  int before = __shfl_up_sync(FULL, lmax, 1), after = __shfl_down_sync(FULL, lmin, 1);
+  if (lane == 0) before = -1;
+  if (lane == 31) after = INT_MAX;
+  // per pair: run length c, rank r, groups of the run ng, own group k; the
+  // inclusive sum of ng over run starts numbers the groups
+  int c[K], r[K], ng[K], gk[K], sum = 0;
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    st[j] = max(st[j], before);
+    const int end = min(min(en[j], after), Pv);
+    c[j] = e[j] >= 0 ? end - st[j] : 1;
+    r[j] = K * lane + j - st[j];
+    ng[j] = div_small(c[j] + gmax - 1, gmax);
+    gk[j] = div_small((r[j] + 1) * ng[j] - 1, c[j]);   // the k with k c / ng <= r < (k + 1) c / ng
+    if (f[j]) sum += ng[j];
+    st[j] = sum;                               // from here: inclusive group count
+  }
+  int lsum = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a = __shfl_up_sync(FULL, lsum, o);
+    if (lane >= o) lsum += a;
+  }
+  const int G = __shfl_sync(FULL, lsum, 31), base = lsum - sum;
+  const int abs = ((p.NT + SK - 1) / SK) * XT_STAGE;   // down-operand bytes per pair
   int bmx = 0;
-  for (int u = lane; u < U; u += 32) {
-    const int c = cnt[u], ng = (c + gmax - 1) / gmax, e = uex[u];
-    const float g13 = p.g13[e], g2 = p.g2[e];
-    for (int k = 0; k < ng; ++k) {
-      const int lo = k * c / ng, hi = (k + 1) * c / ng, gsz = hi - lo;
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    if (e[j] < 0) continue;
+    const int i = K * lane + j;
+    ps[i].pq = (int)(v[j] & 511u);
+    const int lo = div_small(gk[j] * c[j], ng[j]);
+    if (r[j] == lo) {                          // the group's first pair writes its record
+      const int gsz = div_small((gk[j] + 1) * c[j], ng[j]) - lo;
       GroupS d;
-      d.expert = e;
+      d.expert = e[j];
       d.gsz = gsz;
-      d.pair_off = off[u] + lo;
+      d.pair_off = i;
       d.n = XTERMS * gsz;
       d.sbs = gsz * XT_STAGE;
-      d.ab_off = 0;
-      d.g13 = g13;
-      d.g2 = g2;
-      gs[gf[u] + k] = d;
-      asz[gf[u] + k] = ((p.NT + SK - 1) / SK) * d.sbs;
+      d.ab_off = i * abs;
+      d.pad[0] = d.pad[1] = 0;
+      gs[base + st[j] - ng[j] + gk[j]] = d;
       bmx = max(bmx, d.sbs);
     }
   }
-  __syncwarp();
-  warp_scan_excl(asz, G, lane);
-  for (int g = lane; g < G; g += 32) gs[g].ab_off = asz[g];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) bmx = max(bmx, __shfl_xor_sync(0xffffffffu, bmx, o));
+  for (int o = 16; o > 0; o >>= 1) bmx = max(bmx, __shfl_xor_sync(FULL, bmx, o));
   if (lane == 0) {
     hdr->n_groups = G;
     hdr->n1 = G * p.NT;
     hdr->n2 = G * HT;
     hdr->b_max = bmx;
+    hdr->n_pairs = Pv;
   }
   __syncwarp();
+}
+
+__device__ void route_local(const Params& p, const int (&idr)[IDR], GroupS* gs, PairS* ps, RouteHdr* hdr) {
+  if (p.P <= 64) route_sort<2>(p, idr, gs, ps, hdr);
+  else if (p.P <= 128) route_sort<4>(p, idr, gs, ps, hdr);
+  else if (p.P <= 256) route_sort<8>(p, idr, gs, ps, hdr);
+  else route_sort<16>(p, idr, gs, ps, hdr);
 }
 
 // One CTA per unit (row r, 512-element chunk c = stage c of the gate/up
@@ -429,6 +496,7 @@ __global__ void __launch_bounds__(PREP_THR) tc_prep_kernel(Params p) {
       p.ready[q] = 0;
       p.emax[q] = INT_MIN;
     }
+    for (int i = tid; i < HT; i += PREP_THR) p.fcnt[i] = 0;
     bad = __syncthreads_or(bad);
     uint32_t* c = reinterpret_cast<uint32_t*>(p.ctl);
     for (int i = tid; i < (int)(sizeof(Ctl) / 4); i += PREP_THR) c[i] = 0;
@@ -493,11 +561,13 @@ struct Smem {       // fixed part of the dynamic shared memory, before the rings
   ItemMeta meta[NI];
   uint64_t drain[NISS];
   uint64_t init_bar;
+  uint64_t tm_done;           // every epilogue warp's last TMEM read is complete
   uint32_t tmem_base, prod_scratch, mma_scratch[NISS];   // scratch: status words of drain waits
   uint32_t last_flag[NEPI];
   float amx[NEPI][GMAX][2];   // per epilogue group, pair, half: |act| maximum
   int32_t em[NEPI][GMAX];     // down item: the group's common activation exponents
   int32_t xe[NEPI][GMAX];     // gate/up item: the group's rows' x exponents
+  float tws[NEPI][GMAX];      // down item: the group's routing weights
   RouteHdr hdr;
 };
 
@@ -518,6 +588,11 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
   int seen_a = -1;                    // last group whose activation flag was seen set
   bool ok = true, prep_seen = false;  // prep_seen: the prep kernel's results are visible
   uint32_t item = blockIdx.x;         // the first item is static, the rest come from the queue
+  uint32_t cl_next = 0, cl_end = 0;   // items claimed and not yet started: [cl_next, cl_end)
+  // Down items of one or two stages are claimed in batches (of 4 or 2), so the
+  // queue's round trip is paid once per batch; longer items one at a time.
+  const int nst2 = (p.NT + SK - 1) / SK;
+  const uint32_t dclaim = nst2 == 1 ? 4u : nst2 == 2 ? 2u : 1u;
   for (;;) {
     ItemMeta m = {};
     if (!ok || item >= n1 + n2) {
@@ -574,7 +649,15 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
       fence_proxy_async_global();
       prep_seen = true;
     }
-    const uint32_t next = gridDim.x + atomicAdd(&p.ctl->work, 1u);   // the following item, claimed ahead
+    uint32_t next;                      // the following item, claimed ahead
+    if (cl_next < cl_end) {
+      next = cl_next++;
+    } else {
+      const uint32_t k = item >= n1 ? dclaim : 1u;
+      next = gridDim.x + atomicAdd(&p.ctl->work, k);
+      cl_next = next + 1;
+      cl_end = next + k;
+    }
     bool check = m.kind == 2 && seen_a != m.group;
     for (int s = 0; s < m.nst; ++s, ++sc) {
       const int slot = (int)(sc % (uint32_t)p.ns);
@@ -619,8 +702,8 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
   }
 }
 
-// Issuer `iss` of every stage's K blocks [2 iss, 2 iss + 2) into accumulator
-// (buffer, iss). Both issuers consume every stage and item in the same order.
+// Issuer `iss` of its half of every stage's K blocks into accumulator (buffer,
+// iss). Both issuers consume every stage and item in the same order.
 __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS* gs, uint32_t tbase, int iss,
                            volatile uint32_t* status, uint64_t deadline) {
   uint32_t sc = 0, mc = 0, ic = 0;
@@ -650,7 +733,7 @@ __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS
         break;
       }
       const int nkb = s < m.nst - 1 ? SK : m.nkb_last;
-      const int k0 = iss * KB_PER_ISS, k1 = min(nkb, k0 + KB_PER_ISS);
+      const int k0 = iss ? (nkb + 1) >> 1 : 0, k1 = iss ? nkb : (nkb + 1) >> 1;   // <= KB_PER_ISS each
       const uint32_t a0 = smem_u32(ring + (size_t)slot * A_STAGE);
       const uint32_t b0 = smem_u32(ring + p.b_off + (size_t)slot * p.bst);
       const uint32_t bank = sfbase + (sc & 1u) * TM_BANK;
@@ -674,9 +757,50 @@ __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS
   mbar_wait_bounded(&S.drain[iss], 0, &S.mma_scratch[iss], 1u, globaltimer_ns() + p.timeout_ns);
 }
 
-// Whether issuer 1 wrote its accumulator for an item (it owns K blocks 2-3 of each stage).
-__device__ __forceinline__ bool second_acc(const ItemMeta& m) { return m.nst > 1 || m.nkb_last > KB_PER_ISS; }
+// Whether issuer 1 wrote its accumulator for an item (it owns the upper half,
+// ceil(nkb / 2) onwards, of the K blocks of each stage).
+__device__ __forceinline__ bool second_acc(const ItemMeta& m) { return m.nst > 1 || m.nkb_last > 1; }
 
+
+// One finalize unit (output columns [128 tile, 128 tile + 128) of rows
+// [4 rb, 4 rb + 4)) by one epilogue group (et = 0..127), once every routed
+// pair's y covers the tile: out[row, k] = bf16(sum over slots j in order of
+// y[row * topk + j][k]), a slot without a valid expert adding 0. Thread et
+// takes 4 consecutive outputs of row 4 rb + et / 32.
+__device__ void finalize_unit(const Params& p, int tile, int rb, int et) {
+  const int k = tile * 128 + 4 * (et & 31);
+  const int row = 4 * rb + (et >> 5);
+  if (row < p.rows) {
+    float4 v[QX_MAX_TOPK];
+    bool val[QX_MAX_TOPK];
+#pragma unroll
+    for (int j = 0; j < QX_MAX_TOPK; ++j) {   // ids and y loads issued together
+      val[j] = false;
+      v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j < p.topk) {
+        const int q = row * p.topk + j;
+        const long long id = p.ids64 ? __ldg(reinterpret_cast<const long long*>(p.ids) + q)
+                                     : (long long)__ldg(reinterpret_cast<const int*>(p.ids) + q);
+        val[j] = id >= 0 && id < p.E;
+        v[j] = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * HID + k));
+      }
+    }
+    float4 s = val[0] ? v[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 1; j < QX_MAX_TOPK; ++j) {
+      const float4 z = val[j] ? v[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      s.x += z.x;
+      s.y += z.y;
+      s.z += z.z;
+      s.w += z.w;
+    }
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&lo);
+    o.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(p.out + (size_t)row * p.out_stride + k) = o;
+  }
+}
 
 // Epilogue warpgroup eg (warps 2-5 or 7-10): the items of accumulator buffer
 // eg, i.e. every other item. Named barriers 1 + 2 eg (its 128 threads) and
@@ -698,6 +822,11 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
   float(*amx)[2] = S.amx[eg];
   int32_t* em = S.em[eg];
   int32_t* xe_s = S.xe[eg];
+  float* tws = S.tws[eg];
+  // The group whose down-item values (routing weights, common exponents, g2) this
+  // warpgroup holds: consecutive down items of one group fetch them once.
+  int dgrp = -1;
+  float g2c = 0.f;
   for (uint32_t ic = (uint32_t)eg;; ic += NEPI) {   // item ic = meta entry ic
     const uint32_t mc = ic;
     const int mi = (int)(mc % NI);
@@ -710,11 +839,18 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
     bool ok = true;
     if (mt.kind == 1 && et < gr.gsz)   // the rows' x exponents, fetched while the MMAs run
       xe_s[et] = __ldcg(&p.xexp[ps[gr.pair_off + et].pq / p.topk]);
-    if (mt.kind == 2 && et < gr.gsz) {
-      // The group's common exponents, fetched while the MMAs run.
-      ok = wait_flag(&p.ready[mt.group], 1u + p.dep_extra, status, deadline);
-      em[et] = __ldcg(&p.emax[gr.pair_off + et]);
+    if (mt.kind == 2 && mt.group != dgrp) {
+      // A new group's g2, routing weights and common exponents, fetched while the MMAs run.
+      g2c = __ldg(&p.g2[gr.expert]);
+      if (et < gr.gsz) {
+        tws[et] = __ldg(&p.tw[ps[gr.pair_off + et].pq]);
+        ok = wait_flag(&p.ready[mt.group], 1u + p.dep_extra, status, deadline);
+        em[et] = __ldcg(&p.emax[gr.pair_off + et]);
+      }
+      dgrp = mt.group;                 // on a failed wait the loop ends below
     }
+    // The expert's global scale: g13 for a gate/up item (fetched while its MMAs run), g2 for a down item.
+    const float gsc = mt.kind == 1 ? __ldg(&p.g13[gr.expert]) : g2c;
     const int buf = eg;
     ok = mbar_wait_bounded(&S.acc_full[buf], (ic / 2) & 1, status, QX_DEV_TIMEOUT, deadline) && ok;
     if (!bar_and(B1, 128, ok)) break;
@@ -730,7 +866,7 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
         tc::ld16x2(tacc + XTERMS * q, tacc + TM_SLOT + XTERMS * q, v, v1);   // v1 holds data only if two
 #pragma unroll
         for (int t = 0; t < XTERMS; ++t) v[t] += two ? v1[t] : 0.f;
-        const float s = tc::term_sum16(v, xe_s[q]) * gr.g13;
+        const float s = tc::term_sum16(v, xe_s[q]) * gsc;
         if (up) xu[q * 64 + c] = s; else xg[q * 64 + c] = s;
       }
       tc::fence_before_sync();
@@ -767,7 +903,7 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
         float r0 = xg[q * 64 + 2 * lane], r1 = xg[q * 64 + 2 * lane + 1];
         uint8_t* blk = ab + (size_t)q * XT_STAGE + kbl * XT_KB + (lane >> 4) * 128 + (lane & 12);
         float g = tc::exp2i(el), ig = tc::exp2i(-el);
-#pragma unroll 1
+#pragma unroll
         for (int t = 0; t < XTERMS; ++t) {
           const uint32_t w = tc::pack4(tc::digit2(r0, r1, g, ig), lane);
           if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(blk + (t >> 3) * XT_SBO + (t & 7) * 16) = w;
@@ -839,13 +975,32 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
         tc::ld16x2(tacc + XTERMS * q, tacc + TM_SLOT + XTERMS * q, v, v1);   // v1 holds data only if two
 #pragma unroll
         for (int t = 0; t < XTERMS; ++t) v[t] += two ? v1[t] : 0.f;
-        const PairS pr = ps[gr.pair_off + q];
-        p.y[(size_t)pr.pq * HID + h] = tc::term_sum16(v, em[q]) * (gr.g2 * pr.tw);
+        p.y[(size_t)ps[gr.pair_off + q].pq * HID + h] = tc::term_sum16(v, em[q]) * (gsc * tws[q]);
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.acc_empty[buf]);
+      // The group's y stores are ordered before thread 0's release by the barrier:
+      // the tile's counter counts the routed pairs whose y covers it.
+      asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
+      if (et == 0) red_add_release_gpu(&p.fcnt[mt.tile], (uint32_t)gr.gsz);
     }
+  }
+  // This warp reads TMEM no more: TMEM may be released once all epilogue warps say so.
+  tc::fence_before_sync();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&S.tm_done);
+  // Finalize units (output tile, block of 4 rows), dealt round robin over every
+  // CTA's epilogue groups: each waits (bounded) until its tile's counter holds
+  // every routed pair, then sums its rows. A post without a valid pair needs no
+  // wait and writes zeros.
+  const int rbn = (p.rows + 3) >> 2;
+  for (int u = blockIdx.x * NEPI + eg; u < HT * rbn; u += gridDim.x * NEPI) {
+    const int tile = u / rbn;
+    bool ok = true;
+    if (et == 0) ok = wait_flag(&p.fcnt[tile], (uint32_t)S.hdr.n_pairs, status, deadline);
+    if (!bar_and(B1, 128, ok)) break;   // every thread's y reads follow thread 0's acquire
+    finalize_unit(p, tile, u - tile * rbn, et);
   }
 }
 
@@ -858,7 +1013,10 @@ __global__ void __launch_bounds__(NTHR, 1) tc_decode_kernel(Params p) {
   PairS* ps = reinterpret_cast<PairS*>(smem + p.tab_off + (size_t)p.P * sizeof(GroupS));
   const int warp = threadIdx.x >> 5;
   volatile uint32_t* status = &p.ctl->status;
-  if (threadIdx.x == 0) {
+  // Warp 0 loads the call's expert ids while other warps set up the CTA.
+  int idr[IDR];
+  if (warp == 0) load_ids(p, threadIdx.x & 31, idr);
+  if (threadIdx.x == 64) {
     for (int s = 0; s < MAXNS; ++s) {
       mbar_init(&S.full[s], 1);
       mbar_init(&S.empty[s], NISS);
@@ -873,12 +1031,16 @@ __global__ void __launch_bounds__(NTHR, 1) tc_decode_kernel(Params p) {
     }
     for (int i = 0; i < NISS; ++i) mbar_init(&S.drain[i], 1);
     mbar_init(&S.init_bar, 1);
+    mbar_init(&S.tm_done, NEPI * 4);
     fence_mbar_init();
   }
   if (warp == 1) {
     tc::tmem_alloc(&S.tmem_base, TM_COLS);
     tc::tmem_relinquish();
   }
+  // Every CTA barrier below follows code that one lane of a warp ran alone: the
+  // warp reconverges first, so that it arrives at the barrier once.
+  __syncwarp();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -896,11 +1058,9 @@ __global__ void __launch_bounds__(NTHR, 1) tc_decode_kernel(Params p) {
   // The ids, routing weights and x come from work before the prep kernel, so the
   // routing needs no wait; the prep kernel's results are waited for by the
   // threads that read them (producer, epilogue).
-  if (warp == 0) {
-    route_local(p, reinterpret_cast<int*>(ring), gs, ps, &S.hdr);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the ring's next writers are bulk copies
-  }
+  if (warp == 0) route_local(p, idr, gs, ps, &S.hdr);
   pdl_launch_dependents();
+  __syncwarp();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -924,43 +1084,18 @@ __global__ void __launch_bounds__(NTHR, 1) tc_decode_kernel(Params p) {
   }
   // The producer drained its copies and the issuers their tensor-core work (all
   // bounded) before returning; the epilogue's last TMEM reads are complete.
+  __syncwarp();
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 1) tc::tmem_dealloc(tbase, TM_COLS);
-}
-
-// out[row, k] = bf16(sum over slots j in order of y[row*topk + j][k]); slots
-// without a valid expert contribute nothing.
-__global__ void __launch_bounds__(256) tc_finalize_kernel(Params p) {
-  pdl_wait();
-  const int n4 = p.rows * (HID / 4);
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
-    const int row = i / (HID / 4), k = (i - row * (HID / 4)) * 4;
-    float4 v[QX_MAX_TOPK];
-#pragma unroll
-    for (int j = 0; j < QX_MAX_TOPK; ++j) {
-      float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < p.topk) {
-        const int q = row * p.topk + j;
-        const long long id = p.ids64 ? reinterpret_cast<const long long*>(p.ids)[q]
-                                     : (long long)reinterpret_cast<const int*>(p.ids)[q];
-        if (id >= 0 && id < p.E) z = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * HID + k));
-      }
-      v[j] = z;
+  if (warp == 1) {
+    // TMEM is released after the epilogue warps' last reads (bounded wait).
+    if ((threadIdx.x & 31) == 0) {
+      S.mma_scratch[0] = 0;
+      mbar_wait_bounded(&S.tm_done, 0, &S.mma_scratch[0], 1u, globaltimer_ns() + p.timeout_ns);
     }
-    float4 s = v[0];
-#pragma unroll
-    for (int j = 1; j < QX_MAX_TOPK; ++j) {
-      s.x += v[j].x;
-      s.y += v[j].y;
-      s.z += v[j].z;
-      s.w += v[j].w;
-    }
-    const __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
-    uint2 o;
-    o.x = *reinterpret_cast<const uint32_t*>(&lo);
-    o.y = *reinterpret_cast<const uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(p.out + (size_t)row * p.out_stride + k) = o;
+    __syncwarp();
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tbase, TM_COLS);
   }
 }
 
@@ -1082,6 +1217,7 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream)
   p.ctl = reinterpret_cast<Ctl*>(ws + L.ctl);
   p.cnt1 = reinterpret_cast<uint32_t*>(ws + L.cnt1);
   p.ready = reinterpret_cast<uint32_t*>(ws + L.ready);
+  p.fcnt = reinterpret_cast<uint32_t*>(ws + L.fcnt);
   p.emax = reinterpret_cast<int32_t*>(ws + L.emax);
   p.eloc = reinterpret_cast<int32_t*>(ws + L.eloc);
   p.xexp = reinterpret_cast<int32_t*>(ws + L.xexp);
@@ -1100,7 +1236,6 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream)
   p.ring_off = (int)(((size_t)p.tab_off + tables + 127) & ~size_t(127));
   p.ring_bytes = (int)(SMEM_LIMIT - (size_t)p.ring_off);
   if (p.ring_bytes - 512 < 2 * (A_STAGE + p.bst)) return QX_ERR_SHAPE;   // two slots of the widest group
-  if ((size_t)p.ring_bytes < (size_t)RT_WORDS * 4) return QX_ERR_SHAPE;     // routing scratch
   p.ns = p.b_off = 0;
   p.timeout_ns = timeout_ns();
   p.dep_extra = dep_extra();
@@ -1121,15 +1256,6 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream)
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, tc_decode_kernel, p) != cudaSuccess) return QX_ERR_LAUNCH;
-
-  cudaLaunchConfig_t cfg2 = {};
-  const int n4 = a->rows * (HID / 4);
-  cfg2.gridDim = dim3((n4 + 255) / 256, 1, 1);
-  cfg2.blockDim = dim3(256, 1, 1);
-  cfg2.stream = st;
-  cfg2.attrs = attr;
-  cfg2.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg2, tc_finalize_kernel, p) != cudaSuccess) return QX_ERR_LAUNCH;
   return QX_OK;
 }
 

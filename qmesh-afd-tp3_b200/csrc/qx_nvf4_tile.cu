@@ -43,6 +43,7 @@ __global__ void __launch_bounds__(128, 1)
     tc::tmem_alloc(&tmem_base, TM_COLS);
     tc::tmem_relinquish();
   }
+  __syncwarp();   // warp 0 reconverges after its lane 0's set-up: one arrival per warp
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -92,6 +93,7 @@ __global__ void __launch_bounds__(128, 1)
     if (!loaded) mbar_wait_bounded(&bar_load, 0, &grace_status, 1u, grace);
     if (issued && !done) mbar_wait_bounded(&bar_mma, 0, &grace_status, 1u, grace);
   }
+  __syncwarp();
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tbase, TM_COLS);

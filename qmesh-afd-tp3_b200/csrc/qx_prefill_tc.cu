@@ -391,6 +391,7 @@ struct Smem {
   uint64_t full[MAXNS], empty[MAXNS], acc_full[2], acc_empty[2], meta_full[NI], meta_empty[NI];
   ItemMeta meta[NI];
   uint64_t drain[NISS];
+  uint64_t tm_done;           // every epilogue warp's last TMEM read is complete
   uint32_t tmem_base, prod_scratch, mma_scratch[NISS];
   int32_t pq[NEPI][16];
   float tw[NEPI][16];
@@ -653,6 +654,10 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, uint32_t tbase, in
       }
     }
   }
+  // This warp reads TMEM no more: TMEM may be released once all epilogue warps say so.
+  tc::fence_before_sync();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&S.tm_done);
 }
 
 __global__ void __launch_bounds__(NTHR, 1) pf_main_kernel(Params p) {
@@ -676,12 +681,16 @@ __global__ void __launch_bounds__(NTHR, 1) pf_main_kernel(Params p) {
       mbar_init(&S.meta_empty[i], NISS + 1);
     }
     for (int i = 0; i < NISS; ++i) mbar_init(&S.drain[i], 1);
+    mbar_init(&S.tm_done, NEPI * 4);
     fence_mbar_init();
   }
   if (warp == 1) {
     tc::tmem_alloc(&S.tmem_base, TM_COLS);
     tc::tmem_relinquish();
   }
+  // Each CTA barrier follows code that one lane of a warp ran alone: the warp
+  // reconverges first, so that it arrives at the barrier once.
+  __syncwarp();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -705,9 +714,20 @@ __global__ void __launch_bounds__(NTHR, 1) pf_main_kernel(Params p) {
   } else if (threadIdx.x == 0) {
     atomicOr(const_cast<uint32_t*>(status), (uint32_t)QX_DEV_OVERFLOW);   // a group too wide for two ring slots
   }
+  __syncwarp();
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 1) tc::tmem_dealloc(tbase, TM_COLS);
+  if (warp == 1) {
+    // TMEM is released after the epilogue warps' last reads (bounded wait; none
+    // ran when the ring could not hold two stages).
+    if ((threadIdx.x & 31) == 0 && p.ns >= 2) {
+      S.mma_scratch[0] = 0;
+      mbar_wait_bounded(&S.tm_done, 0, &S.mma_scratch[0], 1u, globaltimer_ns() + p.timeout_ns);
+    }
+    __syncwarp();
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tbase, TM_COLS);
+  }
 }
 
 // out[t, k] = bf16(sum over slots j in order of y[t * topk + j, k]).

@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(THR) xchg_kernel(Args a) {
   if (a.rank != a.dst) {
     // The slot (call & 1) was last used by call - 2: wait for its acknowledgement.
     if (t == 0) s_ok = call <= 2u || wait_at_least(&me->ack[c], call - 2u, a.status, deadline);
+    __syncwarp();   // warp 0 reconverges after lane 0's wait: one arrival per warp
     __syncthreads();
     if (!s_ok) return;
     __nv_bfloat16* dst = slot_of(a.buf[a.dst], call, a.rank, a.rows_max);
@@ -127,6 +128,7 @@ __global__ void __launch_bounds__(THR) xchg_kernel(Args a) {
   if (t == 0) s_ok = 1;
   __syncthreads();
   if (t < a.world && t != a.dst && !wait_at_least(&me->flag[t][c], call, a.status, deadline)) s_ok = 0;
+  __syncwarp();
   __syncthreads();
   if (!s_ok) return;
   for (int u = u0 + t; u < u1; u += THR) {

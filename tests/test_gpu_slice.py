@@ -111,7 +111,8 @@ def test_all_padding_gives_zero(small):
     ids = torch.full((3, 6), -1, dtype=torch.int32)
     tw = torch.zeros(3, 6)
     _, q, inv = H.activations(3, 1)
-    out = _run(ar, q, inv, ids, tw)
+    stale = torch.full((3, 5120), float("nan"), dtype=torch.bfloat16, device=ar.dev)   # must be overwritten
+    out = _run(ar, q, inv, ids, tw, out=stale)
     assert (out.float() == 0).all()
 
 
@@ -274,3 +275,12 @@ def test_config3_zipf_rows48_shard(cuda_ready, layout):
     ar, ids, tw, q, inv = _full_layer_case(cuda_ready, 3, 48, bias=bias, a0=2016, a1=2304, layout=layout)
     p, u = _check_full(ar, ids, tw, q, inv, 2016, 2304)
     print("config3 shard", p, "unique experts", u)
+
+
+@pytest.mark.parametrize("a0,a1", [(576, 1152), (1152, 1440), (0, 1152)])
+def test_config2_shards(cuda_ready, layout, a0, a1):
+    """BASELINE config 2 column shards (4-, 8- and 2-way splits): the 576- and
+    288-column shards run their down items in claimed batches of 2 and 4."""
+    ar, ids, tw, q, inv = _full_layer_case(cuda_ready, 2, 6, a0=a0, a1=a1, layout=layout)
+    p, u = _check_full(ar, ids, tw, q, inv, a0, a1)
+    print("config2 shard", (a0, a1), p, "unique experts", u)

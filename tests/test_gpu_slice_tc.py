@@ -24,7 +24,8 @@ def ws_offsets(rows, topk, width):
     """Byte offsets inside a qx_slice_decode_tc workspace (mirror of its layout)."""
     p, nt = rows * topk, (width + 63) // 64
     o, off = 0, {}
-    for name, size in [("ctl", 256), ("cnt1", p * 4), ("ready", p * 4), ("emax", p * 4), ("eloc", p * nt * 4),
+    for name, size in [("ctl", 256), ("cnt1", p * 4), ("ready", p * 4), ("fcnt", 40 * 4), ("emax", p * 4),
+                       ("eloc", p * nt * 4),
                        ("xexp", rows * 4), ("xt", rows * 10 * 4096)]:
         off[name] = o
         o = _al(o + size)
