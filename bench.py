@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -159,7 +160,8 @@ def run_ours(args) -> dict | None:
     ws = alloc_workspace(rows, TOPK, a0, a1, dev, args.layout)
     part = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
     gathered = [torch.empty_like(part) for _ in range(world)] if world > 1 and args.xchg == "nccl" else None
-    xchg = P2PExchange(rows_max=rows, dst=0, device=dev) if world > 1 and args.xchg == "p2p" else None
+    xchg = P2PExchange(rows_max=rows, dst=0, device=dev) if world > 1 and args.xchg in ("p2p", "fused") else None
+    fused = world > 1 and args.xchg == "fused"
 
     def exchange(p: torch.Tensor) -> torch.Tensor | None:
         if xchg is not None:
@@ -171,14 +173,32 @@ def run_ours(args) -> dict | None:
 
     def step(i: int) -> None:
         q, inv, ids, tw = dq[i % len(dq)]
-        launch(views[i % layers], q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=stream.cuda_stream,
-               layout=args.layout)
+        st = torch.cuda.current_stream(dev).cuda_stream   # the capture stream while a graph is recorded
+        if fused:   # slice and combine in one kernel per rank
+            xchg.slice_combine(views[i % layers], q, ids, tw, out, a0, a1, ws, x_scale=inv, stream=st)
+            return
+        launch(views[i % layers], q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=st, layout=args.layout)
         if world > 1:
             exchange(part)
 
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
+    # The device-timed steps replay one CUDA graph per (draw, layer) pair, as a
+    # serving loop replays its per-layer graphs: the host issues one graph launch
+    # per step instead of the Python argument set-up of every call.
+    graphs = None
+    if not args.no_graphs and not (world > 1 and args.xchg == "nccl"):
+        period = len(dq) * layers // math.gcd(len(dq), layers)
+        graphs = []
+        for j in range(period):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step(j)
+            graphs.append(g)
+        for i in range(args.warmup):
+            graphs[(args.warmup + i) % period].replay()
+        torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     ev0 = torch.cuda.Event(enable_timing=True)
@@ -187,7 +207,10 @@ def run_ours(args) -> dict | None:
         torch.cuda.synchronize()
         ev0.record(stream)
         for i in range(args.steps):
-            step(args.warmup + i)
+            if graphs is not None:
+                graphs[(2 * args.warmup + i) % len(graphs)].replay()
+            else:
+                step(2 * args.warmup + i)
         ev1.record(stream)
         torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
@@ -220,6 +243,11 @@ def run_ours(args) -> dict | None:
             return
         for d, s in zip(dev_in, src):
             d.copy_(s, non_blocking=True)
+        if fused:
+            if xchg.slice_combine(views[i % layers], dev_in[0], dev_in[2], dev_in[3], out, a0, a1, ws,
+                                  x_scale=dev_in[1], stream=stream.cuda_stream) is not None:
+                out_h.copy_(out, non_blocking=True)
+            return
         launch(views[i % layers], dev_in[0], dev_in[2], dev_in[3], part, a0, a1, ws, x_scale=dev_in[1],
                stream=stream.cuda_stream, layout=args.layout)
         if exchange(part) is not None:
@@ -279,10 +307,12 @@ def run_ours(args) -> dict | None:
                        "routing_draws": args.draws, "mean_unique_experts": round(mean_u, 2),
                        "zipf_s": args.zipf, "seed": args.seed,
                        "l2": "inputs larger than L2: ~%.0f MB of expert weights per step" % (mean_u * EXPERT_BYTES / 1e6),
+                       "timed_loop": "per-step CUDA graph replay" if graphs is not None else "eager calls",
                        "parallelism": f"column-split tp{world}",
-                       "exchange": None if world == 1 else (
-                           "one-shot NVLink store + rank-ordered FP32 sum kernel" if args.xchg == "p2p"
-                           else "NCCL all-gather + rank-ordered FP32 sum kernel"),
+                       "exchange": None if world == 1 else {
+                           "fused": "in the slice kernel: NVLink stores of each finalize unit + rank-ordered FP32 sum",
+                           "p2p": "one-shot NVLink store + rank-ordered FP32 sum kernel",
+                           "nccl": "NCCL all-gather + rank-ordered FP32 sum kernel"}[args.xchg],
                        "kernel": "tcgen05 mxf4nvf4 (16-term e2m1 activations)" if args.layout == "tc"
                        else "register dequant + mma.sync"},
             "tokens_per_s": round(rows / (us_layer * 1e-6), 1),
@@ -294,8 +324,10 @@ def run_ours(args) -> dict | None:
                          "kernel_us": round(k_mean, 3), "alg_bytes_per_launch": int(alg_bytes)},
             "e2e": {"value": round(us_e2e, 3), "unit": "us/layer", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            # prep + decode (tc) or prologue + main + finalize (frag) per step, + the combine kernel for N > 1
-            "gpu_launches": args.steps * (2 if args.layout == "tc" else 3) + (args.steps if world > 1 else 0),
+            # prep + decode (tc) or prologue + main + finalize (frag) per step, + a combine kernel for N > 1
+            # unless the combine is fused into the decode kernel
+            "gpu_launches": args.steps * (2 if args.layout == "tc" else 3)
+            + (args.steps if world > 1 and not fused else 0),
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu:
@@ -529,8 +561,11 @@ def main() -> int:
     ap.add_argument("--draws", type=int, default=16)
     ap.add_argument("--cpu-layers", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--xchg", default="p2p", choices=["p2p", "nccl"],
-                    help="N>1 combine: one-shot NVLink kernel (p2p) or NCCL all-gather + combine kernel")
+    ap.add_argument("--no-graphs", action="store_true",
+                    help="time the device loop with eager calls instead of per-step CUDA graph replays")
+    ap.add_argument("--xchg", default="fused", choices=["fused", "p2p", "nccl"],
+                    help="N>1 combine: fused into the slice kernel's finalize (fused), a separate one-shot "
+                         "NVLink kernel (p2p), or NCCL all-gather + combine kernel (nccl)")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
                     help="decode: BASELINE configs 1/2 (default); prefill: config 4 (2048-token W4A4 chunk)")
     ap.add_argument("--tokens", type=int, default=PREFILL_TOKENS)

@@ -231,6 +231,19 @@ size_t qx_arena_tc_w2_bytes(int32_t n_experts, int32_t width);
 size_t qx_slice_workspace_tc_bytes(int32_t rows, int32_t topk, int32_t c0, int32_t c1);
 int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* args, void* stream);
 
+/* The tensor-core slice with the rank combine fused into its finalize, one
+ * kernel per rank and call: each rank's BF16 partial goes straight from the
+ * finalize into the output rank's receive slots (the buffers of qx_xchg_alloc,
+ * mapped with qx_ipc_open; x->bufs, rank, world, dst, rows_max as for
+ * qx_combine_p2p), and the output rank writes bf16(sum over ranks in order of
+ * the partials [+ x->shared]) to args->out, as qx_combine_p2p would. Sender
+ * ranks do not write args->out; x->part, x->out and x->status are not used (a
+ * wait that runs out sets QX_DEV_TIMEOUT in the workspace status). A buffer
+ * serves either this call or qx_combine_p2p, not both interleaved. Replaces the
+ * slice + seam pair (gx/kernels/ext_variant.cu:11-24, then
+ * native/qmesh_afd_seam.cu:309-361). */
+int qx_slice_decode_tc_xchg(const QxArena* arena, const QxSliceArgs* args, const QxXchgArgs* x, void* stream);
+
 /* Self-check of the block-scaled NVFP4 tensor-core path (no counterpart in the
  * reference): d[128][n] (FP32, row-major) = sum over nkb 64-wide K blocks of
  * (A * SFA) x (B * SFB)^T, computed by tcgen05.mma.kind::mxf4nvf4 with the

@@ -58,6 +58,7 @@
 #include "qmesh_b200.h"
 #include "qx_ptx.cuh"
 #include "qx_tc.cuh"
+#include "qx_xchg.cuh"
 
 namespace qx {
 namespace tcd {
@@ -162,6 +163,12 @@ struct Params {
                       // bytes per slot, offset of the activation ring
   uint64_t timeout_ns;
   uint32_t dep_extra; // test hook: extra arrivals a down item waits for (0 in service)
+  // fused rank combine (qx_slice_decode_tc_xchg; xworld == 0 otherwise): every
+  // rank's exchange buffer, the optional shared-expert partial of the output rank
+  uint8_t* xbuf[QX_XCHG_MAX_RANKS];
+  const __nv_bfloat16* xshared;
+  int64_t xshared_stride;
+  int xrank, xworld, xdst, xrows_max;
 };
 
 struct ItemMeta {
@@ -568,6 +575,7 @@ struct Smem {       // fixed part of the dynamic shared memory, before the rings
   int32_t em[NEPI][GMAX];     // down item: the group's common activation exponents
   int32_t xe[NEPI][GMAX];     // gate/up item: the group's rows' x exponents
   float tws[NEPI][GMAX];      // down item: the group's routing weights
+  uint32_t xcall[NEPI];       // fused combine: the call number of the unit in hand
   RouteHdr hdr;
 };
 
@@ -762,44 +770,118 @@ __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS
 __device__ __forceinline__ bool second_acc(const ItemMeta& m) { return m.nst > 1 || m.nkb_last > 1; }
 
 
-// One finalize unit (output columns [128 tile, 128 tile + 128) of rows
-// [4 rb, 4 rb + 4)) by one epilogue group (et = 0..127), once every routed
-// pair's y covers the tile: out[row, k] = bf16(sum over slots j in order of
-// y[row * topk + j][k]), a slot without a valid expert adding 0. Thread et
-// takes 4 consecutive outputs of row 4 rb + et / 32.
-__device__ void finalize_unit(const Params& p, int tile, int rb, int et) {
-  const int k = tile * 128 + 4 * (et & 31);
-  const int row = 4 * rb + (et >> 5);
-  if (row < p.rows) {
-    float4 v[QX_MAX_TOPK];
-    bool val[QX_MAX_TOPK];
+// One finalize unit: output columns [128 tile, 128 tile + 128) of rows
+// [4 rb, 4 rb + 4), by one epilogue group (et = 0..127), once every routed
+// pair's y covers the tile. Thread et takes 4 consecutive outputs (column k) of
+// row 4 rb + et / 32: bf16(sum over slots j in order of y[row * topk + j][k]),
+// a slot without a valid expert adding 0. Returns the 4 BF16 values (zeros for a
+// row past the post's last).
+__device__ uint2 unit_partial(const Params& p, int tile, int rb, int et, int& row, int& k) {
+  k = tile * 128 + 4 * (et & 31);
+  row = 4 * rb + (et >> 5);
+  if (row >= p.rows) return make_uint2(0u, 0u);
+  float4 v[QX_MAX_TOPK];
+  bool val[QX_MAX_TOPK];
 #pragma unroll
-    for (int j = 0; j < QX_MAX_TOPK; ++j) {   // ids and y loads issued together
-      val[j] = false;
-      v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < p.topk) {
-        const int q = row * p.topk + j;
-        const long long id = p.ids64 ? __ldg(reinterpret_cast<const long long*>(p.ids) + q)
-                                     : (long long)__ldg(reinterpret_cast<const int*>(p.ids) + q);
-        val[j] = id >= 0 && id < p.E;
-        v[j] = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * HID + k));
-      }
+  for (int j = 0; j < QX_MAX_TOPK; ++j) {   // ids and y loads issued together
+    val[j] = false;
+    v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (j < p.topk) {
+      const int q = row * p.topk + j;
+      const long long id = p.ids64 ? __ldg(reinterpret_cast<const long long*>(p.ids) + q)
+                                   : (long long)__ldg(reinterpret_cast<const int*>(p.ids) + q);
+      val[j] = id >= 0 && id < p.E;
+      v[j] = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * HID + k));
     }
-    float4 s = val[0] ? v[0] : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int j = 1; j < QX_MAX_TOPK; ++j) {
-      const float4 z = val[j] ? v[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-      s.x += z.x;
-      s.y += z.y;
-      s.z += z.z;
-      s.w += z.w;
-    }
-    const __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
-    uint2 o;
-    o.x = *reinterpret_cast<const uint32_t*>(&lo);
-    o.y = *reinterpret_cast<const uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(p.out + (size_t)row * p.out_stride + k) = o;
   }
+  float4 s = val[0] ? v[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int j = 1; j < QX_MAX_TOPK; ++j) {
+    const float4 z = val[j] ? v[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s.x += z.x;
+    s.y += z.y;
+    s.z += z.z;
+    s.w += z.w;
+  }
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
+// Rank r's exchange buffer, chosen without indexing the parameter array at run
+// time (which would copy the parameters to local memory).
+__device__ __forceinline__ uint8_t* xbuf_at(const Params& p, int r) {
+  uint8_t* b = p.xbuf[0];
+#pragma unroll
+  for (int i = 1; i < QX_XCHG_MAX_RANKS; ++i)
+    if (r == i) b = p.xbuf[i];
+  return b;
+}
+
+__device__ __forceinline__ void add4(float (&s)[4], uint2 v) {
+  s[0] += __uint_as_float(v.x << 16);
+  s[1] += __uint_as_float(v.x & 0xffff0000u);
+  s[2] += __uint_as_float(v.y << 16);
+  s[3] += __uint_as_float(v.y & 0xffff0000u);
+}
+
+// Finalize unit u (tile, rb). Alone, it writes the output. In the fused rank
+// combine a sender stores its BF16 values straight into the output rank's
+// receive slot (peer memory, plain stores) once that slot's use two calls ago
+// is acknowledged and, after a barrier over the group, one thread fences at
+// system scope and releases the unit's flag; the
+// output rank acquires every sender's flag for the unit, sums the ranks' BF16
+// partials in FP32 in rank order (then the shared-expert partial) with one BF16
+// rounding (native/qmesh_afd_seam.cu:309-361) and acknowledges. Every wait is
+// bounded; false when one ran out (QX_DEV_TIMEOUT recorded).
+__device__ bool finalize_unit(const Params& p, Smem& S, int u, int tile, int rb, int et, int eg, int B1,
+                              uint32_t* status, uint64_t deadline) {
+  using namespace xb;
+  int row, k;
+  const uint2 mine = unit_partial(p, tile, rb, et, row, k);
+  const bool has = row < p.rows;
+  if (p.xworld == 0) {
+    if (has) *reinterpret_cast<uint2*>(p.out + (size_t)row * p.out_stride + k) = mine;
+    return true;
+  }
+  Hdr* me = reinterpret_cast<Hdr*>(xbuf_at(p, p.xrank));
+  bool ok = true;
+  if (et == 0) S.xcall[eg] = __ldcg(&me->useq[u]) + 1u;
+  if (p.xrank != p.xdst) {
+    if (et == 0) {
+      const uint32_t call = S.xcall[eg];
+      ok = call <= 2u || wait_at_least(&me->uack[u], call - 2u, status, deadline);
+    }
+    if (!bar_and(B1, 128, ok)) return false;
+    const uint32_t call = S.xcall[eg];
+    if (has)
+      *reinterpret_cast<uint2*>(slot_of(xbuf_at(p, p.xdst), call, p.xrank, p.xrows_max) + (size_t)row * HID + k) = mine;
+    asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");   // the group's stores, then one fence and release
+    if (et == 0) {
+      fence_acq_rel_sys();
+      st_release_sys(&reinterpret_cast<Hdr*>(xbuf_at(p, p.xdst))->uflag[p.xrank][u], call);
+      me->useq[u] = call;
+    }
+    return true;
+  }
+  asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
+  const uint32_t call = S.xcall[eg];
+  if (et < p.xworld && et != p.xdst) ok = wait_at_least(&me->uflag[et][u], call, status, deadline);
+  if (!bar_and(B1, 128, ok)) return false;
+  if (has) {
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < p.xworld; ++r)
+      add4(s, r == p.xdst ? mine
+                          : __ldcg(reinterpret_cast<const uint2*>(slot_of(xbuf_at(p, p.xrank), call, r, p.xrows_max) +
+                                                                  (size_t)row * HID + k)));
+    if (p.xshared) add4(s, *reinterpret_cast<const uint2*>(p.xshared + (size_t)row * p.xshared_stride + k));
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(s[0], s[1]), hi = __floats2bfloat162_rn(s[2], s[3]);
+    *reinterpret_cast<uint2*>(p.out + (size_t)row * p.out_stride + k) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+  }
+  asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");   // every slot read has returned its value
+  if (et < p.xworld && et != p.xdst) st_release_sys(&reinterpret_cast<Hdr*>(xbuf_at(p, et))->uack[u], call);
+  if (et == 0) me->useq[u] = call;
+  return true;
 }
 
 // Epilogue warpgroup eg (warps 2-5 or 7-10): the items of accumulator buffer
@@ -1000,7 +1082,7 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
     bool ok = true;
     if (et == 0) ok = wait_flag(&p.fcnt[tile], (uint32_t)S.hdr.n_pairs, status, deadline);
     if (!bar_and(B1, 128, ok)) break;   // every thread's y reads follow thread 0's acquire
-    finalize_unit(p, tile, u - tile * rbn, et);
+    if (!finalize_unit(p, S, u, tile, u - tile * rbn, et, eg, B1, const_cast<uint32_t*>(status), deadline)) break;
   }
 }
 
@@ -1162,7 +1244,10 @@ size_t qx_slice_workspace_tc_bytes(int32_t rows, int32_t topk, int32_t c0, int32
   return ws_layout(rows, topk, c1 - c0).total;
 }
 
-int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream) {
+}  // extern "C"
+
+// The slice call, alone (x == nullptr) or with the fused rank combine.
+static int tc_launch(const QxArena* arena, const QxSliceArgs* a, const QxXchgArgs* x, void* stream) {
   if (!arena || !a) return QX_ERR_ARG;
   if (!a->x || !a->ids || !a->tw || !a->out || !a->workspace || !arena->w13 || !arena->w2 || !arena->g13 ||
       !arena->g2)
@@ -1239,6 +1324,30 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream)
   p.ns = p.b_off = 0;
   p.timeout_ns = timeout_ns();
   p.dep_extra = dep_extra();
+  p.xworld = 0;
+  p.xshared = nullptr;
+  p.xshared_stride = 0;
+  p.xrank = p.xdst = p.xrows_max = 0;
+  for (int r = 0; r < QX_XCHG_MAX_RANKS; ++r) p.xbuf[r] = nullptr;
+  if (x && x->world > 1) {
+    if (x->world > QX_XCHG_MAX_RANKS || x->rank < 0 || x->rank >= x->world || x->dst < 0 || x->dst >= x->world)
+      return QX_ERR_ARG;
+    if (x->rows_max < a->rows || x->rows_max > QX_MAX_ROWS) return QX_ERR_SHAPE;
+    for (int r = 0; r < x->world; ++r) {
+      if (!x->bufs[r] || (reinterpret_cast<uintptr_t>(x->bufs[r]) & 255u)) return QX_ERR_ARG;
+      p.xbuf[r] = reinterpret_cast<uint8_t*>(x->bufs[r]);
+    }
+    if (x->rank == x->dst && x->shared) {
+      if ((reinterpret_cast<uintptr_t>(x->shared) & 7u) || (x->shared_stride & 3) || x->shared_stride < HID)
+        return QX_ERR_ALIGN;
+      p.xshared = reinterpret_cast<const __nv_bfloat16*>(x->shared);
+      p.xshared_stride = x->shared_stride;
+    }
+    p.xworld = x->world;
+    p.xrank = x->rank;
+    p.xdst = x->dst;
+    p.xrows_max = x->rows_max;
+  }
   const size_t smem_bytes = SMEM_LIMIT;
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -1257,6 +1366,17 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream)
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, tc_decode_kernel, p) != cudaSuccess) return QX_ERR_LAUNCH;
   return QX_OK;
+}
+
+extern "C" {
+
+int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream) {
+  return tc_launch(arena, a, nullptr, stream);
+}
+
+int qx_slice_decode_tc_xchg(const QxArena* arena, const QxSliceArgs* a, const QxXchgArgs* x, void* stream) {
+  if (!x) return QX_ERR_ARG;
+  return tc_launch(arena, a, x, stream);
 }
 
 }  // extern "C"

@@ -4,19 +4,11 @@
 // one BF16 rounding (native/qmesh_afd_seam.cu:309-361 seam_combine_kernel; the
 // fixed NODE-A, NODE-B, NODE-C, shared order of README.md:88-90).
 //
-// Each rank owns one exchange buffer (cudaMalloc'd by qx_xchg_alloc, mapped into
-// every other rank's address space with CUDA IPC):
-//   header: flag[sender][chunk]  written by the sender into the output rank's
-//                                buffer: the call number whose chunk has landed;
-//           ack[chunk]           written by the output rank into each sender's
-//                                buffer: the last call number it has consumed;
-//           seq[chunk]           this rank's own call counter per chunk;
-//   slots:  [2][sender][rows_max][5120] BF16 receive slots, alternating by call
-//           number, so a sender may run one call ahead of the output rank.
+// Each rank owns one exchange buffer (layout in qx_xchg.cuh).
 // One CTA per chunk of the [rows, 5120] partial. A sender's CTA waits until its
 // slot's previous use is acknowledged, stores its chunk straight into the output
-// rank's slot with plain 16-byte stores, fences at system scope and releases the
-// chunk's flag. The output rank's CTA acquires every sender's flag for its chunk,
+// rank's slot with plain 16-byte stores and, after a barrier, one thread fences
+// at system scope and releases the chunk's flag. The output rank's CTA acquires every sender's flag for its chunk,
 // sums in rank order (its own partial from local memory) and acknowledges. No
 // bulk-copy or tensor-memory-access instruction touches peer memory, and nothing
 // here maps memory for in-switch reduction. Every wait is bounded
@@ -29,21 +21,14 @@
 
 #include "qmesh_b200.h"
 #include "qx_ptx.cuh"
+#include "qx_xchg.cuh"
 
 namespace qx {
 namespace xchg {
 
+using namespace xb;
 constexpr int HID = QX_HIDDEN;
-constexpr int MAXW = QX_XCHG_MAX_RANKS;
-constexpr int NCH = 64;        // chunks = CTAs per call
-constexpr int THR = 256;
-
-struct Hdr {
-  uint32_t flag[MAXW][NCH];
-  uint32_t ack[NCH];
-  uint32_t seq[NCH];
-};
-constexpr size_t HDR_BYTES = (sizeof(Hdr) + 255) & ~size_t(255);
+constexpr int THR = 256;       // threads per chunk CTA (NCH CTAs per call)
 
 struct Args {
   uint8_t* buf[MAXW];          // every rank's exchange buffer (own included), in this address space
@@ -57,31 +42,6 @@ struct Args {
   int rank, world, dst, rows, rows_max;
   uint64_t timeout_ns;
 };
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Bounded wait until (int)(*p - need) >= 0.
-__device__ bool wait_at_least(const uint32_t* p, uint32_t need, uint32_t* status, uint64_t deadline) {
-  for (uint32_t it = 0;; ++it) {
-    if ((int32_t)(ld_acquire_sys(p) - need) >= 0) return true;
-    if ((it & 63u) == 63u && globaltimer_ns() > deadline) {
-      atomicOr(status, (uint32_t)QX_DEV_TIMEOUT);
-      return false;
-    }
-    if (it > 8) __nanosleep(32);
-  }
-}
-
-__device__ __forceinline__ __nv_bfloat16* slot_of(uint8_t* buf, uint32_t call, int sender, int rows_max) {
-  return reinterpret_cast<__nv_bfloat16*>(buf + HDR_BYTES) + ((size_t)(call & 1u) * MAXW + sender) * rows_max * HID;
-}
 
 __device__ __forceinline__ void add8(float (&s)[8], uint4 v) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -115,9 +75,9 @@ __global__ void __launch_bounds__(THR) xchg_kernel(Args a) {
       const uint4 v = *reinterpret_cast<const uint4*>(a.part + (size_t)row * a.part_stride + k);
       *reinterpret_cast<uint4*>(dst + (size_t)row * HID + k) = v;
     }
-    __threadfence_system();
-    __syncthreads();
+    __syncthreads();   // the CTA's stores, then one system-scope fence and release
     if (t == 0) {
+      fence_acq_rel_sys();
       st_release_sys(&reinterpret_cast<Hdr*>(a.buf[a.dst])->flag[a.rank][c], call);
       me->seq[c] = call;
     }

@@ -145,6 +145,8 @@ SIGNATURES = [
     ("qx_ipc_handle", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     ("qx_ipc_open", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
     ("qx_ipc_close", ctypes.c_int, [ctypes.c_void_p]),
+    ("qx_slice_decode_tc_xchg", ctypes.c_int,
+     [ctypes.POINTER(QxArena), ctypes.POINTER(QxSliceArgs), ctypes.POINTER(QxXchgArgs), ctypes.c_void_p]),
     ("qx_combine_p2p", ctypes.c_int, [ctypes.POINTER(QxXchgArgs), ctypes.c_void_p]),
     ("qx_version", ctypes.c_char_p, []),
 ]

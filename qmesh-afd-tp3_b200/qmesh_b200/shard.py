@@ -59,7 +59,8 @@ def combine_across_ranks(part: torch.Tensor, group=None, dst: int = 0, shared: t
 
 
 class P2PExchange:
-    """One-shot rank-ordered combine over NVLink peer memory (`qx_combine_p2p`).
+    """One-shot rank-ordered combine over NVLink peer memory (`qx_combine_p2p`,
+    or fused into the slice kernel by `slice_combine`).
 
     The B200 replacement of the reference's RDMA seam between the column-split
     nodes (native/qmesh_afd_seam.cu:309-361): each rank's BF16 partial is stored
@@ -114,9 +115,40 @@ class P2PExchange:
         self._args.status = self.status.data_ptr()
         dist.barrier(group=group)   # every rank has mapped every buffer before the first step
 
+    def _use(self, mode: str) -> None:
+        # One buffer serves one protocol: the two keep separate call counters.
+        if getattr(self, "_mode", None) not in (None, mode):
+            raise RuntimeError(f"this exchange already runs the {self._mode} protocol")
+        self._mode = mode
+
+    def slice_combine(self, view, x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, out: torch.Tensor,
+                      c0: int, c1: int, workspace: torch.Tensor, x_scale: torch.Tensor | None = None,
+                      shared: torch.Tensor | None = None, stream=None, **kw) -> torch.Tensor | None:
+        """The slice of this rank's columns with the combine fused into its
+        finalize (`qx_slice_decode_tc_xchg`): one kernel per rank and step. On
+        the output rank `out` receives bf16(p0 + ... [+ shared]) and is returned;
+        senders do not write `out` and get None. A wait that runs out sets
+        QX_DEV_TIMEOUT in the workspace status (`expert_slice.device_status`)."""
+        from .expert_slice import launch
+        self._use("fused")
+        rows = x.shape[0]
+        if not 1 <= rows <= self.rows_max:
+            raise ValueError(f"rows {rows} outside 1..{self.rows_max}")
+        a = self._L.QxXchgArgs()
+        for r in range(self.world):
+            a.bufs[r] = self._args.bufs[r]
+        a.rank, a.world, a.dst, a.rows, a.rows_max = self.rank, self.world, self.dst, rows, self.rows_max
+        if shared is not None and self.rank == self.dst:
+            if shared.dtype != torch.bfloat16 or tuple(shared.shape) != (rows, self._L.HIDDEN) or shared.stride(1) != 1:
+                raise TypeError("shared partial must be bf16 [rows, 5120] with unit column stride")
+            a.shared, a.shared_stride = shared.data_ptr(), shared.stride(0)
+        launch(view, x, ids, tw, out, c0, c1, workspace, x_scale=x_scale, stream=stream, layout="tc", xchg=a, **kw)
+        return out if self.rank == self.dst else None
+
     def combine(self, part: torch.Tensor, out: torch.Tensor | None = None, shared: torch.Tensor | None = None,
                 stream=None) -> torch.Tensor | None:
         """Sends this rank's partial; on the output rank returns bf16(p0 + ... [+ shared])."""
+        self._use("chunk")
         if part.dtype != torch.bfloat16 or part.dim() != 2 or part.shape[1] != self._L.HIDDEN or part.stride(1) != 1:
             raise TypeError("partial must be bf16 [rows, 5120] with unit column stride")
         rows = part.shape[0]

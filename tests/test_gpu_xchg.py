@@ -137,3 +137,139 @@ def test_p2p_combine_reports_a_missing_rank():
     assert res[0][2] == res[1][2] == 999000.0
     want = moe.combine_ordered([_part(0, 0, 6).float(), _part(0, 1, 6).float()]).to(torch.bfloat16).float()
     assert torch.equal(torch.from_numpy(res[0][3]), want)
+
+
+# ---- the slice with the combine fused into its finalize (qx_slice_decode_tc_xchg)
+
+def _fused_case(step, rows, n_experts=16):
+    from oracle import moe
+    g = torch.Generator().manual_seed(500 + step)
+    ids, tw = moe.routing(torch.randn(rows, n_experts, generator=g))
+    _, q, inv = moe.make_activation(rows, g)
+    return ids, tw, q, inv
+
+
+def _fused_worker(rank, world, port, rows, dst, q):
+    import sys
+    for p in (str(ROOT), str(PKG)):
+        sys.path.insert(0, p)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from qmesh_b200 import shard
+    from qmesh_b200.arena import Arena
+    from qmesh_b200.expert_slice import alloc_workspace, device_status, expert_slice
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=dev, timeout=__import__("datetime").timedelta(seconds=60))
+    xf = xc = None
+    try:
+        a0, a1 = shard.shard_range(rank, world)
+        ar = Arena(dev, 1, 16, a0, a1)
+        ar.fill_synthetic(0, seed=7)
+        xf = shard.P2PExchange(rows_max=8, dst=dst, device=dev)   # fused protocol
+        xc = shard.P2PExchange(rows_max=8, dst=dst, device=dev)   # chunk protocol, for the comparison
+        ws = alloc_workspace(rows, 6, a0, a1, dev)
+        shared = torch.full((rows, 5120), 0.25, dtype=torch.bfloat16, device=dev)
+        equal, statuses = [], []
+        for step in range(STEPS):
+            ids, tw, xq, inv = (t.to(dev) for t in _fused_case(step, rows))
+            sh = shared if (rank == dst and step % 2) else None
+            out = torch.full((rows, 5120), float("nan"), dtype=torch.bfloat16, device=dev)
+            got = xf.slice_combine(ar.view(0), xq, ids, tw, out, a0, a1, ws, x_scale=inv, shared=sh)
+            statuses.append(device_status(ws))
+            part = expert_slice(ar, 0, xq, ids, tw, x_scale=inv)
+            want = xc.combine(part, shared=sh)
+            torch.cuda.synchronize()
+            if rank == dst:
+                equal.append(bool(torch.equal(got, want)))
+        q.put((rank, equal, statuses, int(xc.status.item())))
+    finally:
+        for x in (xf, xc):
+            if x is not None:
+                x.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("rows,dst", [(6, 0), (3, 1)])
+def test_fused_slice_combine_equals_slice_then_combine(rows, dst):
+    """Over consecutive steps (both receive slots, the acknowledgements) the fused
+    kernel's output on the output rank equals the separate slice partials combined
+    by qx_combine_p2p, bit for bit, with and without a shared-expert partial."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = min(torch.cuda.device_count(), 8)
+    port = 29600 + os.getpid() % 200 + rows
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, rows, dst, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, equal, statuses, st = q.get(timeout=300)
+        res[r] = (equal, statuses, st)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert res[r][1] == [0] * STEPS and res[r][2] == 0, f"rank {r}: {res[r][1]} {res[r][2]}"
+    assert res[dst][0] == [True] * STEPS
+
+
+def _fused_lost_worker(rank, world, port, q):
+    import sys
+    for p in (str(ROOT), str(PKG)):
+        sys.path.insert(0, p)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["QX_TIMEOUT_MS"] = "400"
+    from qmesh_b200 import shard
+    from qmesh_b200.arena import Arena
+    from qmesh_b200.expert_slice import alloc_workspace, device_status
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=dev, timeout=__import__("datetime").timedelta(seconds=60))
+    xf = None
+    try:
+        a0, a1 = shard.shard_range(rank, world)
+        ar = Arena(dev, 1, 16, a0, a1)
+        ar.fill_synthetic(0, seed=7)
+        xf = shard.P2PExchange(rows_max=8, dst=0, device=dev)
+        ws = alloc_workspace(6, 6, a0, a1, dev)
+        ids, tw, xq, inv = (t.to(dev) for t in _fused_case(0, 6))
+        out = torch.empty(6, 5120, dtype=torch.bfloat16, device=dev)
+        xf.slice_combine(ar.view(0), xq, ids, tw, out, a0, a1, ws, x_scale=inv)   # step 0: every rank
+        st0 = device_status(ws)
+        if rank == 0:
+            xf.slice_combine(ar.view(0), xq, ids, tw, out, a0, a1, ws, x_scale=inv)   # rank 1 never sends
+        st1 = device_status(ws)
+        probe = float((torch.arange(1000, device=dev, dtype=torch.float32) * 2).sum().item())
+        q.put((rank, st0, st1, probe))
+    finally:
+        if xf is not None:
+            xf.close()
+        dist.destroy_process_group()
+
+
+def test_fused_combine_reports_a_missing_rank():
+    """Rank 1 skips a step of the fused kernel (between steps, nothing in flight):
+    rank 0's bounded waits run out, QX_DEV_TIMEOUT lands in its workspace status
+    and the GPU context goes on working."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    port = 29800 + os.getpid() % 90
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_fused_lost_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, st0, st1, probe = q.get(timeout=300)
+        res[r] = (st0, st1, probe)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert res[0][0] == 0 and res[1][0] == 0
+    assert res[0][1] & 2 and res[1][1] == 0
+    assert res[0][2] == res[1][2] == 999000.0
