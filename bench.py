@@ -40,8 +40,8 @@ N_EXPERTS = 384
 TOPK = 6
 EXPERT_BYTES = 2 * INTER * (HIDDEN // 2 + HIDDEN // 16) + HIDDEN * (INTER // 2 + INTER // 16)  # 19,906,560
 # DRAM bytes (read + write) per unique expert per launch of tc_decode_kernel, from the ncu capture in
-# profiles/tc_decode_kernel_config1.md (544.78 MB over 27 unique experts, full 2304 columns).
-DRAM_BYTES_PER_UNIQUE = 544.78e6 / 27
+# profiles/tc_decode_kernel_config1.md (544.03 MB over 27 unique experts, full 2304 columns).
+DRAM_BYTES_PER_UNIQUE = 544.03e6 / 27
 METRIC = "MoE-layer decode µs (6 rows) & NVFP4 weight GB/s vs HBM peak, 1/2/4/8 GPU"
 
 
