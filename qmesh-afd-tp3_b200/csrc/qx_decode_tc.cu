@@ -825,14 +825,14 @@ __device__ __forceinline__ void add4(float (&s)[4], uint2 v) {
 }
 
 // Finalize unit u (tile, rb). Alone, it writes the output. In the fused rank
-// combine a sender stores its BF16 values straight into the output rank's
-// receive slot (peer memory, plain stores) once that slot's use two calls ago
-// is acknowledged and, after a barrier over the group, one thread fences at
-// system scope and releases the unit's flag; the
-// output rank acquires every sender's flag for the unit, sums the ranks' BF16
-// partials in FP32 in rank order (then the shared-expert partial) with one BF16
-// rounding (native/qmesh_afd_seam.cu:309-361) and acknowledges. Every wait is
-// bounded; false when one ran out (QX_DEV_TIMEOUT recorded).
+// combine a sender, once the output rank has acknowledged its use of the same
+// receive words two calls ago, stores each thread's 8 BF16 bytes as two 64-bit
+// words {data, call} straight into the output rank's buffer (plain stores over
+// NVLink; a word validates itself, so no fence and no flag); the output rank
+// polls every sender's words for the call, sums the ranks' BF16 partials in
+// FP32 in rank order (then the shared-expert partial) with one BF16 rounding
+// (native/qmesh_afd_seam.cu:309-361) and acknowledges. Every wait is bounded;
+// false when one ran out (QX_DEV_TIMEOUT recorded).
 __device__ bool finalize_unit(const Params& p, Smem& S, int u, int tile, int rb, int et, int eg, int B1,
                               uint32_t* status, uint64_t deadline) {
   using namespace xb;
@@ -853,32 +853,32 @@ __device__ bool finalize_unit(const Params& p, Smem& S, int u, int tile, int rb,
     }
     if (!bar_and(B1, 128, ok)) return false;
     const uint32_t call = S.xcall[eg];
-    if (has)
-      *reinterpret_cast<uint2*>(slot_of(xbuf_at(p, p.xdst), call, p.xrank, p.xrows_max) + (size_t)row * HID + k) = mine;
-    asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");   // the group's stores, then one fence and release
-    if (et == 0) {
-      fence_acq_rel_sys();
-      st_release_sys(&reinterpret_cast<Hdr*>(xbuf_at(p, p.xdst))->uflag[p.xrank][u], call);
-      me->useq[u] = call;
+    if (has) {
+      uint64_t* w = words_of(xbuf_at(p, p.xdst), call, p.xrank, p.xrows_max, row, k);
+      st_relaxed_sys_b64(w, (uint64_t)call << 32 | mine.x);
+      st_relaxed_sys_b64(w + 1, (uint64_t)call << 32 | mine.y);
     }
+    if (et == 0) me->useq[u] = call;
     return true;
   }
   asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
   const uint32_t call = S.xcall[eg];
-  if (et < p.xworld && et != p.xdst) ok = wait_at_least(&me->uflag[et][u], call, status, deadline);
-  if (!bar_and(B1, 128, ok)) return false;
   if (has) {
+    uint8_t* own = xbuf_at(p, p.xrank);
     float s[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int r = 0; r < p.xworld; ++r)
-      add4(s, r == p.xdst ? mine
-                          : __ldcg(reinterpret_cast<const uint2*>(slot_of(xbuf_at(p, p.xrank), call, r, p.xrows_max) +
-                                                                  (size_t)row * HID + k)));
+    for (int r = 0; r < p.xworld && ok; ++r) {
+      uint2 v = mine;
+      if (r != p.xdst) ok = words_wait(words_of(own, call, r, p.xrows_max, row, k), call, v, status, deadline);
+      add4(s, v);
+    }
     if (p.xshared) add4(s, *reinterpret_cast<const uint2*>(p.xshared + (size_t)row * p.xshared_stride + k));
     const __nv_bfloat162 lo = __floats2bfloat162_rn(s[0], s[1]), hi = __floats2bfloat162_rn(s[2], s[3]);
-    *reinterpret_cast<uint2*>(p.out + (size_t)row * p.out_stride + k) =
-        make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+    if (ok)
+      *reinterpret_cast<uint2*>(p.out + (size_t)row * p.out_stride + k) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
   }
-  asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");   // every slot read has returned its value
+  // Every word read above has returned its value: the senders may reuse them.
+  if (!bar_and(B1, 128, ok)) return false;
   if (et < p.xworld && et != p.xdst) st_release_sys(&reinterpret_cast<Hdr*>(xbuf_at(p, et))->uack[u], call);
   if (et == 0) me->useq[u] = call;
   return true;

@@ -132,7 +132,7 @@ extern "C" {
 
 size_t qx_xchg_bytes(int32_t rows_max) {
   if (rows_max < 1 || rows_max > QX_MAX_ROWS) return 0;
-  return HDR_BYTES + (size_t)2 * MAXW * rows_max * HID * sizeof(uint16_t);
+  return HDR_BYTES + slots_bytes(rows_max) + words_bytes(rows_max);
 }
 
 int qx_xchg_alloc(int32_t rows_max, void** buf) {
