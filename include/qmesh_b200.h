@@ -233,10 +233,11 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* args, void* stre
 
 /* The tensor-core slice with the rank combine fused into its finalize, one
  * kernel per rank and call: each rank's BF16 partial goes straight from the
- * finalize into the output rank's receive slots (the buffers of qx_xchg_alloc,
- * mapped with qx_ipc_open; x->bufs, rank, world, dst, rows_max as for
- * qx_combine_p2p), and the output rank writes bf16(sum over ranks in order of
- * the partials [+ x->shared]) to args->out, as qx_combine_p2p would. Sender
+ * finalize into the output rank's receive words (64-bit words that carry the
+ * call number beside 4 data bytes, in the buffers of qx_xchg_alloc mapped with
+ * qx_ipc_open; x->bufs, rank, world, dst, rows_max as for qx_combine_p2p), and
+ * the output rank writes bf16(sum over ranks in order of the partials
+ * [+ x->shared]) to args->out, as qx_combine_p2p would. Sender
  * ranks do not write args->out; x->part, x->out and x->status are not used (a
  * wait that runs out sets QX_DEV_TIMEOUT in the workspace status). A buffer
  * serves either this call or qx_combine_p2p, not both interleaved. Replaces the

@@ -120,6 +120,20 @@ def test_size_queries(lib):
     assert lib.qx_slice_workspace_bytes(1, 9, 0, 2304) == 0
 
 
+def test_exchange_buffer_layout(lib):
+    """Exchange buffer = header (chunk flags/acks/seqs for 8 ranks x 64 chunks,
+    unit acks/seqs for 40 x 16 finalize units, 256-aligned) + the BF16 slots of
+    the chunk protocol [2][8][rows_max][5120] + the 64-bit receive words of the
+    fused protocol [2][8][rows_max][1280][2]."""
+    from qmesh_b200 import _lib
+    hdr = (8 * 64 + 64 + 64 + 640 + 640) * 4
+    hdr = (hdr + 255) // 256 * 256
+    for rows_max in (1, 6, 64):
+        want = hdr + 2 * 8 * rows_max * 5120 * 2 + 2 * 8 * rows_max * 1280 * 2 * 8
+        assert lib.qx_xchg_bytes(rows_max) == want
+    assert lib.qx_xchg_bytes(0) == 0 and lib.qx_xchg_bytes(_lib.MAX_ROWS + 1) == 0
+
+
 def test_decode_rejects_bad_arguments_before_touching_the_device(lib):
     from qmesh_b200 import _lib
     ar = _lib.QxArena(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16),
