@@ -316,7 +316,9 @@ def run_ours(args) -> dict | None:
                        "kernel": "tcgen05 mxf4nvf4 (16-term e2m1 activations)" if args.layout == "tc"
                        else "register dequant + mma.sync"},
             "tokens_per_s": round(rows / (us_layer * 1e-6), 1),
-            "weight_gbs": round(gbs, 1),
+            "weight_gbs": round(gbs, 1),   # per rank: its shard's bytes over its slice kernel time
+            # whole step: every rank's weight bytes over the step time (the config-2 aggregate)
+            "aggregate_weight_gbs": round(mean_u * EXPERT_BYTES / (us_layer * 1e-6) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "peak_kind": peak_kind,
                          "traffic": int(mean_u * DRAM_BYTES_PER_UNIQUE * width / INTER),
