@@ -259,8 +259,12 @@ def run_ours(args) -> dict | None:
     if world > 1:
         dist.barrier()
     ev0.record(stream)
+    if hslice is not None:
+        hslice.order_after(stream)   # the first step's input copy starts inside the timed region
     for i in range(args.steps):
         e2e_step(i)
+    if hslice is not None:
+        hslice.join(stream)   # the last step's output copy runs on the host-slice's copy stream
     ev1.record(stream)
     torch.cuda.synchronize()
     ms_e2e = ev0.elapsed_time(ev1)

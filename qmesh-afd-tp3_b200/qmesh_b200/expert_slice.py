@@ -222,11 +222,14 @@ class HostSlice:
     x (FP8 e4m3 [rows, 5120]), its per-row FP32 scale, ids and tw into one pinned
     staging buffer, moves them with ONE host-to-device copy, runs the slice on
     views of the device copy and brings the BF16 output back with one
-    device-to-host copy, all on one stream and without synchronising the host.
-    Two staging slots alternate, each guarded by an event, so the host can pack
-    call k+1 while call k runs. The returned host tensor belongs to that call's
-    slot and stays valid until the call after next; read it after
-    `torch.cuda.current_stream().synchronize()` (or `done(out)`).
+    device-to-host copy, without synchronising the host. The copies run on two
+    side streams of their own, so call k+1's inputs move while call k computes
+    and call k's output moves while call k+1 computes; the slice itself runs on
+    the caller's current stream, after its inputs have landed. Two staging slots
+    alternate, each guarded by events. The returned host tensor belongs to that
+    call's slot and stays valid until the call after next; read it after
+    `synchronize()` (host) or `join(stream)` (device ordering) or a device-wide
+    synchronisation.
     """
 
     def __init__(self, arena: Arena, rows: int, topk: int = 6, c0: int | None = None, c1: int | None = None,
@@ -247,8 +250,13 @@ class HostSlice:
         self.dev = [torch.empty(self.nbytes, dtype=torch.uint8, device=dev) for _ in range(slots)]
         self.out_d = [torch.empty(rows, _lib.HIDDEN, dtype=torch.bfloat16, device=dev) for _ in range(slots)]
         self.out_h = [torch.empty(rows, _lib.HIDDEN, dtype=torch.bfloat16).pin_memory() for _ in range(slots)]
-        self.events = [torch.cuda.Event() for _ in range(slots)]
+        self.in_stream = torch.cuda.Stream(dev)
+        self.out_stream = torch.cuda.Stream(dev)
+        self.ev_in = [torch.cuda.Event() for _ in range(slots)]     # the slot's inputs have landed
+        self.ev_done = [torch.cuda.Event() for _ in range(slots)]   # the slot's slice has run
+        self.ev_out = [torch.cuda.Event() for _ in range(slots)]    # the slot's output has reached the host
         self.used = [False] * slots
+        self.last: int | None = None
         self.ws = alloc_workspace(rows, topk, self.c0, self.c1, dev, arena.layout)
         self.k = 0
 
@@ -267,7 +275,9 @@ class HostSlice:
         k = self.k
         self.k = (k + 1) % len(self.host)
         if self.used[k]:
-            self.events[k].synchronize()              # the slot's previous call has left it
+            # The slot's previous call has left it: inputs consumed, output copied out
+            # (so its host buffers and its device output may be reused).
+            self.ev_out[k].synchronize()
         with rng("qx.host_stage"):
             hx, hs, hi, ht = self._views(self.host[k], n)
             hx.copy_(x.view(torch.uint8) if x.dtype != torch.uint8 else x)
@@ -276,14 +286,36 @@ class HostSlice:
             ht.copy_(tw)
         stream = torch.cuda.current_stream(self.arena.dev)
         used = self.o_t + _al16(n * self.topk * 4) if n == self.rows else self.nbytes
-        with rng("qx.h2d"):
+        if self.used[k]:
+            self.in_stream.wait_event(self.ev_done[k])     # the slot's previous slice has read its inputs
+        with rng("qx.h2d"), torch.cuda.stream(self.in_stream):
             self.dev[k][:used].copy_(self.host[k][:used], non_blocking=True)
+        self.ev_in[k].record(self.in_stream)
+        stream.wait_event(self.ev_in[k])
         dx, ds, di, dt = self._views(self.dev[k], n)
         launch(self.arena.view(li), dx.view(torch.float8_e4m3fn), di, dt, self.out_d[k][:n], self.c0, self.c1,
                self.ws, x_scale=ds, swiglu_limit=self.limit, has_limit=self.has_limit, stream=stream.cuda_stream,
                layout=self.arena.layout)
-        with rng("qx.d2h"):
+        self.ev_done[k].record(stream)
+        self.out_stream.wait_event(self.ev_done[k])
+        with rng("qx.d2h"), torch.cuda.stream(self.out_stream):
             self.out_h[k][:n].copy_(self.out_d[k][:n], non_blocking=True)
-        self.events[k].record(stream)
+        self.ev_out[k].record(self.out_stream)
         self.used[k] = True
+        self.last = k
         return self.out_h[k][:n]
+
+    def order_after(self, stream=None) -> None:
+        """Order the next calls' input copies after the work queued so far on
+        `stream` (default: the current stream), e.g. a timing event."""
+        self.in_stream.wait_stream(stream or torch.cuda.current_stream(self.arena.dev))
+
+    def join(self, stream=None) -> None:
+        """Order `stream` (default: the current stream) after every call's output copy."""
+        if self.last is not None:
+            (stream or torch.cuda.current_stream(self.arena.dev)).wait_event(self.ev_out[self.last])
+
+    def synchronize(self) -> None:
+        """Block the host until every call's output is in host memory."""
+        if self.last is not None:
+            self.ev_out[self.last].synchronize()

@@ -114,3 +114,29 @@ def test_host_slice_matches_device_call(cuda_ready):
         outs.append((got, want))
         torch.cuda.synchronize()
         assert torch.equal(got, want.cpu()), f"call {step}"
+
+
+def test_host_slice_pipelined_calls(cuda_ready):
+    """Back-to-back HostSlice calls with no host synchronisation between them
+    (input copies overlap the previous call's slice, output copies the next
+    call's): after synchronize() the last two calls' outputs (one per staging
+    slot) equal the device calls'."""
+    from qmesh_b200.arena import Arena
+    from qmesh_b200.expert_slice import HostSlice, expert_slice
+    dev = cuda_ready
+    layer = H.small_layer(34, 8, inter=256)
+    ar = Arena(dev, 1, 8, 0, 256, layout="tc")
+    ar.load_layer(0, layer)
+    hs = HostSlice(ar, 6)
+    cases, got = [], []
+    for step in range(5):
+        ids, tw = H.random_routing(6, 8, 70 + step)
+        _, q, inv = H.activations(6, 70 + step)
+        cases.append((q, inv, ids, tw))
+        got.append(hs(0, q, inv, ids, tw))
+    hs.synchronize()
+    for step in (3, 4):
+        q, inv, ids, tw = cases[step]
+        want = expert_slice(ar, 0, q.to(dev), ids.to(dev), tw.to(dev), x_scale=inv.to(dev))
+        torch.cuda.synchronize()
+        assert torch.equal(got[step], want.cpu()), f"call {step}"
