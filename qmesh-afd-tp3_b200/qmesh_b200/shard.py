@@ -113,11 +113,12 @@ class P2PExchange:
         self._args.rows_max = rows_max
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._args.status = self.status.data_ptr()
+        self._mode: str | None = None     # "chunk" (combine) or "fused" (slice_combine), fixed by the first call
         dist.barrier(group=group)   # every rank has mapped every buffer before the first step
 
     def _use(self, mode: str) -> None:
         # One buffer serves one protocol: the two keep separate call counters.
-        if getattr(self, "_mode", None) not in (None, mode):
+        if self._mode not in (None, mode):
             raise RuntimeError(f"this exchange already runs the {self._mode} protocol")
         self._mode = mode
 

@@ -1,8 +1,12 @@
-"""The one-shot NVLink combine (qx_combine_p2p) on 2+ GPUs, one process per GPU:
-over several consecutive steps (both receive slots, the acknowledgements) its
-output equals the oracle's rank-ordered FP32 sum with one BF16 rounding, bit for
-bit, for either output rank and with a shared-expert partial. Skipped on a box
-with fewer than two GPUs."""
+"""The NVLink rank combines on 2+ GPUs, one process per GPU. The stand-alone
+kernel (qx_combine_p2p): over several consecutive steps (both receive slots, the
+acknowledgements) its output equals the oracle's rank-ordered FP32 sum with one
+BF16 rounding, bit for bit, for either output rank and with a shared-expert
+partial. The slice with the combine fused in (qx_slice_decode_tc_xchg): its
+output equals the slice partials combined by qx_combine_p2p, bit for bit. Both:
+a rank that skips a step makes the output rank's bounded waits run out and
+report, and the context keeps working. Skipped on a box with fewer than two
+GPUs."""
 
 import os
 
