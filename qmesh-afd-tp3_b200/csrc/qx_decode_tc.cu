@@ -89,7 +89,7 @@ constexpr int NEPI = 2;                        // epilogue warpgroups
 //   accumulator (buffer b, issuer i) at 256 b + 128 i;
 //   in the 32-column gaps: the constant all-1.0 scale atom of every activation
 //   operand at 96 (two atoms: operand rows 0..127, 128..255); the weight scale
-//   atoms of issuer i's 4 K blocks of a stage (4 columns each), in two banks
+//   atoms of issuer i's (at most 4) K blocks of a stage (4 columns each), in two banks
 //   alternating by stage, at 224 + 128 i + 16 bank. A stage's scale copies are
 //   issued before its MMAs into the bank the previous stage's MMAs do not read,
 //   so no MMA waits on the copy just before it. Every scale operand starts on a
@@ -1137,9 +1137,9 @@ __global__ void __launch_bounds__(NTHR, 1) tc_decode_kernel(Params p) {
     S.mma_scratch[0] = 0;
     mbar_wait_bounded(&S.init_bar, 0, &S.mma_scratch[0], 1u, globaltimer_ns() + p.timeout_ns);
   }
-  // The ids, routing weights and x come from work before the prep kernel, so the
-  // routing needs no wait; the prep kernel's results are waited for by the
-  // threads that read them (producer, epilogue).
+  // The ids come from work before the prep kernel (which is launched without
+  // early start), so the routing needs no wait; the prep kernel's results are
+  // waited for by the threads that read them (producer, epilogue).
   if (warp == 0) route_local(p, idr, gs, ps, &S.hdr);
   pdl_launch_dependents();
   __syncwarp();
