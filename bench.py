@@ -142,6 +142,10 @@ def run_ours(args) -> dict | None:
         dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
     rows = args.rows
     a0, a1 = shard_range(rank, world)
+    if args.columns:
+        if world > 1:
+            raise SystemExit("--columns times one rank's shard on one GPU (N = 1)")
+        a0, a1 = (int(v) for v in args.columns.split(":"))
     width = a1 - a0
     layers = args.layers
     n_exp = args.experts
@@ -157,6 +161,8 @@ def run_ours(args) -> dict | None:
         workload = f"config3-spec-decode-rows{rows}" + (f"-zipf{args.zipf}" if args.zipf > 0 else "")
     else:
         workload = "config1-decode" if world == 1 else "config2-column-split"
+        if args.columns:
+            workload = f"config2-shard-columns-{a0}-{a1}-on-one-gpu"
     ws = alloc_workspace(rows, TOPK, a0, a1, dev, args.layout)
     part = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
     gathered = [torch.empty_like(part) for _ in range(world)] if world > 1 and args.xchg == "nccl" else None
@@ -286,7 +292,7 @@ def run_ours(args) -> dict | None:
     k_us = [a.elapsed_time(b) * 1e3 for a, b in evs]
     k_mean = sum(k_us) / len(k_us)
     mean_u = sum(uniq[i % len(uniq)] for i in range(args.steps)) / args.steps
-    alg_bytes = mean_u * EXPERT_BYTES / world + rows * HIDDEN * 1 + rows * HIDDEN * 2
+    alg_bytes = mean_u * EXPERT_BYTES * width / INTER + rows * HIDDEN * 1 + rows * HIDDEN * 2
     gbs = alg_bytes / (k_mean * 1e-6) / 1e9
     peak, peak_kind = peaks()
     res = None
@@ -310,7 +316,8 @@ def run_ours(args) -> dict | None:
                        "topk": TOPK, "columns_per_rank": width, "resident_layers": layers,
                        "routing_draws": args.draws, "mean_unique_experts": round(mean_u, 2),
                        "zipf_s": args.zipf, "seed": args.seed,
-                       "l2": "inputs larger than L2: ~%.0f MB of expert weights per step" % (mean_u * EXPERT_BYTES / 1e6),
+                       "l2": "inputs larger than L2: ~%.0f MB of this rank's expert weights per step, %d resident "
+                             "layers in turn" % (mean_u * EXPERT_BYTES * width / INTER / 1e6, layers),
                        "timed_loop": "per-step CUDA graph replay" if graphs is not None else "eager calls",
                        "parallelism": f"column-split tp{world}",
                        "exchange": None if world == 1 else {
@@ -322,7 +329,7 @@ def run_ours(args) -> dict | None:
             "tokens_per_s": round(rows / (us_layer * 1e-6), 1),
             "weight_gbs": round(gbs, 1),   # per rank: its shard's bytes over its slice kernel time
             # whole step: every rank's weight bytes over the step time (the config-2 aggregate)
-            "aggregate_weight_gbs": round(mean_u * EXPERT_BYTES / (us_layer * 1e-6) / 1e9, 1),
+            "aggregate_weight_gbs": round(mean_u * EXPERT_BYTES * width * world / INTER / (us_layer * 1e-6) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "peak_kind": peak_kind,
                          "traffic": int(mean_u * DRAM_BYTES_PER_UNIQUE * width / INTER),
@@ -567,6 +574,8 @@ def main() -> int:
     ap.add_argument("--draws", type=int, default=16)
     ap.add_argument("--cpu-layers", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--columns", default="",
+                    help="A:B — time the slice of intermediate columns [A, B) on one GPU (one rank's shard)")
     ap.add_argument("--no-graphs", action="store_true",
                     help="time the device loop with eager calls instead of per-step CUDA graph replays")
     ap.add_argument("--xchg", default="fused", choices=["fused", "p2p", "nccl"],
