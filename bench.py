@@ -25,6 +25,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -58,11 +59,12 @@ class Clocks:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+        fd, name = tempfile.mkstemp(prefix=f"qx_clocks_{index}_", suffix=".csv")
+        os.close(fd)
+        self.path = Path(name)
 
     def __enter__(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
             self.f = open(self.path, "w")
             q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -76,6 +78,7 @@ class Clocks:
         return self
 
     def __exit__(self, *a):
+        self.rows = []
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -83,13 +86,15 @@ class Clocks:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
             self.f.close()
+            self.rows = self.path.read_text().splitlines()
+        self.path.unlink(missing_ok=True)
 
     def summary(self) -> dict:
-        if self.proc is None or not self.path.is_file():
+        if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.path.read_text().splitlines():
+        for line in self.rows:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -124,6 +129,153 @@ def make_inputs(n_draws: int, rows: int, seed: int, n_experts: int, zipf: float 
     return draws
 
 
+def workload_config(args, world: int) -> dict:
+    """The workload a line is quoted on (the same keys in both arms)."""
+    rows = args.rows
+    if args.zipf > 0 or rows > 6:
+        workload = f"config3-spec-decode-rows{rows}" + (f"-zipf{args.zipf}" if args.zipf > 0 else "")
+    elif args.columns:
+        workload = "config2-shard-columns-%s-on-one-gpu" % args.columns.replace(":", "-")
+    else:
+        workload = "config1-decode" if world == 1 else "config2-column-split"
+    if args.columns:
+        width = int(args.columns.split(":")[1]) - int(args.columns.split(":")[0])
+    else:
+        width = INTER // world
+    return {"workload": workload, "experts": args.experts, "hidden": HIDDEN, "intermediate": INTER, "rows": rows,
+            "topk": TOPK, "columns_per_rank": width, "routing_draws": args.draws, "zipf_s": args.zipf,
+            "seed": args.seed, "parallelism": f"column-split tp{world}"}
+
+
+L2_BYTES = 126e6
+
+
+def expected_unique(rows: int, n_experts: int) -> float:
+    """Expected distinct experts among rows x top-6 uniform draws."""
+    return n_experts * (1.0 - (1.0 - 1.0 / n_experts) ** (rows * TOPK))
+
+
+def resident_layers(step_bytes: float) -> int:
+    """Resident layers the device loop rotates through: a layer's weights are read
+    again only after at least twice the L2 size of other layers' weights."""
+    return max(2, 1 + math.ceil(2 * L2_BYTES / max(step_bytes, 1.0)))
+
+
+def l2_note(step_bytes: float, layers: int) -> str:
+    between = (layers - 1) * step_bytes
+    return ("inputs larger than L2: %.0f MB of this rank's expert weights per step; a layer recurs every %d steps "
+            "with %.0f MB of other layers' weights read in between (L2 126 MB)"
+            % (step_bytes / 1e6, layers, between / 1e6))
+
+
+def ulp_stats(out: torch.Tensor, ref: torch.Tensor, mag: torch.Tensor | None = None) -> dict:
+    """Relative L2 and BF16 ulp errors of `out` against `ref` (CPU float): the ulp
+    is the BF16 spacing at max(|ref|, 2^-10 rms(row)[, |mag|]) ("max_ulp") and
+    at |ref| alone ("max_ulp_floorless"); counts of elements beyond 2 ulp."""
+    out, ref = out.float().cpu(), ref.float().cpu()
+    err = (out - ref).abs()
+
+    def ulp(a):
+        return torch.pow(2.0, torch.floor(torch.log2(a.clamp_min(2.0 ** -126))) - 7.0)
+    rms = ref.pow(2).mean(dim=-1, keepdim=True).sqrt()
+    m = torch.maximum(ref.abs(), (2.0 ** -10 * rms).expand_as(ref))
+    if mag is not None:
+        m = torch.maximum(m, mag.float().cpu().abs())
+    u = err / ulp(m)
+    u0 = err / ulp(ref.abs())
+    return {"rel_l2": float(err.norm() / ref.norm().clamp_min(1e-30)), "max_ulp": float(u.max()),
+            "max_ulp_floorless": float(u0.max()), "n_over_2ulp_floorless": int((u0 > 2).sum()),
+            "n_over_2ulp": int((u > 2).sum()), "elements": ref.numel()}
+
+
+def check_parity(args, world, rank, dev, dq, views, ws, part, out, a0, a1, last, fused, xchg, exchange,
+                 layers, n_exp) -> dict:
+    """Checks the timed path's results outside the timed region.
+
+    N = 1: the output the timed loop left (step `last`) against an eager call of
+    the same step, bit for bit. N > 1: for the last timed step and two more, the
+    output rank's combined output against the rank-ordered combine
+    (qx_combine_ordered) of every rank's plain slice partial gathered with
+    NCCL, bit for bit; and the last timed step against the full 2304-column
+    slice of the same layer on the output rank's GPU alone, within the
+    north-star tolerance (relative L2 5e-3; 2 BF16 ulp per element, the ulp
+    taken at the largest rank partial). Every rank takes the same collective
+    steps; a mismatch ends the run with an error."""
+    import torch.distributed as dist
+    from qmesh_b200.arena import Arena
+    from qmesh_b200.combine import combine_ordered
+    from qmesh_b200.expert_slice import alloc_workspace, launch
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    rows = args.rows
+
+    def plain(i: int, dst: torch.Tensor) -> None:
+        q, inv, ids, tw = dq[i % len(dq)]
+        launch(views[i % layers], q, ids, tw, dst, a0, a1, ws, x_scale=inv, stream=stream, layout=args.layout)
+
+    res = {"checked": True, "steps": 0, "bit_exact": True}
+    if world == 1:
+        torch.cuda.synchronize()
+        timed = part.clone()
+        again = torch.empty_like(part)
+        plain(last, again)
+        torch.cuda.synchronize()
+        res.update(steps=1, bit_exact=bool(torch.equal(timed, again)),
+                   what="timed-loop output vs an eager call of the same step")
+        if not res["bit_exact"]:
+            raise SystemExit(f"parity: timed output differs from an eager call: {res}")
+        return res
+    gathered = [torch.empty_like(part) for _ in range(world)]
+    mine = torch.empty_like(part)
+    cmb = torch.empty_like(part)
+    first_cmb, first_mag = None, None
+    for k, i in enumerate((last, last + 1, last + 2)):
+        if k > 0:   # a fresh step through the same exchange
+            q, inv, ids, tw = dq[i % len(dq)]
+            if fused:
+                xchg.slice_combine(views[i % layers], q, ids, tw, out, a0, a1, ws, x_scale=inv, stream=stream)
+            else:
+                plain(i, part)
+                exchange(part)
+        torch.cuda.synchronize()
+        timed = out.clone()
+        plain(i, mine)
+        dist.all_gather(gathered, mine)
+        ok = True
+        if rank == 0:
+            combine_ordered(gathered, out=cmb)
+            torch.cuda.synchronize()
+            ok = bool(torch.equal(timed, cmb))
+            if k == 0:
+                first_cmb = cmb.clone()
+                first_mag = torch.stack([g.float().abs() for g in gathered]).amax(dim=0)
+        flag = torch.tensor([1 if ok else 0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        res["steps"] += 1
+        res["bit_exact"] = res["bit_exact"] and bool(flag.item())
+    res["what"] = ("combined output vs qx_combine_ordered of the ranks' plain slice partials (NCCL all-gather), "
+                   "3 steps; the last timed step vs the full-column slice on one GPU")
+    ok = True
+    if rank == 0:
+        li = last % layers
+        full = Arena(dev, li + 1, n_exp, 0, INTER, layout=args.layout)
+        full.fill_synthetic(li, seed=1000 + li)
+        wsf = alloc_workspace(rows, TOPK, 0, INTER, dev, args.layout)
+        one = torch.empty_like(part)
+        q, inv, ids, tw = dq[last % len(dq)]
+        launch(full.view(li), q, ids, tw, one, 0, INTER, wsf, x_scale=inv, stream=stream, layout=args.layout)
+        torch.cuda.synchronize()
+        del full, wsf
+        st = ulp_stats(first_cmb, one, first_mag)
+        ok = st["rel_l2"] <= 5e-3 and st["max_ulp"] <= 2.0
+        res["vs_one_gpu"] = {k: (round(v, 7) if isinstance(v, float) else v) for k, v in st.items()}
+        res["vs_one_gpu"]["within_tolerance"] = ok
+    flag = torch.tensor([1 if (ok and res["bit_exact"]) else 0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    if not flag.item():
+        raise SystemExit(f"parity check failed on rank {rank}: {res}")
+    return res
+
+
 def run_ours(args) -> dict | None:
     import torch.distributed as dist
     from qmesh_b200 import build
@@ -147,8 +299,9 @@ def run_ours(args) -> dict | None:
             raise SystemExit("--columns times one rank's shard on one GPU (N = 1)")
         a0, a1 = (int(v) for v in args.columns.split(":"))
     width = a1 - a0
-    layers = args.layers
     n_exp = args.experts
+    step_bytes = expected_unique(rows, n_exp) * EXPERT_BYTES * width / INTER
+    layers = args.layers if args.layers > 0 else resident_layers(step_bytes)
     ar = Arena(dev, layers, n_exp, a0, a1, layout=args.layout)
     ar.check_memory()
     for li in range(layers):
@@ -157,12 +310,6 @@ def run_ours(args) -> dict | None:
     draws = make_inputs(args.draws, rows, seed=args.seed, n_experts=n_exp, zipf=args.zipf)
     dq = [(q.to(dev), inv.to(dev), ids.to(dev), tw.to(dev)) for q, inv, ids, tw in draws]
     uniq = [len(set(ids.flatten().tolist())) for _, _, ids, _ in draws]
-    if args.zipf > 0 or rows > 6:
-        workload = f"config3-spec-decode-rows{rows}" + (f"-zipf{args.zipf}" if args.zipf > 0 else "")
-    else:
-        workload = "config1-decode" if world == 1 else "config2-column-split"
-        if args.columns:
-            workload = f"config2-shard-columns-{a0}-{a1}-on-one-gpu"
     ws = alloc_workspace(rows, TOPK, a0, a1, dev, args.layout)
     part = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
     gathered = [torch.empty_like(part) for _ in range(world)] if world > 1 and args.xchg == "nccl" else None
@@ -209,6 +356,9 @@ def run_ours(args) -> dict | None:
         dist.barrier()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
+    last = 2 * args.warmup + args.steps - 1       # the step whose output the timed loop leaves behind
+    if graphs is not None:
+        last %= len(graphs)
     with Clocks(local) as clk:
         torch.cuda.synchronize()
         ev0.record(stream)
@@ -226,6 +376,10 @@ def run_ours(args) -> dict | None:
         ms = float(t.item())
         dist.barrier()
     us_layer = ms * 1e3 / args.steps
+
+    # ---- parity of the timed path (outside the timed region) ----
+    par = check_parity(args, world, rank, dev, dq, views, ws, part, out, a0, a1, last, fused, xchg, exchange,
+                       layers, n_exp)
 
     # ---- end to end through the public call with host buffers ----
     from qmesh_b200.expert_slice import expert_slice
@@ -311,21 +465,15 @@ def run_ours(args) -> dict | None:
             "vs_baseline": None,
             "dtype": "nvfp4-w/fp8-x/fp32-acc",
             "data": "synthetic (seeded NVFP4 weights from N(0,0.02); FP8 activations from N(0,1))",
-            "config": {"workload": workload,
-                       "experts": n_exp, "hidden": HIDDEN, "intermediate": INTER, "rows": rows,
-                       "topk": TOPK, "columns_per_rank": width, "resident_layers": layers,
-                       "routing_draws": args.draws, "mean_unique_experts": round(mean_u, 2),
-                       "zipf_s": args.zipf, "seed": args.seed,
-                       "l2": "inputs larger than L2: ~%.0f MB of this rank's expert weights per step, %d resident "
-                             "layers in turn" % (mean_u * EXPERT_BYTES * width / INTER / 1e6, layers),
-                       "timed_loop": "per-step CUDA graph replay" if graphs is not None else "eager calls",
-                       "parallelism": f"column-split tp{world}",
-                       "exchange": None if world == 1 else {
-                           "fused": "in the slice kernel: NVLink stores of each finalize unit + rank-ordered FP32 sum",
-                           "p2p": "one-shot NVLink store + rank-ordered FP32 sum kernel",
-                           "nccl": "NCCL all-gather + rank-ordered FP32 sum kernel"}[args.xchg],
-                       "kernel": "tcgen05 mxf4nvf4 (16-term e2m1 activations)" if args.layout == "tc"
-                       else "register dequant + mma.sync"},
+            "config": dict(workload_config(args, world), l2=l2_note(mean_u * EXPERT_BYTES * width / INTER, layers)),
+            "setup": {"resident_layers": layers, "mean_unique_experts": round(mean_u, 2),
+                      "timed_loop": "per-step CUDA graph replay" if graphs is not None else "eager calls",
+                      "exchange": None if world == 1 else {
+                          "fused": "in the slice kernel: NVLink stores of each finalize unit + rank-ordered FP32 sum",
+                          "p2p": "one-shot NVLink store + rank-ordered FP32 sum kernel",
+                          "nccl": "NCCL all-gather + rank-ordered FP32 sum kernel"}[args.xchg],
+                      "kernel": "tcgen05 mxf4nvf4 (16-term e2m1 activations)" if args.layout == "tc"
+                      else "register dequant + mma.sync"},
             "tokens_per_s": round(rows / (us_layer * 1e-6), 1),
             "weight_gbs": round(gbs, 1),   # per rank: its shard's bytes over its slice kernel time
             # whole step: every rank's weight bytes over the step time (the config-2 aggregate)
@@ -342,9 +490,10 @@ def run_ours(args) -> dict | None:
             "gpu_launches": args.steps * (2 if args.layout == "tc" else 3)
             + (args.steps if world > 1 and not fused else 0),
             "clocks": clocks,
+            "parity": par,
         }
         if world == 1 and not args.no_cpu:
-            res["cpu_baseline"] = cpu_baseline(draws, ar, rows, a0, a1, args.cpu_layers)
+            res["cpu_baseline"] = cpu_baseline(args)
     if world > 1:
         if xchg is not None:
             xchg.close()
@@ -353,60 +502,53 @@ def run_ours(args) -> dict | None:
     return res
 
 
-def cpu_baseline(draws, ar, rows, a0, a1, n_layers: int) -> dict:
-    """The reference torch dequant-and-matmul path restated on the host cores."""
-    from oracle import moe
-    n = moe.cpu_threads()
-    times = []
-    for i in range(n_layers):
-        q, inv, ids, tw = draws[i % len(draws)]
-        experts = sorted(set(ids.flatten().tolist()))
-        pack = ar.expert_pack(i % ar.layers, experts)
-        local = torch.tensor([experts.index(e) for e in ids.flatten().tolist()], dtype=torch.int32).view_as(ids)
-        from oracle import nvfp4 as oq
-        x = oq.fp8_ingest(q, inv)
-        t0 = time.perf_counter()
-        moe.slice_w4a16(x, local, tw, pack, 0, a1 - a0)
-        times.append(time.perf_counter() - t0)
-    us = sum(times) / len(times) * 1e6
-    return {"value": round(us, 1), "unit": "us/layer", "cores": n, "kind": "port",
-            "sample": f"{n_layers} layer calls of the config-1 workload ({rows} rows, full columns)"}
-
-
-def run_reference(args) -> dict | None:
-    """The reference's dequantize-and-matmul path of the slice, restated on the host
-    cores (oracle.moe.slice_w4a16), on the same routing draws as our arm: each step
-    routes one draw over a resident random-code layer and runs the full 2304-column
-    slice (about one second per step on 16 cores)."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return None
+def cpu_sample(args, n_calls: int, warmup: int) -> tuple[float, int, str]:
+    """The reference's dequantize-and-matmul path of the slice, restated on the
+    host cores (oracle.moe.slice_w4a16), all host threads: `n_calls` timed full
+    2304-column layer calls (after `warmup` untimed ones) of the bench's own
+    seeded routing draws over a resident random-code layer. The CPU path's cost
+    depends on the shapes only, so random codes stand in for the quantised
+    weights. Returns (µs per call, threads, sample description)."""
     from oracle import moe, nvfp4 as oq
     n = moe.cpu_threads()
-    gen = torch.Generator().manual_seed(1)
     rows = args.rows
-    draws = make_inputs(max(args.draws, 1), rows, seed=1, n_experts=N_EXPERTS)
-    layer = moe.random_code_layer(rows * TOPK, gen)
+    draws = make_inputs(max(args.draws, 1), rows, seed=args.seed, n_experts=args.experts, zipf=args.zipf)
+    layer = moe.random_code_layer(rows * TOPK, torch.Generator().manual_seed(args.seed))
     times = []
-    for i in range(args.warmup + args.steps):
+    for i in range(warmup + n_calls):
         q, inv, ids, tw = draws[i % len(draws)]
         experts = sorted(set(ids.flatten().tolist()))
         local = torch.tensor([experts.index(e) for e in ids.flatten().tolist()], dtype=torch.int32).view_as(ids)
         x = oq.fp8_ingest(q, inv)
         t0 = time.perf_counter()
         moe.slice_w4a16(x, local, tw, layer, 0, INTER)
-        dt = time.perf_counter() - t0
-        if i >= args.warmup:
-            times.append(dt)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
     us = sum(times) / len(times) * 1e6
-    sample = (f"{args.steps} full layer calls of the config-1 workload ({rows} rows, top-{TOPK}, "
-              f"seeded routing draws, routed experts only)")
+    sample = (f"{n_calls} full-layer calls (all 2304 columns, {rows} rows, top-{TOPK}, routed experts only) of "
+              f"the bench's seeded routing draws after {warmup} untimed, {n} threads")
+    return us, n, sample
+
+
+def cpu_baseline(args) -> dict:
+    us, n, sample = cpu_sample(args, args.cpu_layers, 1)
+    return {"value": round(us, 1), "unit": "us/layer", "cores": n, "kind": "port", "sample": sample}
+
+
+def run_reference(args) -> dict | None:
+    """The reference arm: the same CPU sampler as `cpu_baseline`, on rank 0 only,
+    with the ours-arm config keys (the CPU path computes every column of the
+    layer in one process)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    us, n, sample = cpu_sample(args, args.steps, args.warmup)
     return {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/layer",
-            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(us / 1e3, 3), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp32 (W4A16 dequant)", "data": "synthetic",
-            "config": {"workload": "config1-decode", "experts": N_EXPERTS, "hidden": HIDDEN,
-                       "intermediate": INTER, "rows": rows, "topk": TOPK},
+            "config": workload_config(args, world),
             "cpu_baseline": {"value": round(us, 1), "unit": "us/layer", "cores": n, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(us, 1), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -570,7 +712,9 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--rows", type=int, default=6)
     ap.add_argument("--experts", type=int, default=N_EXPERTS)
-    ap.add_argument("--layers", type=int, default=2)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="resident layers the device loop rotates through (0: enough that a layer's weights are "
+                         "re-read only after twice the L2 size of other weights)")
     ap.add_argument("--draws", type=int, default=16)
     ap.add_argument("--cpu-layers", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")

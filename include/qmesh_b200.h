@@ -51,6 +51,15 @@ enum {
   QX_X_BF16 = 2    /* bf16 [rows, hidden] (the reference body's input) */
 };
 
+/* Arena layouts: which kernel family the tiles were stored for. The two
+ * layouts have the same byte counts, so the tag is the only thing that tells
+ * them apart; every slice entry point refuses an arena whose tag is not its own
+ * with QX_ERR_ARG (an untagged arena, layout 0, included). */
+enum {
+  QX_LAYOUT_TC = 0x54430001,   /* tensor-core tiles: qx_slice_decode_tc(_xchg), qx_slice_prefill_tc */
+  QX_LAYOUT_FRAG = 0x46520002  /* register-fed fragment tiles: qx_slice_decode, qx_slice_decode_static */
+};
+
 /* Geometry of the build's NVFP4 arena (one MoE layer on one GPU).
  *
  * The arena holds intermediate columns [a0, a1) of every expert. Codes and
@@ -63,6 +72,7 @@ typedef struct {
   const float*   g2;       /* [E] w2 weight_scale_2 */
   int32_t        n_experts;
   int32_t        a0, a1;   /* arena column range, multiples of 32 */
+  int32_t        layout;   /* QX_LAYOUT_TC or QX_LAYOUT_FRAG */
 } QxArena;
 
 /* One call of the routed-expert slice over columns [c0, c1). */
@@ -96,10 +106,11 @@ size_t qx_arena_w2_bytes(int32_t n_experts, int32_t width);
 /* Workspace bytes one qx_slice_decode call needs. */
 size_t qx_slice_workspace_bytes(int32_t rows, int32_t topk, int32_t c0, int32_t c1);
 
-/* Routed-expert NVFP4 SwiGLU slice (decode, rows <= QX_MAX_ROWS).
- * Replaces gx/kernels/ext_variant.cu:11-24 run(). Two launches on `stream`
- * (a routing/activation prologue and the persistent weight-streaming kernel);
- * capture-safe. */
+/* Routed-expert NVFP4 SwiGLU slice (decode, rows <= QX_MAX_ROWS) over an
+ * arena in the fragment layout (QX_LAYOUT_FRAG).
+ * Replaces gx/kernels/ext_variant.cu:11-24 run(). Three launches on `stream`
+ * (a routing/activation prologue, the persistent weight-streaming kernel and
+ * the slot-order finalize); capture-safe. */
 int qx_slice_decode(const QxArena* arena, const QxSliceArgs* args, void* stream);
 
 /* Limits of qx_slice_decode_static. */
@@ -120,14 +131,22 @@ int qx_slice_decode(const QxArena* arena, const QxSliceArgs* args, void* stream)
  * QX_STATIC_MAX_ROWS rows, QX_STATIC_MAX_TOPK slots and QX_STATIC_MAX_WIDTH
  * columns; larger calls return QX_ERR_SHAPE. args->workspace and
  * args->workspace_bytes are ignored; inputs and outputs are the caller's, as in
- * qx_slice_decode. It allocates nothing and calls no allocating routine.
+ * qx_slice_decode, and the arena must be in the fragment layout
+ * (QX_LAYOUT_FRAG). It allocates nothing and calls no allocating routine.
  *
  * The first call on a device looks up the array's device address (with that
  * device current); make that first call before any stream capture. Every call
  * on a device shares the one array, and the kernels reinitialise what must
  * start at zero on each call: calls that overlap on the GPU (two streams, or
- * two host threads) race on the array and must be serialised by the caller. */
+ * two host threads) race on the array and must be serialised by the caller.
+ * Device-side conditions of the last call (QX_DEV_BAD_ID, QX_DEV_TIMEOUT, ...)
+ * sit in the array's status word: read them with qx_slice_decode_static_status. */
 int qx_slice_decode_static(const QxArena* arena, const QxSliceArgs* args, void* stream);
+
+/* The QX_DEV_* bits that the last qx_slice_decode_static call on the current
+ * device recorded (a host copy, synchronous on `stream`; queue it after that
+ * call). QX_ERR_DEVICE if no call has run on this device yet. */
+int qx_slice_decode_static_status(uint32_t* status, void* stream);
 
 /* Fixed-order combine: out = bf16(fp32(parts[0]) + ... + fp32(parts[n-1])), in
  * that order, one rounding (out_f32: keep FP32). parts[i] are BF16 [rows, hidden]

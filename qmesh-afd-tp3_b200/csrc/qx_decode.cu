@@ -40,6 +40,8 @@
 // less than 2^18; f16 x f16 products are exact in the FP32 accumulator. The
 // down projection's FP32 activation enters as two f16 terms (hi + lo, 22
 // significant bits) scaled by a power of two chosen from the SwiGLU clamp.
+#include <atomic>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -1010,6 +1012,7 @@ int qx_slice_decode(const QxArena* arena, const QxSliceArgs* a, void* stream) {
   if ((a->x_fmt == QX_X_E4M3 || a->x_fmt == QX_X_E4M3_POST) && !a->x_scale) return QX_ERR_ARG;
   if (a->x_fmt < QX_X_E4M3 || a->x_fmt > QX_X_BF16) return QX_ERR_ARG;
   if (a->rows < 1 || a->rows > QX_MAX_ROWS || a->topk < 1 || a->topk > QX_MAX_TOPK) return QX_ERR_SHAPE;
+  if (arena->layout != QX_LAYOUT_FRAG) return QX_ERR_ARG;
   if (arena->n_experts < 1 || arena->n_experts > MAXE) return QX_ERR_SHAPE;
   if (arena->a0 % TC || arena->a1 % TC || arena->a1 <= arena->a0) return QX_ERR_SHAPE;
   if (a->c0 % TC || a->c1 % TC || a->c0 < arena->a0 || a->c1 > arena->a1 || a->c1 <= a->c0) return QX_ERR_SHAPE;
@@ -1156,24 +1159,47 @@ static __device__ __align__(256) uint8_t g_static_ws[qx::kStaticWsBytes];
 
 // Device address of g_static_ws per device, looked up on the first call made
 // with that device current. In host code the name g_static_ws is only a
-// host-side handle, so it is never passed to a kernel directly.
-static void* g_static_ws_addr[64] = {nullptr};
+// host-side handle, so it is never passed to a kernel directly. Host threads
+// making their first call on a device at the same time may both look it up;
+// they store the same address, and the atomics keep that well defined.
+static std::atomic<void*> g_static_ws_addr[64];
+
+static void* static_ws_of_current(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  *dev_out = dev;
+  void* ptr = g_static_ws_addr[dev].load(std::memory_order_acquire);
+  if (ptr == nullptr) {
+    if (cudaGetSymbolAddress(&ptr, g_static_ws) != cudaSuccess || ptr == nullptr) return nullptr;
+    g_static_ws_addr[dev].store(ptr, std::memory_order_release);
+  }
+  return ptr;
+}
 
 extern "C" int qx_slice_decode_static(const QxArena* arena, const QxSliceArgs* args, void* stream) {
   if (!arena || !args) return QX_ERR_ARG;
+  if (arena->layout != QX_LAYOUT_FRAG) return QX_ERR_ARG;
   if (args->rows < 1 || args->rows > QX_STATIC_MAX_ROWS || args->topk < 1 || args->topk > QX_STATIC_MAX_TOPK ||
       args->c1 - args->c0 > QX_STATIC_MAX_WIDTH || args->c1 <= args->c0 || (args->c1 - args->c0) % qx::TC)
     return QX_ERR_SHAPE;
   if (qx::ws_layout(args->rows, args->topk, args->c1 - args->c0).total > qx::kStaticWsBytes) return QX_ERR_SHAPE;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QX_ERR_DEVICE;
-  if (g_static_ws_addr[dev] == nullptr) {
-    void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_static_ws) != cudaSuccess || ptr == nullptr) return QX_ERR_DEVICE;
-    g_static_ws_addr[dev] = ptr;
-  }
+  void* ws = static_ws_of_current(&dev);
+  if (ws == nullptr) return QX_ERR_DEVICE;
   QxSliceArgs a = *args;
-  a.workspace = g_static_ws_addr[dev];
+  a.workspace = ws;
   a.workspace_bytes = qx::kStaticWsBytes;
   return qx_slice_decode(arena, &a, stream);
+}
+
+// The status word of the static scratch (its control block sits at offset 0,
+// as in every workspace) for the current device; only after a call has looked
+// the array up on this device.
+extern "C" int qx_slice_decode_static_status(uint32_t* status, void* stream) {
+  if (!status) return QX_ERR_ARG;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QX_ERR_DEVICE;
+  void* ws = g_static_ws_addr[dev].load(std::memory_order_acquire);
+  if (ws == nullptr) return QX_ERR_DEVICE;
+  return qx_status_read(ws, status, stream);
 }

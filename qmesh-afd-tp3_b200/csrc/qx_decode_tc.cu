@@ -1255,6 +1255,7 @@ static int tc_launch(const QxArena* arena, const QxSliceArgs* a, const QxXchgArg
   if ((a->x_fmt == QX_X_E4M3 || a->x_fmt == QX_X_E4M3_POST) && !a->x_scale) return QX_ERR_ARG;
   if (a->x_fmt < QX_X_E4M3 || a->x_fmt > QX_X_BF16) return QX_ERR_ARG;
   if (a->rows < 1 || a->rows > QX_MAX_ROWS || a->topk < 1 || a->topk > QX_MAX_TOPK) return QX_ERR_SHAPE;
+  if (arena->layout != QX_LAYOUT_TC) return QX_ERR_ARG;
   if (arena->n_experts < 1 || arena->n_experts > MAXE) return QX_ERR_SHAPE;
   if (a->c1 - a->c0 > 64 * 64) return QX_ERR_SHAPE;   // at most 64 column tiles per slice
   if (arena->a0 % 32 || arena->a1 % 32 || arena->a1 <= arena->a0) return QX_ERR_SHAPE;

@@ -790,6 +790,7 @@ int qx_slice_prefill_tc(const QxArena* arena, const QxSliceArgs* a, const float*
   if ((a->x_fmt == QX_X_E4M3 || a->x_fmt == QX_X_E4M3_POST) && !a->x_scale) return QX_ERR_ARG;
   if (a->x_fmt < QX_X_E4M3 || a->x_fmt > QX_X_BF16) return QX_ERR_ARG;
   if (a->rows < 1 || a->rows > QX_PREFILL_MAX_ROWS || a->topk < 1 || a->topk > QX_MAX_TOPK) return QX_ERR_SHAPE;
+  if (arena->layout != QX_LAYOUT_TC) return QX_ERR_ARG;
   if (arena->n_experts < 1 || arena->n_experts > MAXE) return QX_ERR_SHAPE;
   if (arena->a0 % 32 || arena->a1 % 32 || arena->a1 <= arena->a0) return QX_ERR_SHAPE;
   if ((a->c0 - arena->a0) % 64 || a->c1 % 32 || a->c0 < arena->a0 || a->c1 > arena->a1 || a->c1 <= a->c0)

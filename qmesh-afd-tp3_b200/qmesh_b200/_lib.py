@@ -34,6 +34,9 @@ QX_DEV_BAD_ID = 1
 QX_DEV_TIMEOUT = 2
 QX_DEV_OVERFLOW = 4
 
+QX_LAYOUT_TC = 0x54430001
+QX_LAYOUT_FRAG = 0x46520002
+
 QX_X_E4M3 = 0
 QX_X_E4M3_POST = 1
 QX_X_BF16 = 2
@@ -56,6 +59,7 @@ class QxArena(ctypes.Structure):
         ("n_experts", ctypes.c_int32),
         ("a0", ctypes.c_int32),
         ("a1", ctypes.c_int32),
+        ("layout", ctypes.c_int32),
     ]
 
 
@@ -113,6 +117,7 @@ SIGNATURES = [
      [ctypes.POINTER(QxArena), ctypes.POINTER(QxSliceArgs), ctypes.c_void_p]),
     ("qx_slice_decode_static", ctypes.c_int,
      [ctypes.POINTER(QxArena), ctypes.POINTER(QxSliceArgs), ctypes.c_void_p]),
+    ("qx_slice_decode_static_status", ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_void_p]),
     ("qx_combine_ordered", ctypes.c_int,
      [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p,
       ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]),

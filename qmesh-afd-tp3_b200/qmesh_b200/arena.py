@@ -151,4 +151,4 @@ class Arena:
         return _lib.QxArena(
             ctypes.c_void_p(self.w13[li].data_ptr()), ctypes.c_void_p(self.w2[li].data_ptr()),
             ctypes.c_void_p(self.g13[li].data_ptr()), ctypes.c_void_p(self.g2[li].data_ptr()),
-            self.n_experts, self.a0, self.a1)
+            self.n_experts, self.a0, self.a1, _lib.QX_LAYOUT_TC if self.layout == "tc" else _lib.QX_LAYOUT_FRAG)

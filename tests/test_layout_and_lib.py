@@ -137,7 +137,7 @@ def test_exchange_buffer_layout(lib):
 def test_decode_rejects_bad_arguments_before_touching_the_device(lib):
     from qmesh_b200 import _lib
     ar = _lib.QxArena(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16),
-                      8, 0, 2304)
+                      8, 0, 2304, _lib.QX_LAYOUT_FRAG)
     base = dict(x=16, x_scale=16, x_stride=5120, x_fmt=0, ids=16, ids_int64=0, tw=16, rows=1, topk=6,
                 c0=0, c1=2304, swiglu_limit=10.0, has_limit=1, out=16, out_stride=5120, workspace=256,
                 workspace_bytes=1 << 30)
@@ -159,6 +159,27 @@ def test_decode_rejects_bad_arguments_before_touching_the_device(lib):
     assert call(workspace=128) == _lib.QX_ERR_ALIGN
     assert call(workspace_bytes=1024) == _lib.QX_ERR_WORKSPACE
     assert lib.qx_slice_decode(None, None, None) == _lib.QX_ERR_ARG
+
+
+def test_entry_points_refuse_an_arena_of_the_other_layout(lib):
+    """The tensor-core and fragment layouts have equal byte counts, so the arena's
+    layout tag is what keeps a tc arena out of the fragment kernels (and the
+    reverse): refused with QX_ERR_ARG before any device work."""
+    from qmesh_b200 import _lib
+    base = dict(x=16, x_scale=16, x_stride=5120, x_fmt=0, ids=16, ids_int64=0, tw=16, rows=1, topk=6,
+                c0=0, c1=2304, swiglu_limit=10.0, has_limit=1, out=16, out_stride=5120, workspace=256,
+                workspace_bytes=1 << 30)
+    args = _lib.QxSliceArgs(*[base[f[0]] for f in _lib.QxSliceArgs._fields_])
+    p = [ctypes.c_void_p(16)] * 4
+    for layout, refused_by in ((_lib.QX_LAYOUT_TC, ("qx_slice_decode", "qx_slice_decode_static")),
+                               (_lib.QX_LAYOUT_FRAG, ("qx_slice_decode_tc",)),
+                               (0, ("qx_slice_decode", "qx_slice_decode_tc", "qx_slice_decode_static"))):
+        ar = _lib.QxArena(*p, 8, 0, 2304, layout)
+        for name in refused_by:
+            assert getattr(lib, name)(ctypes.byref(ar), ctypes.byref(args), None) == _lib.QX_ERR_ARG, (name, layout)
+        if layout != _lib.QX_LAYOUT_TC:
+            assert lib.qx_slice_prefill_tc(ctypes.byref(ar), ctypes.byref(args), ctypes.c_void_p(16),
+                                           None) == _lib.QX_ERR_ARG
 
 
 def test_combine_rejects_bad_arguments(lib):
