@@ -144,10 +144,21 @@ def workload_config(args, world: int) -> dict:
         width = INTER // world
     return {"workload": workload, "experts": args.experts, "hidden": HIDDEN, "intermediate": INTER, "rows": rows,
             "topk": TOPK, "columns_per_rank": width, "routing_draws": args.draws, "zipf_s": args.zipf,
-            "seed": args.seed, "parallelism": f"column-split tp{world}"}
+            "seed": args.seed, "parallelism": f"column-split tp{world}",
+            "shared_expert": "dense NVFP4 SwiGLU, intermediate 2304, weight 1, on rank 0" if shared_on(args, world)
+            else None}
 
 
 L2_BYTES = 126e6
+SHARED_SEED = 999
+
+
+def shared_on(args, world: int) -> bool:
+    """Config 2's shared-expert stand-in: on for the column split (N > 1, 6 rows,
+    uniform routing) unless --shared off; --shared on forces it."""
+    if args.shared != "auto":
+        return args.shared == "on"
+    return world > 1 and args.rows == 6 and args.zipf == 0 and not args.columns
 
 
 def expected_unique(rows: int, n_experts: int) -> float:
@@ -188,25 +199,30 @@ def ulp_stats(out: torch.Tensor, ref: torch.Tensor, mag: torch.Tensor | None = N
             "n_over_2ulp": int((u > 2).sum()), "elements": ref.numel()}
 
 
-def check_parity(args, world, rank, dev, dq, views, ws, part, out, a0, a1, last, fused, xchg, exchange,
+def check_parity(args, world, rank, dev, dq, views, ws, part, out, a0, a1, last, slice_step, shv, sh_call,
                  layers, n_exp) -> dict:
     """Checks the timed path's results outside the timed region.
 
-    N = 1: the output the timed loop left (step `last`) against an eager call of
-    the same step, bit for bit. N > 1: for the last timed step and two more, the
+    N = 1: the output the timed loop left (step `last`) against the same step
+    run again, bit for bit. N > 1: for the last timed step and two more, the
     output rank's combined output against the rank-ordered combine
     (qx_combine_ordered) of every rank's plain slice partial gathered with
-    NCCL, bit for bit; and the last timed step against the full 2304-column
-    slice of the same layer on the output rank's GPU alone, within the
-    north-star tolerance (relative L2 5e-3; 2 BF16 ulp per element, the ulp
-    taken at the largest rank partial). Every rank takes the same collective
-    steps; a mismatch ends the run with an error."""
+    NCCL, followed by a separate shared-expert call when config 2's shared
+    expert is on, bit for bit; and the last timed step against the full
+    2304-column slice of the same layer (with the shared expert) on the output
+    rank's GPU alone, within the north-star tolerance (relative L2 5e-3; 2 BF16
+    ulp per element, the ulp taken at the largest partial). Every rank takes
+    the same collective steps; a mismatch ends the run with an error."""
     import torch.distributed as dist
     from qmesh_b200.arena import Arena
     from qmesh_b200.combine import combine_ordered
     from qmesh_b200.expert_slice import alloc_workspace, launch
     stream = torch.cuda.current_stream(dev).cuda_stream
     rows = args.rows
+
+    def run(i: int) -> None:
+        q, inv, ids, tw = dq[i % len(dq)]
+        slice_step(views[i % layers], q, inv, ids, tw, stream)
 
     def plain(i: int, dst: torch.Tensor) -> None:
         q, inv, ids, tw = dq[i % len(dq)]
@@ -216,11 +232,10 @@ def check_parity(args, world, rank, dev, dq, views, ws, part, out, a0, a1, last,
     if world == 1:
         torch.cuda.synchronize()
         timed = part.clone()
-        again = torch.empty_like(part)
-        plain(last, again)
+        run(last)
         torch.cuda.synchronize()
-        res.update(steps=1, bit_exact=bool(torch.equal(timed, again)),
-                   what="timed-loop output vs an eager call of the same step")
+        res.update(steps=1, bit_exact=bool(torch.equal(timed, part)),
+                   what="timed-loop output vs the same step run again")
         if not res["bit_exact"]:
             raise SystemExit(f"parity: timed output differs from an eager call: {res}")
         return res
@@ -230,30 +245,30 @@ def check_parity(args, world, rank, dev, dq, views, ws, part, out, a0, a1, last,
     first_cmb, first_mag = None, None
     for k, i in enumerate((last, last + 1, last + 2)):
         if k > 0:   # a fresh step through the same exchange
-            q, inv, ids, tw = dq[i % len(dq)]
-            if fused:
-                xchg.slice_combine(views[i % layers], q, ids, tw, out, a0, a1, ws, x_scale=inv, stream=stream)
-            else:
-                plain(i, part)
-                exchange(part)
+            run(i)
         torch.cuda.synchronize()
         timed = out.clone()
         plain(i, mine)
         dist.all_gather(gathered, mine)
         ok = True
         if rank == 0:
-            combine_ordered(gathered, out=cmb)
+            parts = list(gathered)
+            if sh_call is not None:
+                q, inv, _, _ = dq[i % len(dq)]
+                parts.append(sh_call(q, inv, stream).clone())
+            combine_ordered(parts, out=cmb)
             torch.cuda.synchronize()
             ok = bool(torch.equal(timed, cmb))
             if k == 0:
                 first_cmb = cmb.clone()
-                first_mag = torch.stack([g.float().abs() for g in gathered]).amax(dim=0)
+                first_mag = torch.stack([g.float().abs() for g in parts]).amax(dim=0)
         flag = torch.tensor([1 if ok else 0], device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         res["steps"] += 1
         res["bit_exact"] = res["bit_exact"] and bool(flag.item())
-    res["what"] = ("combined output vs qx_combine_ordered of the ranks' plain slice partials (NCCL all-gather), "
-                   "3 steps; the last timed step vs the full-column slice on one GPU")
+    res["what"] = ("combined output vs qx_combine_ordered of the ranks' plain slice partials (NCCL all-gather)"
+                   + (" and a separate shared-expert call" if sh_call is not None else "")
+                   + ", 3 steps; the last timed step vs the full-column slice on one GPU")
     ok = True
     if rank == 0:
         li = last % layers
@@ -262,7 +277,8 @@ def check_parity(args, world, rank, dev, dq, views, ws, part, out, a0, a1, last,
         wsf = alloc_workspace(rows, TOPK, 0, INTER, dev, args.layout)
         one = torch.empty_like(part)
         q, inv, ids, tw = dq[last % len(dq)]
-        launch(full.view(li), q, ids, tw, one, 0, INTER, wsf, x_scale=inv, stream=stream, layout=args.layout)
+        launch(full.view(li), q, ids, tw, one, 0, INTER, wsf, x_scale=inv, stream=stream, layout=args.layout,
+               shared=shv)
         torch.cuda.synchronize()
         del full, wsf
         st = ulp_stats(first_cmb, one, first_mag)
@@ -315,24 +331,53 @@ def run_ours(args) -> dict | None:
     gathered = [torch.empty_like(part) for _ in range(world)] if world > 1 and args.xchg == "nccl" else None
     xchg = P2PExchange(rows_max=rows, dst=0, device=dev) if world > 1 and args.xchg in ("p2p", "fused") else None
     fused = world > 1 and args.xchg == "fused"
+    # config 2's shared-expert stand-in: one dense NVFP4 SwiGLU over all 2304
+    # columns, every row with weight 1, on the output rank (rank 0), added after
+    # the ranks' routed partials
+    with_shared = shared_on(args, world)
+    shv, sh_call = None, None
+    if with_shared and rank == 0:
+        if args.layout != "tc":
+            raise SystemExit("the shared expert runs on the tensor-core slice (--layout tc)")
+        sh_arena = Arena(dev, 1, 1, 0, INTER, layout="tc")
+        sh_arena.fill_synthetic(0, seed=SHARED_SEED)
+        shv = sh_arena.view(0)
+        ws_s = alloc_workspace(rows, 1, 0, INTER, dev)
+        sh_ids = torch.zeros(rows, 1, dtype=torch.int32, device=dev)
+        sh_tw = torch.ones(rows, 1, dtype=torch.float32, device=dev)
+        sh_out = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
 
-    def exchange(p: torch.Tensor) -> torch.Tensor | None:
+        def sh_call(q, inv, st) -> torch.Tensor:
+            """The shared expert as a call of its own (ids 0, weight 1)."""
+            launch(shv, q, sh_ids, sh_tw, sh_out, 0, INTER, ws_s, x_scale=inv, stream=st)
+            return sh_out
+
+    def exchange(p: torch.Tensor, shared: torch.Tensor | None = None) -> torch.Tensor | None:
         if xchg is not None:
-            return xchg.combine(p, out=out)
-        return combine_across_ranks(p, dst=0, out=out, combine=combine_ordered, gathered=gathered)
+            return xchg.combine(p, out=out, shared=shared)
+        return combine_across_ranks(p, dst=0, out=out, combine=combine_ordered, gathered=gathered, shared=shared)
     out = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
     views = [ar.view(li) for li in range(layers)]
     stream = torch.cuda.current_stream(dev)
 
+    def slice_step(view, q, inv, ids, tw, st) -> None:
+        """One step through the public calls: N = 1 the slice (with the shared
+        expert in the same kernel when configured); N > 1 the fused slice +
+        combine (the output rank runs the shared expert in its kernel), or the
+        slice, a separate shared-expert call on the output rank and the combine."""
+        if fused:
+            xchg.slice_combine(view, q, ids, tw, out, a0, a1, ws, x_scale=inv, stream=st, shared_expert=shv)
+            return
+        if world == 1:
+            launch(view, q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=st, layout=args.layout, shared=shv)
+            return
+        launch(view, q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=st, layout=args.layout)
+        exchange(part, sh_call(q, inv, st) if sh_call is not None else None)
+
     def step(i: int) -> None:
         q, inv, ids, tw = dq[i % len(dq)]
         st = torch.cuda.current_stream(dev).cuda_stream   # the capture stream while a graph is recorded
-        if fused:   # slice and combine in one kernel per rank
-            xchg.slice_combine(views[i % layers], q, ids, tw, out, a0, a1, ws, x_scale=inv, stream=st)
-            return
-        launch(views[i % layers], q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=st, layout=args.layout)
-        if world > 1:
-            exchange(part)
+        slice_step(views[i % layers], q, inv, ids, tw, st)
 
     for i in range(args.warmup):
         step(i)
@@ -378,7 +423,7 @@ def run_ours(args) -> dict | None:
     us_layer = ms * 1e3 / args.steps
 
     # ---- parity of the timed path (outside the timed region) ----
-    par = check_parity(args, world, rank, dev, dq, views, ws, part, out, a0, a1, last, fused, xchg, exchange,
+    par = check_parity(args, world, rank, dev, dq, views, ws, part, out, a0, a1, last, slice_step, shv, sh_call,
                        layers, n_exp)
 
     # ---- end to end through the public call with host buffers ----
@@ -390,7 +435,7 @@ def run_ours(args) -> dict | None:
     d2h = out_h.numel() * out_h.element_size()
 
     hslice = None
-    if world == 1:
+    if world == 1 and shv is None:
         # the public host-buffer call: one packed host-to-device copy per step
         from qmesh_b200.expert_slice import HostSlice
         hslice = HostSlice(ar, rows, TOPK, a0, a1)
@@ -403,15 +448,9 @@ def run_ours(args) -> dict | None:
             return
         for d, s in zip(dev_in, src):
             d.copy_(s, non_blocking=True)
-        if fused:
-            if xchg.slice_combine(views[i % layers], dev_in[0], dev_in[2], dev_in[3], out, a0, a1, ws,
-                                  x_scale=dev_in[1], stream=stream.cuda_stream) is not None:
-                out_h.copy_(out, non_blocking=True)
-            return
-        launch(views[i % layers], dev_in[0], dev_in[2], dev_in[3], part, a0, a1, ws, x_scale=dev_in[1],
-               stream=stream.cuda_stream, layout=args.layout)
-        if exchange(part) is not None:
-            out_h.copy_(out, non_blocking=True)
+        slice_step(views[i % layers], dev_in[0], dev_in[1], dev_in[2], dev_in[3], stream.cuda_stream)
+        if rank == 0:
+            out_h.copy_(out if world > 1 else part, non_blocking=True)
 
     for i in range(args.warmup):
         e2e_step(i)
@@ -440,13 +479,15 @@ def run_ours(args) -> dict | None:
         q, inv, ids, tw = dq[i % len(dq)]
         a.record(stream)
         launch(views[i % layers], q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=stream.cuda_stream,
-               layout=args.layout)
+               layout=args.layout, shared=shv)
         b.record(stream)
     torch.cuda.synchronize()
     k_us = [a.elapsed_time(b) * 1e3 for a, b in evs]
     k_mean = sum(k_us) / len(k_us)
     mean_u = sum(uniq[i % len(uniq)] for i in range(args.steps)) / args.steps
-    alg_bytes = mean_u * EXPERT_BYTES * width / INTER + rows * HIDDEN * 1 + rows * HIDDEN * 2
+    shared_bytes = EXPERT_BYTES if with_shared else 0     # on the output rank
+    alg_bytes = (mean_u * EXPERT_BYTES * width / INTER + (shared_bytes if rank == 0 else 0)
+                 + rows * HIDDEN * 1 + rows * HIDDEN * 2)
     gbs = alg_bytes / (k_mean * 1e-6) / 1e9
     peak, peak_kind = peaks()
     res = None
@@ -467,6 +508,8 @@ def run_ours(args) -> dict | None:
             "data": "synthetic (seeded NVFP4 weights from N(0,0.02); FP8 activations from N(0,1))",
             "config": dict(workload_config(args, world), l2=l2_note(mean_u * EXPERT_BYTES * width / INTER, layers)),
             "setup": {"resident_layers": layers, "mean_unique_experts": round(mean_u, 2),
+                      "shared_expert": ("in the output rank's slice kernel" if fused or world == 1
+                                        else "a separate call on the output rank") if with_shared else None,
                       "timed_loop": "per-step CUDA graph replay" if graphs is not None else "eager calls",
                       "exchange": None if world == 1 else {
                           "fused": "in the slice kernel: NVLink stores of each finalize unit + rank-ordered FP32 sum",
@@ -477,7 +520,8 @@ def run_ours(args) -> dict | None:
             "tokens_per_s": round(rows / (us_layer * 1e-6), 1),
             "weight_gbs": round(gbs, 1),   # per rank: its shard's bytes over its slice kernel time
             # whole step: every rank's weight bytes over the step time (the config-2 aggregate)
-            "aggregate_weight_gbs": round(mean_u * EXPERT_BYTES * width * world / INTER / (us_layer * 1e-6) / 1e9, 1),
+            "aggregate_weight_gbs": round((mean_u * EXPERT_BYTES * width * world / INTER + shared_bytes)
+                                          / (us_layer * 1e-6) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "peak_kind": peak_kind,
                          "traffic": int(mean_u * DRAM_BYTES_PER_UNIQUE * width / INTER),
@@ -487,8 +531,9 @@ def run_ours(args) -> dict | None:
                     "d2h_bytes_per_step": d2h},
             # prep + decode (tc) or prologue + main + finalize (frag) per step, + a combine kernel for N > 1
             # unless the combine is fused into the decode kernel
-            "gpu_launches": args.steps * (2 if args.layout == "tc" else 3)
-            + (args.steps if world > 1 and not fused else 0),
+            "gpu_launches": args.steps * ((2 if args.layout == "tc" else 3)
+                                          + (1 if world > 1 and not fused else 0)
+                                          + (2 if with_shared and world > 1 and not fused else 0)),
             "clocks": clocks,
             "parity": par,
         }
@@ -502,18 +547,23 @@ def run_ours(args) -> dict | None:
     return res
 
 
-def cpu_sample(args, n_calls: int, warmup: int) -> tuple[float, int, str]:
+def cpu_sample(args, n_calls: int, warmup: int, world: int = 1) -> tuple[float, int, str]:
     """The reference's dequantize-and-matmul path of the slice, restated on the
     host cores (oracle.moe.slice_w4a16), all host threads: `n_calls` timed full
     2304-column layer calls (after `warmup` untimed ones) of the bench's own
-    seeded routing draws over a resident random-code layer. The CPU path's cost
-    depends on the shapes only, so random codes stand in for the quantised
-    weights. Returns (µs per call, threads, sample description)."""
+    seeded routing draws over a resident random-code layer, plus config 2's
+    shared expert (every row, weight 1) and the ordered combine when that is on.
+    The CPU path's cost depends on the shapes only, so random codes stand in for
+    the quantised weights. Returns (µs per call, threads, sample description)."""
     from oracle import moe, nvfp4 as oq
     n = moe.cpu_threads()
     rows = args.rows
     draws = make_inputs(max(args.draws, 1), rows, seed=args.seed, n_experts=args.experts, zipf=args.zipf)
     layer = moe.random_code_layer(rows * TOPK, torch.Generator().manual_seed(args.seed))
+    with_shared = shared_on(args, world)
+    sh_layer = moe.random_code_layer(1, torch.Generator().manual_seed(SHARED_SEED)) if with_shared else None
+    sh_ids = torch.zeros(rows, 1, dtype=torch.int32)
+    sh_tw = torch.ones(rows, 1)
     times = []
     for i in range(warmup + n_calls):
         q, inv, ids, tw = draws[i % len(draws)]
@@ -521,11 +571,14 @@ def cpu_sample(args, n_calls: int, warmup: int) -> tuple[float, int, str]:
         local = torch.tensor([experts.index(e) for e in ids.flatten().tolist()], dtype=torch.int32).view_as(ids)
         x = oq.fp8_ingest(q, inv)
         t0 = time.perf_counter()
-        moe.slice_w4a16(x, local, tw, layer, 0, INTER)
+        routed = moe.slice_w4a16(x, local, tw, layer, 0, INTER)
+        if sh_layer is not None:
+            moe.combine_ordered([routed], shared=moe.slice_w4a16(x, sh_ids, sh_tw, sh_layer, 0, INTER))
         if i >= warmup:
             times.append(time.perf_counter() - t0)
     us = sum(times) / len(times) * 1e6
-    sample = (f"{n_calls} full-layer calls (all 2304 columns, {rows} rows, top-{TOPK}, routed experts only) of "
+    what = "routed experts and the shared expert" if with_shared else "routed experts only"
+    sample = (f"{n_calls} full-layer calls (all 2304 columns, {rows} rows, top-{TOPK}, {what}) of "
               f"the bench's seeded routing draws after {warmup} untimed, {n} threads")
     return us, n, sample
 
@@ -543,7 +596,7 @@ def run_reference(args) -> dict | None:
     if rank != 0:
         return None
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    us, n, sample = cpu_sample(args, args.steps, args.warmup)
+    us, n, sample = cpu_sample(args, args.steps, args.warmup, world)
     return {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/layer",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(us / 1e3, 3), "higher_is_better": False, "scaling": "strong",
@@ -720,6 +773,8 @@ def main() -> int:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--columns", default="",
                     help="A:B — time the slice of intermediate columns [A, B) on one GPU (one rank's shard)")
+    ap.add_argument("--shared", default="auto", choices=["auto", "on", "off"],
+                    help="config 2's shared expert on rank 0 (auto: on for N > 1 at 6 rows, uniform routing)")
     ap.add_argument("--no-graphs", action="store_true",
                     help="time the device loop with eager calls instead of per-step CUDA graph replays")
     ap.add_argument("--xchg", default="fused", choices=["fused", "p2p", "nccl"],

@@ -264,6 +264,23 @@ int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* args, void* stre
  * native/qmesh_afd_seam.cu:309-361). */
 int qx_slice_decode_tc_xchg(const QxArena* arena, const QxSliceArgs* args, const QxXchgArgs* x, void* stream);
 
+/* The tensor-core slice plus a shared expert: the dense NVFP4 SwiGLU that the
+ * reference runs beside the routed experts on the node that writes the layer
+ * output, added after the routed partials in the reference's fixed order
+ * (README.md:88-90: NODE-A, NODE-B, NODE-C, shared; native/qmesh_afd_seam.cu:309-361).
+ * `shared` is a one-expert arena in the tensor-core layout over its whole
+ * intermediate range [a0, a1) (at most 4096 columns); every row of the call
+ * goes through it with weight 1, as extra work items of the same kernel. The
+ * output is bf16(fp32(routed partial) + fp32(shared)) for x == NULL, and
+ * bf16(p_0 + ... + p_{N-1} + shared) on the output rank of a fused rank combine
+ * (x as for qx_slice_decode_tc_xchg; only the output rank passes `shared`, and
+ * x->shared must be NULL). The shared expert's BF16 output and the routed
+ * partial are each bit-identical to separate qx_slice_decode_tc calls (the
+ * shared one with ids 0, weights 1, topk 1). Same workspace as
+ * qx_slice_decode_tc (qx_slice_workspace_tc_bytes has room for it). */
+int qx_slice_decode_tc_shared(const QxArena* arena, const QxSliceArgs* args, const QxArena* shared,
+                              const QxXchgArgs* x, void* stream);
+
 /* Self-check of the block-scaled NVFP4 tensor-core path (no counterpart in the
  * reference): d[128][n] (FP32, row-major) = sum over nkb 64-wide K blocks of
  * (A * SFA) x (B * SFB)^T, computed by tcgen05.mma.kind::mxf4nvf4 with the

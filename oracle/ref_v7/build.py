@@ -1,12 +1,12 @@
 """Build oracle/_ref/libref_v7.so from the reference's own v7 kernel source.
 
-    python oracle/ref_v7/build.py [/path/to/QMesh-AFD-TP3]
+    python oracle/ref_v7/build.py [REFERENCE_ROOT]     # or QX_REFERENCE_ROOT=...
 
 Test infrastructure only: the library is the reference's decode kernel, compiled
 unmodified for sm_100a (its converts cvt.rn.f16x2.e2m1x2 / .e4m3x2 exist there),
 used by tests/test_gpu_ref_v7.py to pin the CPU oracle to the reference's actual
-arithmetic. Nothing under the product loads it. Skips quietly when the reference
-tree is absent (the prebuilt file travels with the repository snapshot).
+arithmetic. Nothing under the product loads it. Without a reference tree the
+prebuilt file (which travels with the repository snapshot) is used as it is.
 """
 
 from __future__ import annotations
@@ -21,9 +21,10 @@ OUT = HERE.parent / "_ref" / "libref_v7.so"
 KERNEL = "gx/kernels/fp4_decode_moe_swz.cu"
 
 
-def build(ref: str = "/root/reference") -> Path | None:
-    src = Path(ref) / KERNEL
-    if not src.is_file():
+def build(ref: str | None = None) -> Path | None:
+    ref = ref or os.environ.get("QX_REFERENCE_ROOT")
+    src = Path(ref) / KERNEL if ref else None
+    if src is None or not src.is_file():
         return OUT if OUT.is_file() else None
     shim = HERE / "ref_v7_shim.cu"
     if OUT.is_file() and OUT.stat().st_mtime >= max(shim.stat().st_mtime, src.stat().st_mtime):
@@ -37,4 +38,4 @@ def build(ref: str = "/root/reference") -> Path | None:
 
 
 if __name__ == "__main__":
-    print(build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None))

@@ -99,6 +99,16 @@ constexpr int NISS = 2, KB_PER_ISS = SK / NISS;
 static_assert(KB_PER_ISS * 4 <= (int)TM_BANK, "a stage's scale atoms fit one bank");
 static_assert(GMAX * XTERMS <= 96, "an accumulator fits its slot");
 constexpr int XE_LO = -90, XE_HI = 100;      // x exponents
+// K-split of gate/up items: when a call has fewer (group, tile) items than
+// SPLIT_PER_CTA x the grid (narrow column shards), each item's 10 stages are
+// split into ks pieces (ks in {1, 2, 5, 10}, the smallest that reaches the
+// target); a piece stores its FP32 sums and the last piece of an item adds the
+// pieces in piece order. At most MAXSPLIT pieces per call.
+constexpr int SPLIT_PER_CTA = 4;
+constexpr int MAXSPLIT = 1536;     // routed pieces
+constexpr int MAXSPLIT_S = 512;    // shared-expert pieces (their own split, after the routed ones)
+constexpr int MAX_STILES = 64;     // shared-expert column tiles at most (4096 columns)
+constexpr int MAXSG = (QX_MAX_ROWS + 5) / 6;   // shared-expert groups at most
 constexpr int AE_LO = -90, AE_HI = 100;      // SwiGLU-output exponents (even)
 
 struct Ctl {
@@ -111,14 +121,19 @@ struct GroupS {     // one group (<= GMAX routed pairs of one expert), kept in s
   int32_t expert, gsz, pair_off;
   int32_t n, sbs;         // activation operand of either item kind: 16 x gsz rows, bytes per stage
   int32_t ab_off;         // offset of the group's down operand in the activation-term buffer
-  int32_t pad[2];
+  int32_t shared;         // 1: rows of the shared expert (its own arena, weight 1)
+  int32_t pad;
 };
 static_assert(sizeof(GroupS) == 32, "shared group record is 32 bytes");
 
 struct RouteHdr {   // call-wide results of the routing, in shared memory
-  int32_t n_groups, n1, n2, b_max;   // groups, gate/up items, down items, widest activation stage
+  int32_t n_groups, n1, n2, b_max;   // routed groups, gate/up items (pieces), down items, widest activation stage
   int32_t n_pairs;                   // routed pairs with a valid expert
-  int32_t pad[3];
+  int32_t ks, kss;                   // pieces per gate/up (group, tile) item: routed, shared expert
+  int32_t n_sgroups;                 // shared-expert groups (gs[n_groups ...])
+  int32_t n1s, n2s;                  // the first n1s gate/up and n2s down items are the shared expert's
+  int32_t n_fin;                     // pairs whose y every output tile waits for (routed + shared rows)
+  int32_t pad[5];
 };
 
 struct PairS {      // per group position: pair index (row * topk + slot)
@@ -146,15 +161,17 @@ struct Params {
   __nv_bfloat16* out;
   int64_t out_stride;
   Ctl* ctl;
-  uint32_t* cnt1;     // [P] gate/up tiles finished per group
-  uint32_t* ready;    // [P] group activation terms complete
+  uint32_t* cnt1;     // [P + rows] gate/up tiles finished per group
+  uint32_t* ready;    // [P + rows] group activation terms complete
   uint32_t* fcnt;     // [HT] routed pairs whose y is written, per 128-row output tile
-  int32_t* emax;      // [P] per group position: common activation exponent
-  int32_t* eloc;      // [P][NT] per group position and tile: tile exponent
+  uint32_t* pcnt;     // [MAXSPLIT + MAXSG * MAX_STILES] pieces finished per gate/up (group, tile) item
+  float* gpart;       // [MAXSPLIT + MAXSPLIT_S][GMAX][128] FP32 sums of each gate/up piece
+  int32_t* emax;      // [P + rows] per group position: common activation exponent
+  int32_t* eloc;      // [P + rows][MAX_STILES] per group position and tile: tile exponent
   int32_t* xexp;      // [rows]
   uint8_t* xt;        // [rows][10 stages][4096 bytes]: x terms, row-major
-  uint8_t* ab;        // per group: ceil(NT/4) stages of sbs bytes (SwiGLU-output terms)
-  float* y;           // [P][HID]
+  uint8_t* ab;        // per group: ceil(NT / SK) stages of sbs bytes (SwiGLU-output terms)
+  float* y;           // [P + rows][HID]: routed pairs, then the shared expert's rows
   int x_off;          // shared-memory offset of the SwiGLU exchanges (per epilogue group 2 x gmax x 64 floats)
   int tab_off;        // shared-memory offset of the group and pair tables
   int ring_off, ring_bytes;  // shared-memory span of the stage rings
@@ -163,6 +180,16 @@ struct Params {
                       // bytes per slot, offset of the activation ring
   uint64_t timeout_ns;
   uint32_t dep_extra; // test hook: extra arrivals a down item waits for (0 in service)
+  int ae_fixed;       // 1: every SwiGLU-output tile uses exponent ae_val (a clamped SwiGLU's
+  int ae_val;         //    bound); 0: per-tile exponents, fixed up by the group's last tile
+  // shared expert (the output rank's dense SwiGLU of config 2): a one-expert
+  // arena over its intermediate columns [0, sW); every row is routed to it with
+  // weight 1 and its BF16 output is added after the routed partials
+  const uint8_t* sw13;
+  const uint8_t* sw2;
+  const float* sg13;
+  const float* sg2;
+  int sW, sNT;        // sNT == 0: no shared expert
   // fused rank combine (qx_slice_decode_tc_xchg; xworld == 0 otherwise): every
   // rank's exchange buffer, the optional shared-expert partial of the output rank
   uint8_t* xbuf[QX_XCHG_MAX_RANKS];
@@ -174,7 +201,8 @@ struct Params {
 struct ItemMeta {
   int32_t kind;       // 1 gate/up, 2 down, 0 end
   int32_t group, tile, nst, nkb_last;
-  int32_t pad[3];
+  int32_t piece;      // gate/up: the item's K piece (stages piece * nst ...)
+  int32_t pad[2];
 };
 
 __host__ __device__ inline size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -192,25 +220,56 @@ constexpr uint32_t XT_SBO = SK * 256;          // row group to row group
 constexpr uint32_t XT_KB = 256;                // K block to K block
 
 struct WsLayout {
-  size_t ctl, cnt1, ready, fcnt, emax, eloc, xexp, xt, ab, y, total;
+  size_t ctl, cnt1, ready, fcnt, pcnt, emax, eloc, xexp, xt, ab, y, gpart, total;
 };
 
+// The workspace always has room for a shared expert of up to MAX_STILES tiles
+// over the call's rows (about 52 KB per row).
 __host__ inline WsLayout ws_layout(int rows, int topk, int W) {
   WsLayout L;
-  const int P = rows * topk, NT = (W + 63) / 64;
+  const int P = rows * topk, NT = (W + 63) / 64, PS = P + rows;
   size_t o = 0;
   L.ctl = o;      o = al256(o + sizeof(Ctl));
-  L.cnt1 = o;     o = al256(o + (size_t)P * 4);
-  L.ready = o;    o = al256(o + (size_t)P * 4);
+  L.cnt1 = o;     o = al256(o + (size_t)PS * 4);
+  L.ready = o;    o = al256(o + (size_t)PS * 4);
   L.fcnt = o;     o = al256(o + (size_t)HT * 4);
-  L.emax = o;     o = al256(o + (size_t)P * 4);
-  L.eloc = o;     o = al256(o + (size_t)P * NT * 4);
+  L.pcnt = o;     o = al256(o + (size_t)(MAXSPLIT + MAXSG * MAX_STILES) * 4);
+  L.emax = o;     o = al256(o + (size_t)PS * 4);
+  L.eloc = o;     o = al256(o + (size_t)PS * MAX_STILES * 4);
   L.xexp = o;     o = al256(o + (size_t)rows * 4);
   L.xt = o;       o = al256(o + (size_t)rows * (KB1 / SK) * XT_STAGE);
-  L.ab = o;       o = al256(o + (size_t)P * ((NT + SK - 1) / SK) * XT_STAGE);
-  L.y = o;        o = al256(o + (size_t)P * HID * 4);
+  L.ab = o;       o = al256(o + ((size_t)P * ((NT + SK - 1) / SK) + (size_t)rows * (MAX_STILES / SK)) * XT_STAGE);
+  L.y = o;        o = al256(o + (size_t)PS * HID * 4);
+  L.gpart = o;    o = al256(o + (size_t)(MAXSPLIT + MAXSPLIT_S) * GMAX * 128 * 4);
   L.total = o;
   return L;
+}
+
+// Weights and geometry of a group's expert: the call's arena and column range,
+// or the shared expert's one-expert arena over all its columns.
+struct Geo {
+  const uint8_t* w13;
+  const uint8_t* w2;
+  int NT, NTA, tile0, W;
+};
+__device__ __forceinline__ Geo geo_of(const Params& p, const GroupS& g) {
+  Geo r;
+  if (g.shared) {
+    r.w13 = p.sw13; r.w2 = p.sw2; r.NT = p.sNT; r.NTA = p.sNT; r.tile0 = 0; r.W = p.sW;
+  } else {
+    r.w13 = p.w13; r.w2 = p.w2; r.NT = p.NT; r.NTA = p.NTA; r.tile0 = p.tile0; r.W = p.W;
+  }
+  return r;
+}
+
+// Row of a group position's pair code: routed pairs are row * topk + slot,
+// the shared expert's are P + row.
+__device__ __forceinline__ int row_of(const Params& p, int pq) { return pq < p.P ? pq / p.topk : pq - p.P; }
+
+// Index of a gate/up (group, tile) item among the piece counters: routed items
+// first, the shared expert's after MAXSPLIT (only items of a split kind count).
+__device__ __forceinline__ size_t gu_index(const Params& p, const RouteHdr& h, int group, int tile, bool shared) {
+  return shared ? (size_t)MAXSPLIT + (size_t)(group - h.n_groups) * p.sNT + tile : (size_t)group * p.NT + tile;
 }
 
 // ------------------------------------------------------------------ prologue
@@ -460,7 +519,8 @@ __device__ void route_sort(const Params& p, const int (&idr)[IDR], GroupS* gs, P
       d.n = XTERMS * gsz;
       d.sbs = gsz * XT_STAGE;
       d.ab_off = i * abs;
-      d.pad[0] = d.pad[1] = 0;
+      d.shared = 0;
+      d.pad = 0;
       gs[base + st[j] - ng[j] + gk[j]] = d;
       bmx = max(bmx, d.sbs);
     }
@@ -469,10 +529,70 @@ __device__ void route_sort(const Params& p, const int (&idr)[IDR], GroupS* gs, P
   for (int o = 16; o > 0; o >>= 1) bmx = max(bmx, __shfl_xor_sync(FULL, bmx, o));
   if (lane == 0) {
     hdr->n_groups = G;
-    hdr->n1 = G * p.NT;
-    hdr->n2 = G * HT;
     hdr->b_max = bmx;
     hdr->n_pairs = Pv;
+  }
+  __syncwarp();
+}
+
+// Pieces per gate/up item: the smallest of 1, 2, 5, 10 that gives every CTA
+// SPLIT_PER_CTA items, within `cap` pieces. Depends only on the item count, so
+// a call's routed items split the same with or without a shared expert, and a
+// shared expert the same as the equal call of its arena alone.
+__device__ __forceinline__ int split_of(int items, int cap) {
+  const int target = SPLIT_PER_CTA * (int)gridDim.x;
+  int ks = 1;
+  if (items < target) {
+    const int opt[3] = {2, 5, 10};
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      if (items * opt[i] > cap) break;
+      ks = opt[i];
+      if (items * opt[i] >= target) break;
+    }
+  }
+  return ks;
+}
+
+// After the routed tables: the shared expert's groups (every row, in row order,
+// split evenly into groups of at most gmax, as the routing splits one expert's
+// pairs) at gs[G ...], their pairs at ps[Pv ...] (code P + row), and the item
+// counts of the call. One warp.
+__device__ void route_finish(const Params& p, GroupS* gs, PairS* ps, RouteHdr* hdr) {
+  const int lane = threadIdx.x & 31;
+  const int G = hdr->n_groups, Pv = hdr->n_pairs;
+  const int gmax = min(GMAX, p.rows);
+  int Gs = 0;
+  if (p.sNT > 0) {
+    Gs = (p.rows + gmax - 1) / gmax;
+    for (int r = lane; r < p.rows; r += 32) ps[Pv + r].pq = p.P + r;
+    const int abs_r = ((p.NT + SK - 1) / SK) * XT_STAGE, abs_s = ((p.sNT + SK - 1) / SK) * XT_STAGE;
+    if (lane < Gs) {
+      const int lo = div_small(lane * p.rows, Gs), hi = div_small((lane + 1) * p.rows, Gs);
+      GroupS d;
+      d.expert = 0;
+      d.gsz = hi - lo;
+      d.pair_off = Pv + lo;
+      d.n = XTERMS * d.gsz;
+      d.sbs = d.gsz * XT_STAGE;
+      d.ab_off = p.P * abs_r + lo * abs_s;
+      d.shared = 1;
+      d.pad = 0;
+      gs[G + lane] = d;
+    }
+  }
+  __syncwarp();
+  if (lane == 0) {
+    const int ks = split_of(G * p.NT, MAXSPLIT), kss = Gs ? split_of(Gs * p.sNT, MAXSPLIT_S) : 1;
+    hdr->ks = ks;
+    hdr->kss = kss;
+    hdr->n_sgroups = Gs;
+    hdr->n1s = Gs * p.sNT * kss;
+    hdr->n1 = hdr->n1s + G * p.NT * ks;
+    hdr->n2s = Gs * HT;
+    hdr->n2 = (G + Gs) * HT;
+    hdr->n_fin = Pv + (Gs ? p.rows : 0);
+    if (Gs) hdr->b_max = max(hdr->b_max, gmax * XT_STAGE);
   }
   __syncwarp();
 }
@@ -482,6 +602,7 @@ __device__ void route_local(const Params& p, const int (&idr)[IDR], GroupS* gs, 
   else if (p.P <= 128) route_sort<4>(p, idr, gs, ps, hdr);
   else if (p.P <= 256) route_sort<8>(p, idr, gs, ps, hdr);
   else route_sort<16>(p, idr, gs, ps, hdr);
+  route_finish(p, gs, ps, hdr);
 }
 
 // One CTA per unit (row r, 512-element chunk c = stage c of the gate/up
@@ -495,10 +616,12 @@ __global__ void __launch_bounds__(PREP_THR) tc_prep_kernel(Params p) {
   const int tid = threadIdx.x, lane = tid & 31;
   if (blockIdx.x == 0) {
     bool bad = false;
-    for (int q = tid; q < p.P; q += PREP_THR) {
-      const long long id = p.ids64 ? reinterpret_cast<const long long*>(p.ids)[q]
-                                   : (long long)reinterpret_cast<const int*>(p.ids)[q];
-      bad |= !(id == -1 || (id >= 0 && id < p.E));
+    for (int q = tid; q < p.P + p.rows; q += PREP_THR) {
+      if (q < p.P) {
+        const long long id = p.ids64 ? reinterpret_cast<const long long*>(p.ids)[q]
+                                     : (long long)reinterpret_cast<const int*>(p.ids)[q];
+        bad |= !(id == -1 || (id >= 0 && id < p.E));
+      }
       p.cnt1[q] = 0;
       p.ready[q] = 0;
       p.emax[q] = INT_MIN;
@@ -510,6 +633,8 @@ __global__ void __launch_bounds__(PREP_THR) tc_prep_kernel(Params p) {
     __syncthreads();
     if (tid == 0 && bad) p.ctl->status = (uint32_t)QX_DEV_BAD_ID;
   }
+  for (int i = blockIdx.x * PREP_THR + tid; i < MAXSPLIT + MAXSG * MAX_STILES; i += gridDim.x * PREP_THR)
+    p.pcnt[i] = 0;
   const int r = blockIdx.x / NXCH, c = blockIdx.x - r * NXCH;
   float inv = 1.f;
   if (p.x_fmt == QX_X_E4M3) inv = p.x_scale[r];
@@ -591,14 +716,16 @@ __device__ void drain_copies(const Params& p, Smem& S, uint32_t sc) {
 
 __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* gs, const PairS* ps,
                          const RouteHdr& hdr, volatile uint32_t* status, uint64_t deadline) {
-  const uint32_t n1 = (uint32_t)hdr.n1, n2 = (uint32_t)hdr.n2;
+  const uint32_t n1 = (uint32_t)hdr.n1, n2 = (uint32_t)hdr.n2, n1s = (uint32_t)hdr.n1s, n2s = (uint32_t)hdr.n2s;
+  const int G = hdr.n_groups;
   uint32_t sc = 0, mc = 0;
   int seen_a = -1;                    // last group whose activation flag was seen set
   bool ok = true, prep_seen = false;  // prep_seen: the prep kernel's results are visible
   uint32_t item = blockIdx.x;         // the first item is static, the rest come from the queue
   uint32_t cl_next = 0, cl_end = 0;   // items claimed and not yet started: [cl_next, cl_end)
-  // Down items of one or two stages are claimed in batches (of 4 or 2), so the
-  // queue's round trip is paid once per batch; longer items one at a time.
+  // Routed down items of one or two stages are claimed in batches (of 4 or 2),
+  // so the queue's round trip is paid once per batch; longer items (and the
+  // shared expert's, which come first) one at a time.
   const int nst2 = (p.NT + SK - 1) / SK;
   const uint32_t dclaim = nst2 == 1 ? 4u : nst2 == 2 ? 2u : 1u;
   for (;;) {
@@ -606,17 +733,27 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
     if (!ok || item >= n1 + n2) {
       m.kind = 0;
     } else if (item < n1) {
+      // Gate/up pieces: the shared expert's first, then the routed groups'.
+      // Pieces of one (group, tile) are consecutive items, so they run side by side.
+      const bool sh = item < n1s;
+      const uint32_t ks = (uint32_t)(sh ? hdr.kss : hdr.ks), nt = (uint32_t)(sh ? p.sNT : p.NT);
+      const uint32_t loc = sh ? item : item - n1s, it = loc / ks;
       m.kind = 1;
-      m.group = (int)(item / (uint32_t)p.NT);
-      m.tile = (int)(item % (uint32_t)p.NT);
-      m.nst = KB1 / SK;
+      m.group = (int)(it / nt) + (sh ? G : 0);
+      m.tile = (int)(it % nt);
+      m.piece = (int)(loc - it * ks);
+      m.nst = (KB1 / SK) / (int)ks;
       m.nkb_last = SK;
     } else {
+      // Down items: the shared expert's groups first, then the routed groups.
+      const bool sh = item - n1 < n2s;
+      const uint32_t loc = sh ? item - n1 : item - n1 - n2s;
+      const int nt = sh ? p.sNT : p.NT;
       m.kind = 2;
-      m.group = (int)((item - n1) / HT);
-      m.tile = (int)((item - n1) % HT);
-      m.nst = (p.NT + SK - 1) / SK;
-      m.nkb_last = p.NT - (m.nst - 1) * SK;
+      m.group = (int)(loc / HT) + (sh ? G : 0);
+      m.tile = (int)(loc % HT);
+      m.nst = (nt + SK - 1) / SK;
+      m.nkb_last = nt - (m.nst - 1) * SK;
     }
     const int mi = (int)(mc % NI);
     if (mc >= (uint32_t)NI &&
@@ -640,10 +777,12 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
       return;
     }
     const GroupS& gr = gs[m.group];
+    const Geo geo = geo_of(p, gr);
     const int sbs = gr.sbs;
     const uint8_t* a_src = m.kind == 1
-                               ? p.w13 + ((size_t)gr.expert * p.NTA + p.tile0 + m.tile) * (size_t)KB1 * A_KB
-                               : p.w2 + (((size_t)gr.expert * HT + m.tile) * p.NTA + p.tile0) * (size_t)A_KB;
+                               ? geo.w13 + ((size_t)gr.expert * geo.NTA + geo.tile0 + m.tile) * (size_t)KB1 * A_KB +
+                                     (size_t)m.piece * m.nst * SK * A_KB
+                               : geo.w2 + (((size_t)gr.expert * HT + m.tile) * geo.NTA + geo.tile0) * (size_t)A_KB;
     // Weights of the CTA's first stages go out before the prep kernel is waited
     // for: they depend on the routing only (the ring is empty, so every slot is free).
     const int pre = prep_seen ? 0 : min(m.nst, p.ns);
@@ -661,7 +800,7 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
     if (cl_next < cl_end) {
       next = cl_next++;
     } else {
-      const uint32_t k = item >= n1 ? dclaim : 1u;
+      const uint32_t k = item >= n1 + n2s ? dclaim : 1u;
       next = gridDim.x + atomicAdd(&p.ctl->work, k);
       cl_next = next + 1;
       cl_end = next + k;
@@ -685,9 +824,9 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
       if (m.kind == 1) {
         // gate/up: each pair's row-major x-term block of this stage
         for (int q = 0; q < gr.gsz; ++q) {
-          const int row = ps[gr.pair_off + q].pq / p.topk;
-          bulk_g2s(bdst + q * XT_STAGE, p.xt + ((size_t)row * NXCH + s) * XT_STAGE, (uint32_t)XT_STAGE,
-                   &S.full[slot]);
+          const int row = row_of(p, ps[gr.pair_off + q].pq);
+          bulk_g2s(bdst + q * XT_STAGE, p.xt + ((size_t)row * NXCH + m.piece * m.nst + s) * XT_STAGE,
+                   (uint32_t)XT_STAGE, &S.full[slot]);
         }
         continue;
       }
@@ -824,6 +963,19 @@ __device__ __forceinline__ void add4(float (&s)[4], uint2 v) {
   s[3] += __uint_as_float(v.y & 0xffff0000u);
 }
 
+__device__ __forceinline__ uint2 pack_bf16x4(const float (&s)[4]) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(s[0], s[1]), hi = __floats2bfloat162_rn(s[2], s[3]);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
+// The shared expert's BF16 output at (row, k..k+3): its one slot, weight 1,
+// rounded once, as a call of its arena alone would write it.
+__device__ __forceinline__ uint2 shared_partial(const Params& p, int row, int k) {
+  const float4 v = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)(p.P + row) * HID + k));
+  const float s[4] = {v.x, v.y, v.z, v.w};
+  return pack_bf16x4(s);
+}
+
 // Finalize unit u (tile, rb). Alone, it writes the output. In the fused rank
 // combine a sender, once the output rank has acknowledged its use of the same
 // receive words two calls ago, stores each thread's 8 BF16 bytes as two 64-bit
@@ -840,7 +992,16 @@ __device__ bool finalize_unit(const Params& p, Smem& S, int u, int tile, int rb,
   const uint2 mine = unit_partial(p, tile, rb, et, row, k);
   const bool has = row < p.rows;
   if (p.xworld == 0) {
-    if (has) *reinterpret_cast<uint2*>(p.out + (size_t)row * p.out_stride + k) = mine;
+    if (has) {
+      uint2 o = mine;
+      if (p.sNT > 0) {   // bf16(routed + shared) in FP32, the combine's order
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+        add4(s, mine);
+        add4(s, shared_partial(p, row, k));
+        o = pack_bf16x4(s);
+      }
+      *reinterpret_cast<uint2*>(p.out + (size_t)row * p.out_stride + k) = o;
+    }
     return true;
   }
   Hdr* me = reinterpret_cast<Hdr*>(xbuf_at(p, p.xrank));
@@ -872,6 +1033,7 @@ __device__ bool finalize_unit(const Params& p, Smem& S, int u, int tile, int rb,
       add4(s, v);
     }
     if (p.xshared) add4(s, *reinterpret_cast<const uint2*>(p.xshared + (size_t)row * p.xshared_stride + k));
+    else if (p.sNT > 0) add4(s, shared_partial(p, row, k));
     const __nv_bfloat162 lo = __floats2bfloat162_rn(s[0], s[1]), hi = __floats2bfloat162_rn(s[2], s[3]);
     if (ok)
       *reinterpret_cast<uint2*>(p.out + (size_t)row * p.out_stride + k) =
@@ -918,21 +1080,24 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
     if (et == 0) mbar_arrive(&S.meta_empty[mi]);
     if (mt.kind == 0) break;
     const GroupS& gr = gs[mt.group];
+    const Geo geo = geo_of(p, gr);
     bool ok = true;
     if (mt.kind == 1 && et < gr.gsz)   // the rows' x exponents, fetched while the MMAs run
-      xe_s[et] = __ldcg(&p.xexp[ps[gr.pair_off + et].pq / p.topk]);
+      xe_s[et] = __ldcg(&p.xexp[row_of(p, ps[gr.pair_off + et].pq)]);
     if (mt.kind == 2 && mt.group != dgrp) {
-      // A new group's g2, routing weights and common exponents, fetched while the MMAs run.
-      g2c = __ldg(&p.g2[gr.expert]);
+      // A new group's g2, routing weights (1 for the shared expert) and common
+      // exponents, fetched while the MMAs run.
+      g2c = __ldg(gr.shared ? p.sg2 : &p.g2[gr.expert]);
       if (et < gr.gsz) {
-        tws[et] = __ldg(&p.tw[ps[gr.pair_off + et].pq]);
+        const int pq = ps[gr.pair_off + et].pq;
+        tws[et] = pq < p.P ? __ldg(&p.tw[pq]) : 1.f;
         ok = wait_flag(&p.ready[mt.group], 1u + p.dep_extra, status, deadline);
         em[et] = __ldcg(&p.emax[gr.pair_off + et]);
       }
       dgrp = mt.group;                 // on a failed wait the loop ends below
     }
     // The expert's global scale: g13 for a gate/up item (fetched while its MMAs run), g2 for a down item.
-    const float gsc = mt.kind == 1 ? __ldg(&p.g13[gr.expert]) : g2c;
+    const float gsc = mt.kind == 1 ? __ldg(gr.shared ? p.sg13 : &p.g13[gr.expert]) : g2c;
     const int buf = eg;
     ok = mbar_wait_bounded(&S.acc_full[buf], (ic / 2) & 1, status, QX_DEV_TIMEOUT, deadline) && ok;
     if (!bar_and(B1, 128, ok)) break;
@@ -943,17 +1108,38 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       // ---- gate/up tile: rows 0..63 gate, 64..127 up of columns [64 tile, 64 tile + 64)
       const bool up = m >= 64;
       const int c = m & 63;
+      const int ks = gr.shared ? S.hdr.kss : S.hdr.ks;
+      const size_t gi = gu_index(p, S.hdr, mt.group, mt.tile, gr.shared);   // the (group, tile) item
+      // its pieces' sums: routed items from 0, the shared expert's after MAXSPLIT
+      const size_t gp0 = gr.shared ? (size_t)MAXSPLIT + (gi - MAXSPLIT) * ks : gi * ks;
       for (int q = 0; q < gr.gsz; ++q) {
         float v[16], v1[16];
         tc::ld16x2(tacc + XTERMS * q, tacc + TM_SLOT + XTERMS * q, v, v1);   // v1 holds data only if two
 #pragma unroll
         for (int t = 0; t < XTERMS; ++t) v[t] += two ? v1[t] : 0.f;
-        const float s = tc::term_sum16(v, xe_s[q]) * gsc;
-        if (up) xu[q * 64 + c] = s; else xg[q * 64 + c] = s;
+        const float s = tc::term_sum16(v, xe_s[q]);
+        if (ks > 1) __stcg(p.gpart + ((gp0 + mt.piece) * GMAX + q) * 128 + m, s);
+        else if (up) xu[q * 64 + c] = s * gsc;
+        else xg[q * 64 + c] = s * gsc;
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.acc_empty[buf]);
+      if (ks > 1) {
+        // A piece of a K-split item: its sums are stored (ordered before thread
+        // 0's acq_rel count by the barrier); the item's last piece adds every
+        // piece's sums in piece order and goes on with the tile.
+        asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
+        if (et == 0) *last_flag = atom_add_acq_rel_gpu(&p.pcnt[gi], 1u) == (uint32_t)ks - 1u ? 1u : 0u;
+        asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
+        if (!*last_flag) continue;
+        const float* g0 = p.gpart + gp0 * GMAX * 128 + m;
+        for (int q = 0; q < gr.gsz; ++q) {
+          float s = 0.f;
+          for (int pc = 0; pc < ks; ++pc) s += __ldcg(g0 + ((size_t)pc * GMAX + q) * 128);
+          if (up) xu[q * 64 + c] = s * gsc; else xg[q * 64 + c] = s * gsc;
+        }
+      }
       asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
       const int col0 = mt.tile * 64;
       const int kbl = mt.tile % SK;                   // the tile is K block kbl of down stage tile / SK
@@ -968,8 +1154,9 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
             u = fminf(fmaxf(u, -p.limit), p.limit);
           }
           float a = (g / (1.f + expf(-g))) * u;
-          if (col0 + c >= p.W) a = 0.f;
+          if (col0 + c >= geo.W) a = 0.f;
           xg[q * 64 + c] = a;
+          if (p.ae_fixed) continue;          // the exponent is known: no maximum needed
           float mx = fabsf(a);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -981,7 +1168,7 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       // act = sum_t 2^(el - 2t) q_t (the digit rule of the x terms). Warp w of
       // the group takes pairs w, w + 4; lane l the columns 2l, 2l + 1.
       for (int q = et >> 5; q < gr.gsz; q += 4) {
-        const int el = act_exponent(fmaxf(amx[q][0], amx[q][1]));
+        const int el = p.ae_fixed ? p.ae_val : act_exponent(fmaxf(amx[q][0], amx[q][1]));
         float r0 = xg[q * 64 + 2 * lane], r1 = xg[q * 64 + 2 * lane + 1];
         uint8_t* blk = ab + (size_t)q * XT_STAGE + kbl * XT_KB + (lane >> 4) * 128 + (lane & 12);
         float g = tc::exp2i(el), ig = tc::exp2i(-el);
@@ -993,7 +1180,7 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
           ig *= 4.f;
         }
         if (lane == 0) {
-          p.eloc[(size_t)(gr.pair_off + q) * p.NT + mt.tile] = el;
+          p.eloc[(size_t)(gr.pair_off + q) * MAX_STILES + mt.tile] = el;
           atomicMax(&p.emax[gr.pair_off + q], el);
         }
       }
@@ -1002,10 +1189,15 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
       if (et == 0) {
         const uint32_t old = atom_add_acq_rel_gpu(&p.cnt1[mt.group], 1u);
-        *last_flag = (old == (uint32_t)p.NT - 1u) ? 1u : 0u;
+        *last_flag = (old == (uint32_t)geo.NT - 1u) ? 1u : 0u;
       }
       asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
-      if (*last_flag) {
+      if (*last_flag && p.ae_fixed) {
+        // Last tile of the group, every tile on the one fixed exponent: the
+        // terms are final (the other tiles' stores were acquired through the
+        // count above); release them to the down items.
+        if (et == 0) st_release_gpu(&p.ready[mt.group], 1u);
+      } else if (*last_flag) {
         // Last tile of the group: bring every tile to the pair's common exponent
         // em by moving its terms d = (em - el) / 2 places down (term t becomes
         // term t + d; the last d terms, below the common precision, drop out).
@@ -1013,10 +1205,11 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
         // now; NT x gsz <= 64 gmax), then one item per warp and lane = (K half,
         // term) owning 16 code bytes, four items in flight per warp.
         int* dsh = reinterpret_cast<int*>(xg);
-        const int nit = p.NT * gr.gsz;
+        const int nit = geo.NT * gr.gsz;
         for (int i = et; i < nit; i += 128) {
           const int tile = i / gr.gsz, q = i - tile * gr.gsz;
-          dsh[i] = (__ldcg(&p.emax[gr.pair_off + q]) - __ldcg(&p.eloc[(size_t)(gr.pair_off + q) * p.NT + tile])) >> 1;
+          dsh[i] = (__ldcg(&p.emax[gr.pair_off + q]) -
+                    __ldcg(&p.eloc[(size_t)(gr.pair_off + q) * MAX_STILES + tile])) >> 1;
         }
         asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
         const int ew = et >> 5, t = lane & 15, kh = lane >> 4;
@@ -1080,7 +1273,7 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
   for (int u = blockIdx.x * NEPI + eg; u < HT * rbn; u += gridDim.x * NEPI) {
     const int tile = u / rbn;
     bool ok = true;
-    if (et == 0) ok = wait_flag(&p.fcnt[tile], (uint32_t)S.hdr.n_pairs, status, deadline);
+    if (et == 0) ok = wait_flag(&p.fcnt[tile], (uint32_t)S.hdr.n_fin, status, deadline);
     if (!bar_and(B1, 128, ok)) break;   // every thread's y reads follow thread 0's acquire
     if (!finalize_unit(p, S, u, tile, u - tile * rbn, et, eg, B1, const_cast<uint32_t*>(status), deadline)) break;
   }
@@ -1092,7 +1285,7 @@ __global__ void __launch_bounds__(NTHR, 1) tc_decode_kernel(Params p) {
   uint8_t* ring = smem + p.ring_off;
   float* xg = reinterpret_cast<float*>(smem + p.x_off);
   GroupS* gs = reinterpret_cast<GroupS*>(smem + p.tab_off);
-  PairS* ps = reinterpret_cast<PairS*>(smem + p.tab_off + (size_t)p.P * sizeof(GroupS));
+  PairS* ps = reinterpret_cast<PairS*>(smem + p.tab_off + (size_t)(p.P + p.rows) * sizeof(GroupS));
   const int warp = threadIdx.x >> 5;
   volatile uint32_t* status = &p.ctl->status;
   // Warp 0 loads the call's expert ids while other warps set up the CTA.
@@ -1246,8 +1439,10 @@ size_t qx_slice_workspace_tc_bytes(int32_t rows, int32_t topk, int32_t c0, int32
 
 }  // extern "C"
 
-// The slice call, alone (x == nullptr) or with the fused rank combine.
-static int tc_launch(const QxArena* arena, const QxSliceArgs* a, const QxXchgArgs* x, void* stream) {
+// The slice call, alone (x == nullptr) or with the fused rank combine, and with
+// the shared expert's arena (sh) on the output rank.
+static int tc_launch(const QxArena* arena, const QxSliceArgs* a, const QxXchgArgs* x, const QxArena* sh,
+                     void* stream) {
   if (!arena || !a) return QX_ERR_ARG;
   if (!a->x || !a->ids || !a->tw || !a->out || !a->workspace || !arena->w13 || !arena->w2 || !arena->g13 ||
       !arena->g2)
@@ -1304,6 +1499,8 @@ static int tc_launch(const QxArena* arena, const QxSliceArgs* a, const QxXchgArg
   p.cnt1 = reinterpret_cast<uint32_t*>(ws + L.cnt1);
   p.ready = reinterpret_cast<uint32_t*>(ws + L.ready);
   p.fcnt = reinterpret_cast<uint32_t*>(ws + L.fcnt);
+  p.pcnt = reinterpret_cast<uint32_t*>(ws + L.pcnt);
+  p.gpart = reinterpret_cast<float*>(ws + L.gpart);
   p.emax = reinterpret_cast<int32_t*>(ws + L.emax);
   p.eloc = reinterpret_cast<int32_t*>(ws + L.eloc);
   p.xexp = reinterpret_cast<int32_t*>(ws + L.xexp);
@@ -1315,7 +1512,7 @@ static int tc_launch(const QxArena* arena, const QxSliceArgs* a, const QxXchgArg
     p.bst = p.gmax * XT_STAGE;   // the widest possible group, for the shape check
   }
   // shared memory: [Smem][exchange][tables][rings: ns weight stages | ns activation stages]
-  const size_t tables = (size_t)p.P * (sizeof(GroupS) + sizeof(PairS));
+  const size_t tables = (size_t)(p.P + p.rows) * (sizeof(GroupS) + sizeof(PairS));
   const size_t xchg = (size_t)NEPI * 2 * p.gmax * 64 * sizeof(float);
   p.x_off = (int)((sizeof(Smem) + 15) & ~size_t(15));
   p.tab_off = (int)(((size_t)p.x_off + xchg + 15) & ~size_t(15));
@@ -1325,6 +1522,19 @@ static int tc_launch(const QxArena* arena, const QxSliceArgs* a, const QxXchgArg
   p.ns = p.b_off = 0;
   p.timeout_ns = timeout_ns();
   p.dep_extra = dep_extra();
+  // With the clamp, |act| = |silu(min(g, L)) * clamp(u, -L, L)| <= L^2: one
+  // exponent E with 6 * 2^E >= L^2 covers every tile, so the tiles' terms need
+  // no common-exponent fixup. For L <= 16 the 16 terms then still resolve act
+  // to 2^(E - 31) <= 2^-24, far below the BF16 rounding of the output.
+  p.ae_fixed = 0;
+  p.ae_val = 0;
+  if (p.has_limit && p.limit > 0.f && p.limit <= 16.f) {
+    const double bound = (double)p.limit * (double)p.limit * 1.001;
+    int e = XE_LO;
+    while (6.0 * ldexp(1.0, e) < bound) ++e;
+    p.ae_fixed = 1;
+    p.ae_val = e;
+  }
   p.xworld = 0;
   p.xshared = nullptr;
   p.xshared_stride = 0;
@@ -1349,6 +1559,24 @@ static int tc_launch(const QxArena* arena, const QxSliceArgs* a, const QxXchgArg
     p.xdst = x->dst;
     p.xrows_max = x->rows_max;
   }
+  p.sw13 = p.sw2 = nullptr;
+  p.sg13 = p.sg2 = nullptr;
+  p.sW = p.sNT = 0;
+  if (sh) {
+    if (sh->layout != QX_LAYOUT_TC || sh->n_experts != 1 || !sh->w13 || !sh->w2 || !sh->g13 || !sh->g2)
+      return QX_ERR_ARG;
+    if (sh->a0 % 32 || sh->a1 % 32 || sh->a1 <= sh->a0 || sh->a1 - sh->a0 > MAX_STILES * 64) return QX_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(sh->w13) & 15u) || (reinterpret_cast<uintptr_t>(sh->w2) & 15u))
+      return QX_ERR_ALIGN;
+    // only the rank that writes the output adds the shared expert, and not twice
+    if (p.xworld > 1 && (p.xrank != p.xdst || p.xshared)) return QX_ERR_ARG;
+    p.sw13 = sh->w13;
+    p.sw2 = sh->w2;
+    p.sg13 = sh->g13;
+    p.sg2 = sh->g2;
+    p.sW = sh->a1 - sh->a0;
+    p.sNT = (p.sW + 63) / 64;
+  }
   const size_t smem_bytes = SMEM_LIMIT;
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -1372,12 +1600,18 @@ static int tc_launch(const QxArena* arena, const QxSliceArgs* a, const QxXchgArg
 extern "C" {
 
 int qx_slice_decode_tc(const QxArena* arena, const QxSliceArgs* a, void* stream) {
-  return tc_launch(arena, a, nullptr, stream);
+  return tc_launch(arena, a, nullptr, nullptr, stream);
 }
 
 int qx_slice_decode_tc_xchg(const QxArena* arena, const QxSliceArgs* a, const QxXchgArgs* x, void* stream) {
   if (!x) return QX_ERR_ARG;
-  return tc_launch(arena, a, x, stream);
+  return tc_launch(arena, a, x, nullptr, stream);
+}
+
+int qx_slice_decode_tc_shared(const QxArena* arena, const QxSliceArgs* a, const QxArena* shared,
+                              const QxXchgArgs* x, void* stream) {
+  if (!shared) return QX_ERR_ARG;
+  return tc_launch(arena, a, x, shared, stream);
 }
 
 }  // extern "C"

@@ -152,6 +152,9 @@ SIGNATURES = [
     ("qx_ipc_close", ctypes.c_int, [ctypes.c_void_p]),
     ("qx_slice_decode_tc_xchg", ctypes.c_int,
      [ctypes.POINTER(QxArena), ctypes.POINTER(QxSliceArgs), ctypes.POINTER(QxXchgArgs), ctypes.c_void_p]),
+    ("qx_slice_decode_tc_shared", ctypes.c_int,
+     [ctypes.POINTER(QxArena), ctypes.POINTER(QxSliceArgs), ctypes.POINTER(QxArena), ctypes.POINTER(QxXchgArgs),
+      ctypes.c_void_p]),
     ("qx_combine_p2p", ctypes.c_int, [ctypes.POINTER(QxXchgArgs), ctypes.c_void_p]),
     ("qx_version", ctypes.c_char_p, []),
 ]

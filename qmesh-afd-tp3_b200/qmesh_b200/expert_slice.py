@@ -82,15 +82,27 @@ def _slice_args(x, ids, tw, out, c0, c1, workspace, x_scale, swiglu_limit, has_l
 def launch(view: _lib.QxArena, x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, out: torch.Tensor,
            c0: int, c1: int, workspace: torch.Tensor, x_scale: torch.Tensor | None = None,
            swiglu_limit: float = SWIGLU_LIMIT, has_limit: bool = True, stream=None, layout: str = "tc",
-           xchg: _lib.QxXchgArgs | None = None) -> None:
+           xchg: _lib.QxXchgArgs | None = None, shared: _lib.QxArena | None = None) -> None:
     """Validate and launch one slice call (no allocation, no host sync). `layout` is
     the arena's: "tc" runs qx_slice_decode_tc, "frag" qx_slice_decode. With `xchg`
     (tensor-core layout only) the call also combines the ranks' partials:
-    qx_slice_decode_tc_xchg, see `shard.P2PExchange.slice_combine`."""
+    qx_slice_decode_tc_xchg, see `shard.P2PExchange.slice_combine`. With
+    `shared` (the view of a one-expert tensor-core arena) the same kernel also
+    runs that shared expert over every row with weight 1 and adds its BF16
+    output after the routed partials (qx_slice_decode_tc_shared)."""
     lib = _lib.load()
     args = _slice_args(x, ids, tw, out, c0, c1, workspace, x_scale, swiglu_limit, has_limit)
     if stream is None:
         stream = torch.cuda.current_stream(x.device).cuda_stream
+    if shared is not None:
+        if layout != "tc":
+            raise ValueError("the shared expert runs on the tensor-core slice (layout 'tc')")
+        with rng("qx.slice_shared"):
+            rc = lib.qx_slice_decode_tc_shared(ctypes.byref(view), ctypes.byref(args), ctypes.byref(shared),
+                                               ctypes.byref(xchg) if xchg is not None else None,
+                                               ctypes.c_void_p(stream))
+        _lib.check(rc, "qx_slice_decode_tc_shared")
+        return
     if xchg is not None:
         if layout != "tc":
             raise ValueError("the fused rank combine runs on the tensor-core slice (layout 'tc')")

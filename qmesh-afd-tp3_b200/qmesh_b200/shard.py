@@ -124,11 +124,15 @@ class P2PExchange:
 
     def slice_combine(self, view, x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, out: torch.Tensor,
                       c0: int, c1: int, workspace: torch.Tensor, x_scale: torch.Tensor | None = None,
-                      shared: torch.Tensor | None = None, stream=None, **kw) -> torch.Tensor | None:
+                      shared: torch.Tensor | None = None, shared_expert=None, stream=None,
+                      **kw) -> torch.Tensor | None:
         """The slice of this rank's columns with the combine fused into its
         finalize (`qx_slice_decode_tc_xchg`): one kernel per rank and step. On
         the output rank `out` receives bf16(p0 + ... [+ shared]) and is returned;
-        senders do not write `out` and get None. A wait that runs out sets
+        senders do not write `out` and get None. `shared` is a BF16 partial
+        computed elsewhere; `shared_expert` (output rank only) is the view of a
+        one-expert arena that the same kernel runs over every row with weight 1
+        and adds last (`qx_slice_decode_tc_shared`). A wait that runs out sets
         QX_DEV_TIMEOUT in the workspace status (`expert_slice.device_status`)."""
         from .expert_slice import launch
         self._use("fused")
@@ -143,7 +147,10 @@ class P2PExchange:
             if shared.dtype != torch.bfloat16 or tuple(shared.shape) != (rows, self._L.HIDDEN) or shared.stride(1) != 1:
                 raise TypeError("shared partial must be bf16 [rows, 5120] with unit column stride")
             a.shared, a.shared_stride = shared.data_ptr(), shared.stride(0)
-        launch(view, x, ids, tw, out, c0, c1, workspace, x_scale=x_scale, stream=stream, layout="tc", xchg=a, **kw)
+        if shared_expert is not None and (self.rank != self.dst or shared is not None):
+            raise ValueError("only the output rank runs the shared expert, and not beside a shared partial")
+        launch(view, x, ids, tw, out, c0, c1, workspace, x_scale=x_scale, stream=stream, layout="tc", xchg=a,
+               shared=shared_expert, **kw)
         return out if self.rank == self.dst else None
 
     def combine(self, part: torch.Tensor, out: torch.Tensor | None = None, shared: torch.Tensor | None = None,

@@ -277,3 +277,77 @@ def test_fused_combine_reports_a_missing_rank():
     assert res[0][0] == 0 and res[1][0] == 0
     assert res[0][1] & 2 and res[1][1] == 0
     assert res[0][2] == res[1][2] == 999000.0
+
+
+# ---- the shared expert inside the output rank's fused kernel (qx_slice_decode_tc_shared)
+
+def _shared_worker(rank, world, port, rows, q):
+    import sys
+    for p in (str(ROOT), str(PKG)):
+        sys.path.insert(0, p)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from qmesh_b200 import shard
+    from qmesh_b200.arena import Arena
+    from qmesh_b200.expert_slice import alloc_workspace, device_status, expert_slice
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=dev, timeout=__import__("datetime").timedelta(seconds=60))
+    xf = xc = None
+    try:
+        a0, a1 = shard.shard_range(rank, world)
+        ar = Arena(dev, 1, 16, a0, a1)
+        ar.fill_synthetic(0, seed=7)
+        sh = Arena(dev, 1, 1, 0, 2304)             # the shared expert, full width, on the output rank
+        sh.fill_synthetic(0, seed=8)
+        xf = shard.P2PExchange(rows_max=8, dst=0, device=dev)
+        xc = shard.P2PExchange(rows_max=8, dst=0, device=dev)
+        ws = alloc_workspace(rows, 6, a0, a1, dev)
+        ws_s = alloc_workspace(rows, 1, 0, 2304, dev)
+        zeros = torch.zeros(rows, 1, dtype=torch.int32, device=dev)
+        ones = torch.ones(rows, 1, dtype=torch.float32, device=dev)
+        equal, statuses = [], []
+        for step in range(STEPS):
+            ids, tw, xq, inv = (t.to(dev) for t in _fused_case(step, rows))
+            out = torch.full((rows, 5120), float("nan"), dtype=torch.bfloat16, device=dev)
+            got = xf.slice_combine(ar.view(0), xq, ids, tw, out, a0, a1, ws, x_scale=inv,
+                                   shared_expert=sh.view(0) if rank == 0 else None)
+            statuses.append(device_status(ws))
+            part = expert_slice(ar, 0, xq, ids, tw, x_scale=inv)
+            sh_out = expert_slice(sh, 0, xq, zeros, ones, x_scale=inv, workspace=ws_s) if rank == 0 else None
+            want = xc.combine(part, shared=sh_out)
+            torch.cuda.synchronize()
+            if rank == 0:
+                equal.append(bool(torch.equal(got, want)))
+        q.put((rank, equal, statuses))
+    finally:
+        for x in (xf, xc):
+            if x is not None:
+                x.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("rows", [6, 2])
+def test_fused_combine_with_shared_expert_kernel(rows):
+    """The output rank runs the shared expert as extra items of its fused kernel:
+    the combined output equals the routed partials plus a separate shared-expert
+    call (ids 0, weight 1) combined by qx_combine_p2p, bit for bit, step after step."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = min(torch.cuda.device_count(), 8)
+    port = 29700 + os.getpid() % 90 + rows
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_shared_worker, args=(r, world, port, rows, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, equal, statuses = q.get(timeout=300)
+        res[r] = (equal, statuses)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert res[r][1] == [0] * STEPS, f"rank {r}: {res[r][1]}"
+    assert res[0][0] == [True] * STEPS
