@@ -6,49 +6,56 @@
 // Same contract and numerics bar as qx_slice_decode (the reference v7 body,
 // gx/kernels/fp4_decode_moe_swz.cu:187-402: x = bf16(e4m3 * inv),
 // g, u = g13 * x.W, act = min(g,L)/(1+exp(-min(g,L))) * clamp(u,-L,L),
-// y_j = g2 * tw_j * act.W2, out = bf16(sum_j y_j)). The activation side of each
-// product enters the MMA as eight residual NVFP4 terms with power-of-two column
-// scales: the gate/up input x as 16 unscaled e2m1 terms (x = sum_t 2^(E-2t) q_t,
-// to 2^-30 of the row maximum), the SwiGLU output as 8 block-scaled NVFP4 terms
-// (to about 2^-24 of each 16-element block's maximum). Each term's product with
-// the weights is exact in the tensor core and the partial sums meet in FP32 in
-// the epilogue.
+// y_j = g2 * tw_j * act.W2, out = bf16(sum_j y_j)). The activation side of
+// every product enters the MMA as 16 unscaled e2m1 terms on an exponent grid of
+// step 2 (v = sum_t 2^(E - 2t) q_t, to 2^-30 of the exponent's range; the
+// B-side block scales are a constant 1.0 atom): the gate/up input x with one
+// exponent per row, the SwiGLU output with one exponent per pair, fixed at the
+// clamp's bound L^2 when the clamp is on (else per tile, moved to the pair's
+// largest by the group's last tile). Each term's product with the weights is
+// exact in the tensor core and the partial sums meet in FP32 in the epilogue.
 //
 // Kernels, chained with programmatic dependent launch:
 //   tc_prep_kernel     one CTA per (row, 512-element chunk): the reference
 //                      ingest, the row's exponent, the chunk's 16 x terms in the
 //                      row-major operand layout (one 4,096-byte block per row and
-//                      stage); CTA 0 also resets the call's counters and checks the
-//                      ids. Independent of the routing, so it runs while the
-//                      decode kernel starts.
-//   tc_decode_kernel   persistent, one CTA per SM, 7 warps. Every CTA first
-//                      builds the routing tables itself from the ids (unique
-//                      experts, groups of <= 6 routed pairs of one expert, the
-//                      item counts; deterministic, so all CTAs agree), then
-//                      warp 0    producer: streams each item's weight tile (bulk async
-//                                copy, 8 K blocks = 36,864 bytes per stage) and
-//                                activation operand into a shared-memory ring; the
-//                                first item is the CTA's index and its weights are
-//                                in flight before the prep kernel is waited for,
-//                                later items come from one atomic queue;
-//                      warps 1, 6  MMA issuers: each copies its K blocks' scale atoms
-//                                into TMEM and issues one M=128 x N x K=64
-//                                block-scaled MMA per K block (the lower / upper
-//                                half of every stage's K blocks) into its own
-//                                accumulator;
-//                      warps 2-5 epilogue: gate/up items -> SwiGLU -> the pair's
-//                                activation terms for the down projection
-//                                (tile-local exponent, fixed up by the group's last
-//                                tile); down items -> y_j = g2 tw_j act.W2 per
-//                                output row.
+//                      stage); resets the call's counters and checks the ids.
+//                      Independent of the routing, so it runs while the decode
+//                      kernel starts.
+//   tc_decode_kernel   persistent, one CTA per SM, 352 threads (11 warps). Every
+//                      CTA first builds the routing tables itself from the ids
+//                      (unique experts, groups of <= 6 routed pairs of one
+//                      expert, then the shared expert's groups of rows when one
+//                      is given; deterministic, so all CTAs agree), then
+//                      warp 0      producer: streams each item's weight tile (bulk
+//                                  async copy, 8 K blocks = 36,864 bytes per stage)
+//                                  and activation operand into a shared-memory
+//                                  ring; the first item is the CTA's index and its
+//                                  weights are in flight before the prep kernel is
+//                                  waited for, later items come from one atomic
+//                                  queue;
+//                      warps 1, 6  MMA issuers: each copies its K blocks' scale
+//                                  atoms into TMEM and issues one M=128 x N x K=64
+//                                  block-scaled MMA per K block (the lower / upper
+//                                  half of every stage's K blocks) into its own
+//                                  accumulator;
+//                      warps 2-5, 7-10  two epilogue warpgroups, taking alternate
+//                                  items: gate/up -> SwiGLU -> the pair's 16
+//                                  activation terms for the down projection; down ->
+//                                  y_j = g2 tw_j act.W2 per output row; then
+//                                  finalize units.
 //                      Items: gate/up (group, 64-column tile: 64 gate + 64 up rows
-//                      over K = 5120) then down (group, 128-row output tile over
-//                      the slice's columns). A down item waits (bounded) for its
-//                      group's activation terms. Every down item counts its
+//                      over K = 5120, split into 2, 5 or 10 K pieces when a call
+//                      has too few items to fill the grid, the last piece adding
+//                      the pieces' sums in order), then down (group, 128-row output
+//                      tile over the slice's columns). A down item waits (bounded)
+//                      for its group's activation terms. Every down item counts its
 //                      pairs into its 128-row output tile's counter; after its
 //                      items each epilogue group finalizes some (output tile,
 //                      4-row block) units, out = bf16(sum over slots j in order
-//                      of y_j), once their tile's counter is complete.
+//                      of y_j) [+ the shared expert's bf16 output], once their
+//                      tile's counter is complete, or hands them to the fused rank
+//                      combine (qx_xchg.cuh).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <limits.h>

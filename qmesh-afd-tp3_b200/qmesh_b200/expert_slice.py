@@ -238,10 +238,12 @@ class HostSlice:
     side streams of their own, so call k+1's inputs move while call k computes
     and call k's output moves while call k+1 computes; the slice itself runs on
     the caller's current stream, after its inputs have landed. Two staging slots
-    alternate, each guarded by events. The returned host tensor belongs to that
-    call's slot and stays valid until the call after next; read it after
-    `synchronize()` (host) or `join(stream)` (device ordering) or a device-wide
-    synchronisation.
+    alternate, each guarded by events. Without `out`, the returned host tensor
+    belongs to that call's slot and is overwritten by the call after next (a
+    caller that keeps outputs passes `out`, or copies); with `out` (a host BF16
+    tensor [rows, 5120], pinned for an asynchronous copy) the output lands there
+    and is the caller's to keep. Either way, read it after `synchronize()`
+    (host) or `join(stream)` (device ordering) or a device-wide synchronisation.
     """
 
     def __init__(self, arena: Arena, rows: int, topk: int = 6, c0: int | None = None, c1: int | None = None,
@@ -280,10 +282,13 @@ class HostSlice:
         return x, s, i, t
 
     def __call__(self, li: int, x: torch.Tensor, x_scale: torch.Tensor, ids: torch.Tensor,
-                 tw: torch.Tensor) -> torch.Tensor:
+                 tw: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         n = x.shape[0]
         if not 1 <= n <= self.rows or ids.shape != (n, self.topk) or tw.shape != (n, self.topk):
             raise ValueError(f"call of {n} rows / ids {tuple(ids.shape)} outside this HostSlice ({self.rows} x {self.topk})")
+        if out is not None and (out.device.type != "cpu" or out.dtype != torch.bfloat16
+                                or tuple(out.shape) != (n, _lib.HIDDEN)):
+            raise TypeError(f"out must be a host bf16 [{n}, {_lib.HIDDEN}] tensor")
         k = self.k
         self.k = (k + 1) % len(self.host)
         if self.used[k]:
@@ -310,12 +315,13 @@ class HostSlice:
                layout=self.arena.layout)
         self.ev_done[k].record(stream)
         self.out_stream.wait_event(self.ev_done[k])
+        dst = self.out_h[k][:n] if out is None else out
         with rng("qx.d2h"), torch.cuda.stream(self.out_stream):
-            self.out_h[k][:n].copy_(self.out_d[k][:n], non_blocking=True)
+            dst.copy_(self.out_d[k][:n], non_blocking=True)
         self.ev_out[k].record(self.out_stream)
         self.used[k] = True
         self.last = k
-        return self.out_h[k][:n]
+        return dst
 
     def order_after(self, stream=None) -> None:
         """Order the next calls' input copies after the work queued so far on

@@ -3,6 +3,8 @@
 from __future__ import annotations
 
 import functools
+import json
+import os
 
 import torch
 
@@ -45,20 +47,37 @@ def element_ulp(ref: torch.Tensor, mag: torch.Tensor | None = None) -> torch.Ten
 
 
 def parity(out: torch.Tensor, ref: torch.Tensor, mag: torch.Tensor | None = None) -> dict:
+    """Errors of `out` against `ref`: relative L2; the ulp measure the tolerance
+    uses (max_ulp, with the row floor and `mag`); and the literal per-element
+    figure of the north star, the BF16 ulp at |ref| alone (max_ulp_floorless),
+    with the count of elements beyond 2 such ulp."""
     out = out.float().cpu()
     ref = ref.float().cpu()
     err = (out - ref).abs()
     rel = (err.norm() / ref.norm().clamp_min(1e-30)).item()
     u = err / element_ulp(ref, mag)
+    u0 = err / bf16_ulp(ref)
     i = int(u.argmax())
     idx = [int(v) for v in torch.unravel_index(torch.tensor(i), ref.shape)]
     return {"rel_l2": rel, "max_ulp": u.max().item(), "max_abs": err.max().item(),
+            "max_ulp_floorless": u0.max().item(), "n_over_2ulp_floorless": int((u0 > MAX_ULP).sum()),
+            "n_over_1ulp_floorless": int((u0 > 1.0).sum()), "elements": ref.numel(),
             "exact": float((err == 0).float().mean()), "worst": {"at": idx, "out": out.flatten()[i].item(),
                                                                 "ref": ref.flatten()[i].item()}}
 
 
 def assert_parity(out, ref, what="", mag=None):
+    """The north-star tolerance (relative L2 and ulp with the floor). Every call
+    prints its figures, floor-free ones included, and appends them as a JSON
+    line to $QX_PARITY_LOG when that is set."""
     p = parity(out, ref, mag)
+    print(f"parity {what}: relL2 {p['rel_l2']:.2e} max_ulp {p['max_ulp']:.2f} floor-free max_ulp "
+          f"{p['max_ulp_floorless']:.2f} ({p['n_over_2ulp_floorless']} of {p['elements']} elements > 2 ulp)")
+    log = os.environ.get("QX_PARITY_LOG")
+    if log:
+        with open(log, "a") as f:
+            f.write(json.dumps({"what": what, "test": os.environ.get("PYTEST_CURRENT_TEST", ""),
+                                **{k: v for k, v in p.items() if k != "worst"}}) + "\n")
     assert p["rel_l2"] <= REL_L2 and p["max_ulp"] <= MAX_ULP, f"{what} {p}"
     return p
 

@@ -140,3 +140,28 @@ def test_host_slice_pipelined_calls(cuda_ready):
         want = expert_slice(ar, 0, q.to(dev), ids.to(dev), tw.to(dev), x_scale=inv.to(dev))
         torch.cuda.synchronize()
         assert torch.equal(got[step], want.cpu()), f"call {step}"
+
+
+def test_host_slice_out_keeps_every_call(cuda_ready):
+    """With `out`, each of five pipelined calls' outputs lands in the caller's own
+    pinned tensor and all five stay valid (without it only the last two would)."""
+    from qmesh_b200.arena import Arena
+    from qmesh_b200.expert_slice import HostSlice, expert_slice
+    dev = cuda_ready
+    layer = H.small_layer(35, 8, inter=256)
+    ar = Arena(dev, 1, 8, 0, 256, layout="tc")
+    ar.load_layer(0, layer)
+    hs = HostSlice(ar, 6)
+    cases, outs = [], []
+    for step in range(5):
+        ids, tw = H.random_routing(6, 8, 90 + step)
+        _, q, inv = H.activations(6, 90 + step)
+        cases.append((q, inv, ids, tw))
+        o = torch.empty(6, 5120, dtype=torch.bfloat16).pin_memory()
+        assert hs(0, q, inv, ids, tw, out=o) is o
+        outs.append(o)
+    hs.synchronize()
+    for step, (q, inv, ids, tw) in enumerate(cases):
+        want = expert_slice(ar, 0, q.to(dev), ids.to(dev), tw.to(dev), x_scale=inv.to(dev))
+        torch.cuda.synchronize()
+        assert torch.equal(outs[step], want.cpu()), f"call {step}"
