@@ -20,8 +20,9 @@
 //                      expert, each group's operand offsets and scales;
 //   pf_place_kernel    each pair's position in its expert's range (any order:
 //                      a pair's result does not depend on its neighbours);
-//   pf_xquant_kernel   one CTA per position: the row's NVFP4 codes and scales
-//                      written straight into its group's B operand (MMA layout);
+//   pf_xquant_kernel   one CTA per token row: the row's NVFP4 codes and scales,
+//                      quantised once, written straight into the B operand of
+//                      each of the row's routed pairs (MMA layout);
 //   pf_main_kernel     persistent, one CTA per SM: items gate/up (group,
 //                      64-column tile) then down (group, 128-row tile), the same
 //                      producer / two MMA issuers / two epilogue warpgroups
@@ -106,6 +107,7 @@ struct Params {
   Group* groups;      // [gmax]
   int32_t* grp_of_pos;// [P] group of a position
   int32_t* pos_pair;  // [P] pair at a position
+  int32_t* pos_of;    // [P] position of a pair (routed pairs only)
   uint32_t* cnt1;     // [gmax] gate/up tiles finished per group
   uint8_t* xq;        // per group: 10 stages of sbs bytes
   uint8_t* ab;        // per group: ceil(NT/8) stages of sbs bytes
@@ -131,7 +133,7 @@ __host__ __device__ inline int sbs_of(int npad) { return npad * 256 + SK * tc::S
 __host__ __device__ inline int groups_bound(int P, int E) { return P / GP + (E < P ? E : P) + 1; }
 
 struct WsLayout {
-  size_t ctl, cnt, fill, off, groups, grp_of_pos, pos_pair, cnt1, xq, ab, y, total;
+  size_t ctl, cnt, fill, off, groups, grp_of_pos, pos_pair, pos_of, cnt1, xq, ab, y, total;
 };
 
 __host__ inline WsLayout ws_layout(int rows, int topk, int W, int E) {
@@ -146,6 +148,7 @@ __host__ inline WsLayout ws_layout(int rows, int topk, int W, int E) {
   L.groups = o;     o = al256(o + (size_t)G * sizeof(Group));
   L.grp_of_pos = o; o = al256(o + (size_t)P * 4);
   L.pos_pair = o;   o = al256(o + (size_t)P * 4);
+  L.pos_of = o;     o = al256(o + (size_t)P * 4);
   L.cnt1 = o;       o = al256(o + (size_t)G * 4);
   L.xq = o;         o = al256(o + (size_t)(KB1 / SK) * opnd);
   L.ab = o;         o = al256(o + (size_t)((NT + SK - 1) / SK) * opnd);
@@ -234,7 +237,16 @@ __global__ void __launch_bounds__(256) pf_prep_kernel(Params p) {
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  if ((t & 31) == 0) atomicMax(&p.ctl->amax_bits, __float_as_uint(amax));   // amax >= 0: bits order as values
+  // one atomic per row (every row's CTA hits the same word: keep them few)
+  __shared__ float wmax[8];
+  if ((t & 31) == 0) wmax[t >> 5] = amax;
+  __syncthreads();
+  if (t == 0) {
+    float m = wmax[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, wmax[i]);
+    atomicMax(&p.ctl->amax_bits, __float_as_uint(m));   // amax >= 0: bits order as values
+  }
   if (t < p.topk) {
     const long long id = id_of(p, r * p.topk + t);
     if (id >= 0 && id < p.E) atomicAdd(&p.cnt[id], 1u);
@@ -360,18 +372,16 @@ __global__ void __launch_bounds__(256) pf_place_kernel(Params p) {
   if (id < 0 || id >= p.E) return;
   const uint32_t pos = p.off[id] + atomicAdd(&p.fill[id], 1u);
   p.pos_pair[pos] = q;
+  p.pos_of[q] = (int32_t)pos;
 }
 
-// One CTA per position: the NVFP4 codes and scales of its row (x quantised with
-// a1g) into its group's B operand: stage s, row r: codes at
-// (r / 8) 2048 + kb 256 + (K half) 128 + (r % 8) 16, scales in the stage's K-block
-// atoms at npad 256 + kb 512 + (r % 32) 16 + (r / 32) 4 + j.
+// One CTA per token row: the row's NVFP4 codes and scales (x quantised with
+// a1g, once), written into the B operand of every routed pair of the row at
+// its position r in its group: stage s, codes at (r / 8) 2048 + kb 256 +
+// (K half) 128 + (r % 8) 16, scales in the stage's K-block atoms at
+// npad 256 + kb 512 + (r % 32) 16 + (r / 32) 4 + j.
 __global__ void __launch_bounds__(XQ_THR) pf_xquant_kernel(Params p) {
-  const int pos = blockIdx.x;
-  if (pos >= (int)p.ctl->n_valid) return;
-  const int q = p.pos_pair[pos], t = q / p.topk;
-  const Group g = p.groups[p.grp_of_pos[pos]];
-  const int r = pos - g.pos_off;
+  const int t = blockIdx.x;
   const float inv = row_inv(p, t);
   const uint8_t* xr = reinterpret_cast<const uint8_t*>(p.x) + (size_t)t * p.x_stride;
   const int b = threadIdx.x;                     // 16-element block
@@ -380,10 +390,18 @@ __global__ void __launch_bounds__(XQ_THR) pf_xquant_kernel(Params p) {
   uint32_t w[2];
   const uint32_t sb = quant16(v, p.ctl->a1g, w);
   const int s = b >> 5, kb = (b >> 2) & (SK - 1), j = b & 3;
-  uint8_t* st = p.xq + g.xq_off + (size_t)s * g.sbs;
-  *reinterpret_cast<uint2*>(st + (r >> 3) * 2048 + kb * 256 + (j >> 1) * 128 + (r & 7) * 16 + (j & 1) * 8) =
-      make_uint2(w[0], w[1]);
-  st[g.npad * 256 + kb * 512 + (r & 31) * 16 + (r >> 5) * 4 + j] = (uint8_t)sb;
+  for (int k = 0; k < p.topk; ++k) {
+    const int q = t * p.topk + k;
+    const long long id = id_of(p, q);
+    if (id < 0 || id >= p.E) continue;
+    const int pos = p.pos_of[q];
+    const Group& g = p.groups[p.grp_of_pos[pos]];
+    const int r = pos - g.pos_off;
+    uint8_t* st = p.xq + g.xq_off + (size_t)s * g.sbs;
+    *reinterpret_cast<uint2*>(st + (r >> 3) * 2048 + kb * 256 + (j >> 1) * 128 + (r & 7) * 16 + (j & 1) * 8) =
+        make_uint2(w[0], w[1]);
+    st[g.npad * 256 + kb * 512 + (r & 31) * 16 + (r >> 5) * 4 + j] = (uint8_t)sb;
+  }
 }
 
 // ------------------------------------------------------------------ main kernel
@@ -852,6 +870,7 @@ int qx_slice_prefill_tc(const QxArena* arena, const QxSliceArgs* a, const float*
   p.groups = reinterpret_cast<Group*>(ws + L.groups);
   p.grp_of_pos = reinterpret_cast<int32_t*>(ws + L.grp_of_pos);
   p.pos_pair = reinterpret_cast<int32_t*>(ws + L.pos_pair);
+  p.pos_of = reinterpret_cast<int32_t*>(ws + L.pos_of);
   p.cnt1 = reinterpret_cast<uint32_t*>(ws + L.cnt1);
   p.xq = ws + L.xq;
   p.ab = ws + L.ab;
@@ -867,7 +886,7 @@ int qx_slice_prefill_tc(const QxArena* arena, const QxSliceArgs* a, const float*
   pf_prep_kernel<<<p.rows, 256, 0, st>>>(p);
   pf_route_kernel<<<1, RT_THR, 0, st>>>(p);
   pf_place_kernel<<<(p.P + 255) / 256, 256, 0, st>>>(p);
-  pf_xquant_kernel<<<p.P, XQ_THR, 0, st>>>(p);
+  pf_xquant_kernel<<<p.rows, XQ_THR, 0, st>>>(p);
   pf_main_kernel<<<sms, NTHR, SMEM_LIMIT, st>>>(p);
   pf_finalize_kernel<<<(p.rows * (HID / 8) + 255) / 256 < 4 * sms ? (p.rows * (HID / 8) + 255) / 256 : 4 * sms, 256,
                        0, st>>>(p);
