@@ -106,14 +106,15 @@ constexpr int NISS = 2, KB_PER_ISS = SK / NISS;
 static_assert(KB_PER_ISS * 4 <= (int)TM_BANK, "a stage's scale atoms fit one bank");
 static_assert(GMAX * XTERMS <= 96, "an accumulator fits its slot");
 constexpr int XE_LO = -90, XE_HI = 100;      // x exponents
-// K-split of gate/up items: when a call has fewer (group, tile) items than
-// SPLIT_PER_CTA x the grid (narrow column shards), each item's 10 stages are
-// split into ks pieces (ks in {1, 2, 5, 10}, the smallest that reaches the
-// target); a piece stores its FP32 sums and the last piece of an item adds the
-// pieces in piece order. At most MAXSPLIT pieces per call.
-constexpr int SPLIT_PER_CTA = 4;
-constexpr int MAXSPLIT = 1536;     // routed pieces
-constexpr int MAXSPLIT_S = 512;    // shared-expert pieces (their own split, after the routed ones)
+// K-split of gate/up items: the (group, tile) items that fill whole waves of
+// the grid run whole; the remainder, which would leave most CTAs idle in a last
+// partial wave (narrow column shards), is split into ks pieces of 10 / ks stages
+// (ks in {1, 2, 5, 10}, the largest that keeps the pieces within one wave). A
+// piece stores its FP32 sums and the last piece of an item adds the pieces in
+// piece order. At most MAXSPLIT pieces per call.
+constexpr int MAXSPLIT = 512;      // routed pieces (a split never exceeds the grid)
+constexpr int MAXSPLIT_S = MAXSPLIT;   // shared-expert pieces (their own split, after the routed ones;
+                                       // the same cap, so they split as a call of their arena alone)
 constexpr int MAX_STILES = 64;     // shared-expert column tiles at most (4096 columns)
 constexpr int MAXSG = (QX_MAX_ROWS + 5) / 6;   // shared-expert groups at most
 constexpr int AE_LO = -90, AE_HI = 100;      // SwiGLU-output exponents (even)
@@ -136,11 +137,12 @@ static_assert(sizeof(GroupS) == 32, "shared group record is 32 bytes");
 struct RouteHdr {   // call-wide results of the routing, in shared memory
   int32_t n_groups, n1, n2, b_max;   // routed groups, gate/up items (pieces), down items, widest activation stage
   int32_t n_pairs;                   // routed pairs with a valid expert
-  int32_t ks, kss;                   // pieces per gate/up (group, tile) item: routed, shared expert
+  int32_t ks, kss;                   // pieces per split gate/up (group, tile) item: routed, shared expert
+  int32_t fw, fws;                   // gate/up (group, tile) items that run whole: routed, shared expert
   int32_t n_sgroups;                 // shared-expert groups (gs[n_groups ...])
   int32_t n1s, n2s;                  // the first n1s gate/up and n2s down items are the shared expert's
   int32_t n_fin;                     // pairs whose y every output tile waits for (routed + shared rows)
-  int32_t pad[5];
+  int32_t pad[3];
 };
 
 struct PairS {      // per group position: pair index (row * topk + slot)
@@ -209,7 +211,8 @@ struct ItemMeta {
   int32_t kind;       // 1 gate/up, 2 down, 0 end
   int32_t group, tile, nst, nkb_last;
   int32_t piece;      // gate/up: the item's K piece (stages piece * nst ...)
-  int32_t pad[2];
+  int32_t ks;         // gate/up: pieces of its (group, tile) item (1: whole)
+  int32_t gi;         // gate/up piece: index of its (group, tile) item among the split ones
 };
 
 __host__ __device__ inline size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -273,11 +276,6 @@ __device__ __forceinline__ Geo geo_of(const Params& p, const GroupS& g) {
 // the shared expert's are P + row.
 __device__ __forceinline__ int row_of(const Params& p, int pq) { return pq < p.P ? pq / p.topk : pq - p.P; }
 
-// Index of a gate/up (group, tile) item among the piece counters: routed items
-// first, the shared expert's after MAXSPLIT (only items of a split kind count).
-__device__ __forceinline__ size_t gu_index(const Params& p, const RouteHdr& h, int group, int tile, bool shared) {
-  return shared ? (size_t)MAXSPLIT + (size_t)(group - h.n_groups) * p.sNT + tile : (size_t)group * p.NT + tile;
-}
 
 // ------------------------------------------------------------------ prologue
 // SwiGLU-output exponent of one pair over one 64-column tile: the smallest EVEN
@@ -542,22 +540,21 @@ __device__ void route_sort(const Params& p, const int (&idr)[IDR], GroupS* gs, P
   __syncwarp();
 }
 
-// Pieces per gate/up item: the smallest of 1, 2, 5, 10 that gives every CTA
-// SPLIT_PER_CTA items, within `cap` pieces. Depends only on the item count, so
-// a call's routed items split the same with or without a shared expert, and a
-// shared expert the same as the equal call of its arena alone.
-__device__ __forceinline__ int split_of(int items, int cap) {
-  const int target = SPLIT_PER_CTA * (int)gridDim.x;
+// Split of `items` gate/up (group, tile) items over the grid: the first *whole
+// (a multiple of the grid) run whole; the rest, fewer than the grid, run as ks
+// pieces each, ks the largest of 1, 2, 5, 10 with rest x ks <= grid (and
+// <= cap). Depends only on the item count and the grid, so a call's routed
+// items split the same with or without a shared expert, and a shared expert the
+// same as a call of its arena alone.
+__device__ __forceinline__ int split_of(int items, int cap, int* whole) {
+  const int grid = (int)gridDim.x;
+  *whole = items - items % grid;
+  const int rest = items - *whole;
   int ks = 1;
-  if (items < target) {
-    const int opt[3] = {2, 5, 10};
+  const int opt[3] = {2, 5, 10};
 #pragma unroll
-    for (int i = 0; i < 3; ++i) {
-      if (items * opt[i] > cap) break;
-      ks = opt[i];
-      if (items * opt[i] >= target) break;
-    }
-  }
+  for (int i = 0; i < 3; ++i)
+    if (rest * opt[i] <= grid && rest * opt[i] <= cap) ks = opt[i];
   return ks;
 }
 
@@ -590,12 +587,16 @@ __device__ void route_finish(const Params& p, GroupS* gs, PairS* ps, RouteHdr* h
   }
   __syncwarp();
   if (lane == 0) {
-    const int ks = split_of(G * p.NT, MAXSPLIT), kss = Gs ? split_of(Gs * p.sNT, MAXSPLIT_S) : 1;
+    int fw = 0, fws = 0;
+    const int ks = split_of(G * p.NT, MAXSPLIT, &fw);
+    const int kss = Gs ? split_of(Gs * p.sNT, MAXSPLIT_S, &fws) : 1;
     hdr->ks = ks;
     hdr->kss = kss;
+    hdr->fw = fw;
+    hdr->fws = fws;
     hdr->n_sgroups = Gs;
-    hdr->n1s = Gs * p.sNT * kss;
-    hdr->n1 = hdr->n1s + G * p.NT * ks;
+    hdr->n1s = fws + (Gs * p.sNT - fws) * kss;
+    hdr->n1 = hdr->n1s + fw + (G * p.NT - fw) * ks;
     hdr->n2s = Gs * HT;
     hdr->n2 = (G + Gs) * HT;
     hdr->n_fin = Pv + (Gs ? p.rows : 0);
@@ -680,16 +681,16 @@ __device__ __forceinline__ bool bar_and(int id, int n, bool pred) {
 }
 
 // Bounded wait until a global flag set by other CTAs reaches `need` (acquire).
+// The deadline is checked on the clock; the status word (another L2 round
+// trip) only every 64 polls.
 __device__ bool wait_flag(const uint32_t* flag, uint32_t need, volatile uint32_t* status, uint64_t deadline) {
   for (uint32_t it = 0;; ++it) {
     if (ld_acquire_gpu(flag) >= need) return true;
-    if ((it & 7u) == 7u) {
-      if (*status & QX_DEV_TIMEOUT) return false;
-      if (globaltimer_ns() > deadline) {
-        atomicOr(const_cast<uint32_t*>(status), (uint32_t)QX_DEV_TIMEOUT);
-        return false;
-      }
+    if (globaltimer_ns() > deadline) {
+      atomicOr(const_cast<uint32_t*>(status), (uint32_t)QX_DEV_TIMEOUT);
+      return false;
     }
+    if ((it & 63u) == 63u && (*status & QX_DEV_TIMEOUT)) return false;
     __nanosleep(64);
   }
 }
@@ -708,6 +709,7 @@ struct Smem {       // fixed part of the dynamic shared memory, before the rings
   int32_t xe[NEPI][GMAX];     // gate/up item: the group's rows' x exponents
   float tws[NEPI][GMAX];      // down item: the group's routing weights
   uint32_t xcall[NEPI];       // fused combine: the call number of the unit in hand
+  uint32_t fpend[NEPI][HT];   // down items: routed pairs whose y this group wrote, per output tile, not yet released
   RouteHdr hdr;
 };
 
@@ -740,15 +742,24 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
     if (!ok || item >= n1 + n2) {
       m.kind = 0;
     } else if (item < n1) {
-      // Gate/up pieces: the shared expert's first, then the routed groups'.
-      // Pieces of one (group, tile) are consecutive items, so they run side by side.
+      // Gate/up items: the shared expert's first, then the routed groups'; of
+      // each, the whole items, then the pieces of the split ones (pieces of one
+      // (group, tile) are consecutive, so they run side by side).
       const bool sh = item < n1s;
-      const uint32_t ks = (uint32_t)(sh ? hdr.kss : hdr.ks), nt = (uint32_t)(sh ? p.sNT : p.NT);
-      const uint32_t loc = sh ? item : item - n1s, it = loc / ks;
+      const uint32_t nt = (uint32_t)(sh ? p.sNT : p.NT), fw = (uint32_t)(sh ? hdr.fws : hdr.fw);
+      const uint32_t loc = sh ? item : item - n1s;
+      uint32_t it = loc, ks = 1, piece = 0;
+      if (loc >= fw) {
+        ks = (uint32_t)(sh ? hdr.kss : hdr.ks);
+        it = fw + (loc - fw) / ks;
+        piece = (loc - fw) % ks;
+      }
       m.kind = 1;
       m.group = (int)(it / nt) + (sh ? G : 0);
       m.tile = (int)(it % nt);
-      m.piece = (int)(loc - it * ks);
+      m.piece = (int)piece;
+      m.ks = (int)ks;
+      m.gi = (int)(it - fw) + (sh ? MAXSPLIT : 0);
       m.nst = (KB1 / SK) / (int)ks;
       m.nkb_last = SK;
     } else {
@@ -841,7 +852,11 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
         // The weights of this stage are already in flight; the activation
         // operand waits for its producer. On a timeout the copy is still issued
         // (of stale bytes) so the stage completes and nothing is left pending.
-        if (!wait_flag(&p.ready[m.group], 1u + p.dep_extra, status, deadline)) ok = false;
+        // fixed exponent: the group's terms are final once all its tiles are
+        // counted; else its last tile's fixup releases the ready flag
+        const bool got = p.ae_fixed ? wait_flag(&p.cnt1[m.group], (uint32_t)geo.NT + p.dep_extra, status, deadline)
+                                    : wait_flag(&p.ready[m.group], 1u + p.dep_extra, status, deadline);
+        if (!got) ok = false;
         fence_proxy_async_global();
         check = false;
         if (ok) seen_a = m.group;
@@ -1074,6 +1089,8 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
   int32_t* em = S.em[eg];
   int32_t* xe_s = S.xe[eg];
   float* tws = S.tws[eg];
+  uint32_t* fpend = S.fpend[eg];
+  for (int i = et; i < HT; i += 128) fpend[i] = 0;
   // The group whose down-item values (routing weights, common exponents, g2) this
   // warpgroup holds: consecutive down items of one group fetch them once.
   int dgrp = -1;
@@ -1098,8 +1115,12 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       if (et < gr.gsz) {
         const int pq = ps[gr.pair_off + et].pq;
         tws[et] = pq < p.P ? __ldg(&p.tw[pq]) : 1.f;
-        ok = wait_flag(&p.ready[mt.group], 1u + p.dep_extra, status, deadline);
-        em[et] = __ldcg(&p.emax[gr.pair_off + et]);
+        if (p.ae_fixed) {
+          em[et] = p.ae_val;           // every tile's exponent; the producer waited for the terms
+        } else {
+          ok = wait_flag(&p.ready[mt.group], 1u + p.dep_extra, status, deadline);
+          em[et] = __ldcg(&p.emax[gr.pair_off + et]);
+        }
       }
       dgrp = mt.group;                 // on a failed wait the loop ends below
     }
@@ -1115,10 +1136,10 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       // ---- gate/up tile: rows 0..63 gate, 64..127 up of columns [64 tile, 64 tile + 64)
       const bool up = m >= 64;
       const int c = m & 63;
-      const int ks = gr.shared ? S.hdr.kss : S.hdr.ks;
-      const size_t gi = gu_index(p, S.hdr, mt.group, mt.tile, gr.shared);   // the (group, tile) item
-      // its pieces' sums: routed items from 0, the shared expert's after MAXSPLIT
-      const size_t gp0 = gr.shared ? (size_t)MAXSPLIT + (gi - MAXSPLIT) * ks : gi * ks;
+      const int ks = mt.ks;
+      // a split item's counter, and its pieces' sums: routed items from 0, the shared expert's after MAXSPLIT
+      const size_t gi = (size_t)mt.gi;
+      const size_t gp0 = gi >= (size_t)MAXSPLIT ? (size_t)MAXSPLIT + (gi - MAXSPLIT) * ks : gi * ks;
       for (int q = 0; q < gr.gsz; ++q) {
         float v[16], v1[16];
         tc::ld16x2(tacc + XTERMS * q, tacc + TM_SLOT + XTERMS * q, v, v1);   // v1 holds data only if two
@@ -1151,7 +1172,18 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       const int col0 = mt.tile * 64;
       const int kbl = mt.tile % SK;                   // the tile is K block kbl of down stage tile / SK
       uint8_t* ab = p.ab + gr.ab_off + (size_t)(mt.tile / SK) * gr.sbs;
-      if (!up) {
+      if (p.ae_fixed) {
+        // SwiGLU, the 128 threads two per column (even and odd pairs); no maxima needed
+        const int cc = et & 63;
+        for (int q = et >> 6; q < gr.gsz; q += 2) {
+          float g = xg[q * 64 + cc], u = xu[q * 64 + cc];
+          if (p.has_limit) {
+            g = fminf(g, p.limit);
+            u = fminf(fmaxf(u, -p.limit), p.limit);
+          }
+          xg[q * 64 + cc] = (col0 + cc >= geo.W) ? 0.f : (g / (1.f + expf(-g))) * u;
+        }
+      } else if (!up) {
         // SwiGLU per pair, |act| maxima per half tile
         const int half = warp & 1;   // quarters 0, 1 <-> columns 0..31, 32..63
         for (int q = 0; q < gr.gsz; ++q) {
@@ -1163,7 +1195,6 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
           float a = (g / (1.f + expf(-g))) * u;
           if (col0 + c >= geo.W) a = 0.f;
           xg[q * 64 + c] = a;
-          if (p.ae_fixed) continue;          // the exponent is known: no maximum needed
           float mx = fabsf(a);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -1171,9 +1202,10 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
         }
       }
       asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
-      // 16 unscaled e2m1 terms per pair with the tile's own even exponent el:
-      // act = sum_t 2^(el - 2t) q_t (the digit rule of the x terms). Warp w of
-      // the group takes pairs w, w + 4; lane l the columns 2l, 2l + 1.
+      // 16 unscaled e2m1 terms per pair with the tile's exponent el (fixed, or
+      // the tile's own even one): act = sum_t 2^(el - 2t) q_t (the digit rule of
+      // the x terms). Warp w of the group takes pairs w, w + 4; lane l the
+      // columns 2l, 2l + 1.
       for (int q = et >> 5; q < gr.gsz; q += 4) {
         const int el = p.ae_fixed ? p.ae_val : act_exponent(fmaxf(amx[q][0], amx[q][1]));
         float r0 = xg[q * 64 + 2 * lane], r1 = xg[q * 64 + 2 * lane + 1];
@@ -1191,20 +1223,22 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
           atomicMax(&p.emax[gr.pair_off + q], el);
         }
       }
-      // The group's stores are ordered before thread 0's release (acq_rel) by the
-      // barrier; the group's last tile acquires them through the same counter.
+      // The group's stores are ordered before thread 0's release by the barrier.
       asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
+      if (p.ae_fixed) {
+        // Every tile is on the one exponent: count the tile (release, no reply
+        // awaited); the group's down items wait until every tile is counted.
+        if (et == 0) red_add_release_gpu(&p.cnt1[mt.group], 1u);
+        continue;
+      }
+      // Per-tile exponents: the group's last tile (found by the count, acq_rel)
+      // fixes the group's terms up to a common exponent and releases them.
       if (et == 0) {
         const uint32_t old = atom_add_acq_rel_gpu(&p.cnt1[mt.group], 1u);
         *last_flag = (old == (uint32_t)geo.NT - 1u) ? 1u : 0u;
       }
       asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
-      if (*last_flag && p.ae_fixed) {
-        // Last tile of the group, every tile on the one fixed exponent: the
-        // terms are final (the other tiles' stores were acquired through the
-        // count above); release them to the down items.
-        if (et == 0) st_release_gpu(&p.ready[mt.group], 1u);
-      } else if (*last_flag) {
+      if (*last_flag) {
         // Last tile of the group: bring every tile to the pair's common exponent
         // em by moving its terms d = (em - el) / 2 places down (term t becomes
         // term t + d; the last d terms, below the common precision, drop out).
@@ -1262,12 +1296,16 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.acc_empty[buf]);
-      // The group's y stores are ordered before thread 0's release by the barrier:
-      // the tile's counter counts the routed pairs whose y covers it.
-      asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
-      if (et == 0) red_add_release_gpu(&p.fcnt[mt.tile], (uint32_t)gr.gsz);
+      // Only the finalize reads the tiles' counters, after every item: count the
+      // pairs here and release them once per tile after the loop, so no item
+      // waits for its stores to be performed.
+      if (et == 0) fpend[mt.tile] += (uint32_t)gr.gsz;
     }
   }
+  // The group's y stores are ordered before thread 0's releases by the barrier:
+  // a tile's counter counts the routed pairs whose y covers it.
+  asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
+  if (et < HT && fpend[et]) red_add_release_gpu(&p.fcnt[et], fpend[et]);
   // This warp reads TMEM no more: TMEM may be released once all epilogue warps say so.
   tc::fence_before_sync();
   __syncwarp();

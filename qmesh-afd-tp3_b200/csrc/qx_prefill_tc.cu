@@ -424,16 +424,16 @@ __device__ __forceinline__ bool bar_and(int id, int n, bool pred) {
   return r != 0u;
 }
 
+// Bounded wait until a global counter reaches `need` (acquire); the deadline is
+// checked on the clock, the status word (another L2 round trip) every 64 polls.
 __device__ bool wait_count(const uint32_t* c, uint32_t need, volatile uint32_t* status, uint64_t deadline) {
   for (uint32_t it = 0;; ++it) {
     if (ld_acquire_gpu(c) >= need) return true;
-    if ((it & 7u) == 7u) {
-      if (*status & QX_DEV_TIMEOUT) return false;
-      if (globaltimer_ns() > deadline) {
-        atomicOr(const_cast<uint32_t*>(status), (uint32_t)QX_DEV_TIMEOUT);
-        return false;
-      }
+    if (globaltimer_ns() > deadline) {
+      atomicOr(const_cast<uint32_t*>(status), (uint32_t)QX_DEV_TIMEOUT);
+      return false;
     }
+    if ((it & 63u) == 63u && (*status & QX_DEV_TIMEOUT)) return false;
     __nanosleep(64);
   }
 }

@@ -51,17 +51,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait: true when the phase completed; false when the deadline passed
 // or another thread already raised `abort_bit` in *status (then the caller must
-// stop consuming). Never spins without limit.
+// stop consuming). Never spins without limit. The deadline is checked on the
+// clock; *status lives in global memory (an L2 round trip that the waiting
+// thread cannot overlap), so it is read only every 1024 failed tries, which a
+// wait reaches only when something has already gone wrong.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile uint32_t* status,
                                                   uint32_t abort_bit, uint64_t deadline_ns) {
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 15u) == 15u) {
-      if (*status & abort_bit) return false;
       if (globaltimer_ns() > deadline_ns) {
         atomicOr(const_cast<uint32_t*>(status), abort_bit);
         return false;
       }
+      if ((it & 1023u) == 1023u && (*status & abort_bit)) return false;
     }
   }
 }

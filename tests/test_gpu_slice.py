@@ -280,7 +280,8 @@ def test_config3_zipf_rows48_shard(cuda_ready, layout):
 @pytest.mark.parametrize("a0,a1", [(576, 1152), (1152, 1440), (0, 1152)])
 def test_config2_shards(cuda_ready, layout, a0, a1):
     """BASELINE config 2 column shards (4-, 8- and 2-way splits): the 576- and
-    288-column shards run their down items in claimed batches of 2 and 4."""
+    288-column shards split their last partial wave of gate/up items in K and
+    claim their down items in batches of 2 and 4."""
     ar, ids, tw, q, inv = _full_layer_case(cuda_ready, 2, 6, a0=a0, a1=a1, layout=layout)
     p, u = _check_full(ar, ids, tw, q, inv, a0, a1)
     print("config2 shard", (a0, a1), p, "unique experts", u)

@@ -22,10 +22,13 @@ def _al(v):
 
 def ws_offsets(rows, topk, width):
     """Byte offsets inside a qx_slice_decode_tc workspace (mirror of its layout)."""
-    p, nt = rows * topk, (width + 63) // 64
+    p = rows * topk
+    ps = p + rows                                  # routed pairs, then the shared expert's rows
+    maxsplit, maxsg, max_stiles = 512, (64 + 5) // 6, 64
     o, off = 0, {}
-    for name, size in [("ctl", 256), ("cnt1", p * 4), ("ready", p * 4), ("fcnt", 40 * 4), ("emax", p * 4),
-                       ("eloc", p * nt * 4),
+    for name, size in [("ctl", 256), ("cnt1", ps * 4), ("ready", ps * 4), ("fcnt", 40 * 4),
+                       ("pcnt", (maxsplit + maxsg * max_stiles) * 4), ("emax", ps * 4),
+                       ("eloc", ps * max_stiles * 4),
                        ("xexp", rows * 4), ("xt", rows * 10 * 4096)]:
         off[name] = o
         o = _al(o + size)
