@@ -709,7 +709,6 @@ struct Smem {       // fixed part of the dynamic shared memory, before the rings
   int32_t xe[NEPI][GMAX];     // gate/up item: the group's rows' x exponents
   float tws[NEPI][GMAX];      // down item: the group's routing weights
   uint32_t xcall[NEPI];       // fused combine: the call number of the unit in hand
-  uint32_t fpend[NEPI][HT];   // down items: routed pairs whose y this group wrote, per output tile, not yet released
   RouteHdr hdr;
 };
 
@@ -1089,8 +1088,6 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
   int32_t* em = S.em[eg];
   int32_t* xe_s = S.xe[eg];
   float* tws = S.tws[eg];
-  uint32_t* fpend = S.fpend[eg];
-  for (int i = et; i < HT; i += 128) fpend[i] = 0;
   // The group whose down-item values (routing weights, common exponents, g2) this
   // warpgroup holds: consecutive down items of one group fetch them once.
   int dgrp = -1;
@@ -1172,18 +1169,7 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       const int col0 = mt.tile * 64;
       const int kbl = mt.tile % SK;                   // the tile is K block kbl of down stage tile / SK
       uint8_t* ab = p.ab + gr.ab_off + (size_t)(mt.tile / SK) * gr.sbs;
-      if (p.ae_fixed) {
-        // SwiGLU, the 128 threads two per column (even and odd pairs); no maxima needed
-        const int cc = et & 63;
-        for (int q = et >> 6; q < gr.gsz; q += 2) {
-          float g = xg[q * 64 + cc], u = xu[q * 64 + cc];
-          if (p.has_limit) {
-            g = fminf(g, p.limit);
-            u = fminf(fmaxf(u, -p.limit), p.limit);
-          }
-          xg[q * 64 + cc] = (col0 + cc >= geo.W) ? 0.f : (g / (1.f + expf(-g))) * u;
-        }
-      } else if (!up) {
+      if (!up) {
         // SwiGLU per pair, |act| maxima per half tile
         const int half = warp & 1;   // quarters 0, 1 <-> columns 0..31, 32..63
         for (int q = 0; q < gr.gsz; ++q) {
@@ -1195,6 +1181,7 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
           float a = (g / (1.f + expf(-g))) * u;
           if (col0 + c >= geo.W) a = 0.f;
           xg[q * 64 + c] = a;
+          if (p.ae_fixed) continue;          // the exponent is known: no maximum needed
           float mx = fabsf(a);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -1296,16 +1283,12 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.acc_empty[buf]);
-      // Only the finalize reads the tiles' counters, after every item: count the
-      // pairs here and release them once per tile after the loop, so no item
-      // waits for its stores to be performed.
-      if (et == 0) fpend[mt.tile] += (uint32_t)gr.gsz;
+      // The group's y stores are ordered before thread 0's release by the barrier:
+      // the tile's counter counts the routed pairs whose y covers it.
+      asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
+      if (et == 0) red_add_release_gpu(&p.fcnt[mt.tile], (uint32_t)gr.gsz);
     }
   }
-  // The group's y stores are ordered before thread 0's releases by the barrier:
-  // a tile's counter counts the routed pairs whose y covers it.
-  asm volatile("bar.sync %0, 128;" ::"r"(B1) : "memory");
-  if (et < HT && fpend[et]) red_add_release_gpu(&p.fcnt[et], fpend[et]);
   // This warp reads TMEM no more: TMEM may be released once all epilogue warps say so.
   tc::fence_before_sync();
   __syncwarp();
