@@ -41,8 +41,9 @@ N_EXPERTS = 384
 TOPK = 6
 EXPERT_BYTES = 2 * INTER * (HIDDEN // 2 + HIDDEN // 16) + HIDDEN * (INTER // 2 + INTER // 16)  # 19,906,560
 # DRAM bytes (read + write) per unique expert per launch of tc_decode_kernel, from the ncu capture in
-# profiles/tc_decode_kernel_config1.md (544.03 MB over 27 unique experts, full 2304 columns).
-DRAM_BYTES_PER_UNIQUE = 544.03e6 / 27
+# profiles/tc_decode_kernel_config1.md (543.85 MB over 27 unique experts, full 2304 columns). A shard
+# streams whole 64-column tiles, so its traffic scales with its padded width.
+DRAM_BYTES_PER_UNIQUE = 543.85e6 / 27
 METRIC = "MoE-layer decode µs (6 rows) & NVFP4 weight GB/s vs HBM peak, 1/2/4/8 GPU"
 
 
@@ -524,8 +525,9 @@ def run_ours(args) -> dict | None:
                                           / (us_layer * 1e-6) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "peak_kind": peak_kind,
-                         "traffic": int(mean_u * DRAM_BYTES_PER_UNIQUE * width / INTER),
-                         "traffic_source": "ncu dram bytes per unique expert (small-arena capture) x mean unique experts",
+                         "traffic": int(mean_u * DRAM_BYTES_PER_UNIQUE * (64 * math.ceil(width / 64)) / INTER),
+                         "traffic_source": "ncu dram bytes per unique expert (small-arena capture) x mean unique "
+                                           "experts x padded shard width / 2304",
                          "kernel_us": round(k_mean, 3), "alg_bytes_per_launch": int(alg_bytes)},
             "e2e": {"value": round(us_e2e, 3), "unit": "us/layer", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},

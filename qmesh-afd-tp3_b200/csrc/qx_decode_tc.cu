@@ -145,10 +145,11 @@ struct RouteHdr {   // call-wide results of the routing, in shared memory
   int32_t pad[3];
 };
 
-struct PairS {      // per group position: pair index (row * topk + slot)
-  int32_t pq;
+struct PairS {      // per group position
+  int32_t pq;       // routed pair index (row * topk + slot), or P + row for the shared expert's
+  int32_t row;      // the pair's activation row
 };
-static_assert(sizeof(PairS) == 4, "shared pair record is 4 bytes");
+static_assert(sizeof(PairS) == 8, "shared pair record is 8 bytes");
 
 struct Params {
   const void* x;
@@ -272,9 +273,6 @@ __device__ __forceinline__ Geo geo_of(const Params& p, const GroupS& g) {
   return r;
 }
 
-// Row of a group position's pair code: routed pairs are row * topk + slot,
-// the shared expert's are P + row.
-__device__ __forceinline__ int row_of(const Params& p, int pq) { return pq < p.P ? pq / p.topk : pq - p.P; }
 
 
 // ------------------------------------------------------------------ prologue
@@ -514,6 +512,7 @@ __device__ void route_sort(const Params& p, const int (&idr)[IDR], GroupS* gs, P
     if (e[j] < 0) continue;
     const int i = K * lane + j;
     ps[i].pq = (int)(v[j] & 511u);
+    ps[i].row = div_small(ps[i].pq, p.topk);
     const int lo = div_small(gk[j] * c[j], ng[j]);
     if (r[j] == lo) {                          // the group's first pair writes its record
       const int gsz = div_small((gk[j] + 1) * c[j], ng[j]) - lo;
@@ -569,7 +568,10 @@ __device__ void route_finish(const Params& p, GroupS* gs, PairS* ps, RouteHdr* h
   int Gs = 0;
   if (p.sNT > 0) {
     Gs = (p.rows + gmax - 1) / gmax;
-    for (int r = lane; r < p.rows; r += 32) ps[Pv + r].pq = p.P + r;
+    for (int r = lane; r < p.rows; r += 32) {
+      ps[Pv + r].pq = p.P + r;
+      ps[Pv + r].row = r;
+    }
     const int abs_r = ((p.NT + SK - 1) / SK) * XT_STAGE, abs_s = ((p.sNT + SK - 1) / SK) * XT_STAGE;
     if (lane < Gs) {
       const int lo = div_small(lane * p.rows, Gs), hi = div_small((lane + 1) * p.rows, Gs);
@@ -727,6 +729,10 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
   const uint32_t n1 = (uint32_t)hdr.n1, n2 = (uint32_t)hdr.n2, n1s = (uint32_t)hdr.n1s, n2s = (uint32_t)hdr.n2s;
   const int G = hdr.n_groups;
   uint32_t sc = 0, mc = 0;
+  // ring position of stage sc, kept incrementally: slot = sc % ns, and the
+  // parity of the slot's previous use, ((sc / ns) - 1) & 1, for sc >= ns
+  int slot = 0;
+  uint32_t prev_phase = 1u;
   int seen_a = -1;                    // last group whose activation flag was seen set
   bool ok = true, prep_seen = false;  // prep_seen: the prep kernel's results are visible
   uint32_t item = blockIdx.x;         // the first item is static, the rest come from the queue
@@ -823,12 +829,21 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
       cl_end = next + k;
     }
     bool check = m.kind == 2 && seen_a != m.group;
-    for (int s = 0; s < m.nst; ++s, ++sc) {
-      const int slot = (int)(sc % (uint32_t)p.ns);
+    // gate/up: the pairs' x-term rows, the item's first stage (the per-stage
+    // loop below issues their copies with no table reads)
+    const uint8_t* xsrc[GMAX];
+#pragma unroll
+    for (int q = 0; q < GMAX; ++q)
+      xsrc[q] = m.kind == 1 && q < gr.gsz
+                    ? p.xt + ((size_t)ps[gr.pair_off + q].row * NXCH + m.piece * m.nst) * XT_STAGE
+                    : p.xt;
+    const int ns = p.ns;
+    // every exit of a stage (end, continue, break) advances sc and its slot together
+    for (int s = 0; s < m.nst; ++s, ++sc, (++slot == ns ? (slot = 0, prev_phase ^= 1u) : 0u)) {
       if (s >= pre) {
         // slot (weights + activation operand) free once stage sc - ns completed
         if (sc >= (uint32_t)p.ns &&
-            !mbar_wait_bounded(&S.empty[slot], ((sc / p.ns) - 1) & 1, status, QX_DEV_TIMEOUT, deadline)) {
+            !mbar_wait_bounded(&S.empty[slot], prev_phase, status, QX_DEV_TIMEOUT, deadline)) {
           ok = false;
           break;
         }
@@ -840,11 +855,10 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
       uint8_t* bdst = ring + p.b_off + (size_t)slot * p.bst;
       if (m.kind == 1) {
         // gate/up: each pair's row-major x-term block of this stage
-        for (int q = 0; q < gr.gsz; ++q) {
-          const int row = row_of(p, ps[gr.pair_off + q].pq);
-          bulk_g2s(bdst + q * XT_STAGE, p.xt + ((size_t)row * NXCH + m.piece * m.nst + s) * XT_STAGE,
-                   (uint32_t)XT_STAGE, &S.full[slot]);
-        }
+#pragma unroll
+        for (int q = 0; q < GMAX; ++q)
+          if (q < gr.gsz)
+            bulk_g2s(bdst + q * XT_STAGE, xsrc[q] + (size_t)s * XT_STAGE, (uint32_t)XT_STAGE, &S.full[slot]);
         continue;
       }
       if (check) {
@@ -862,7 +876,7 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
       }
       bulk_g2s(bdst, p.ab + gr.ab_off + (size_t)s * sbs, (uint32_t)sbs, &S.full[slot]);
       if (!ok) {
-        ++sc;
+        ++sc;   // this stage's copies are issued: drain_copies waits for them
         break;
       }
     }
@@ -875,6 +889,10 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
 __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS* gs, uint32_t tbase, int iss,
                            volatile uint32_t* status, uint64_t deadline) {
   uint32_t sc = 0, mc = 0, ic = 0;
+  // ring position of stage sc, kept incrementally: slot = sc % ns, phase = (sc / ns) & 1
+  int slot = 0;
+  uint32_t phase = 0;
+  const uint32_t ns = (uint32_t)p.ns;
   const uint32_t sfbase = tbase + TM_SF + (uint32_t)iss * TM_SLOT;
   for (;;) {
     const int mi = (int)(mc % NI);
@@ -892,11 +910,10 @@ __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS
     const uint32_t tacc = tbase + (uint32_t)buf * 2u * TM_SLOT + (uint32_t)iss * TM_SLOT;
     bool ok = true, first = true;
     for (int s = 0; s < m.nst; ++s, ++sc) {
-      const int slot = (int)(sc % (uint32_t)p.ns);
       // The stage's operands were written by the bulk copies (async proxy) the
       // barrier tracks; the MMAs read them through the same proxy, so the wait
       // alone orders them (no thread-sync fence, as for any TMA-fed stage).
-      if (!mbar_wait_bounded(&S.full[slot], (sc / p.ns) & 1, status, QX_DEV_TIMEOUT, deadline)) {
+      if (!mbar_wait_bounded(&S.full[slot], phase, status, QX_DEV_TIMEOUT, deadline)) {
         ok = false;
         break;
       }
@@ -914,6 +931,10 @@ __device__ void mma_issuer(const Params& p, uint8_t* ring, Smem& S, const GroupS
         first = false;
       }
       tc::commit(&S.empty[slot]);          // arrives when this issuer's work on the stage is done
+      if (++slot == (int)ns) {
+        slot = 0;
+        phase ^= 1u;
+      }
     }
     if (!ok) break;
     tc::commit(&S.acc_full[buf]);
@@ -1104,7 +1125,7 @@ __device__ void epilogue(const Params& p, Smem& S, float* xg, const GroupS* gs, 
     const Geo geo = geo_of(p, gr);
     bool ok = true;
     if (mt.kind == 1 && et < gr.gsz)   // the rows' x exponents, fetched while the MMAs run
-      xe_s[et] = __ldcg(&p.xexp[row_of(p, ps[gr.pair_off + et].pq)]);
+      xe_s[et] = __ldcg(&p.xexp[ps[gr.pair_off + et].row]);
     if (mt.kind == 2 && mt.group != dgrp) {
       // A new group's g2, routing weights (1 for the shared expert) and common
       // exponents, fetched while the MMAs run.
