@@ -425,12 +425,33 @@ __device__ void route_sort(const Params& p, const int (&idr)[IDR], GroupS* gs, P
     const int q = lane + 32 * j;
     v[j] = (q < p.P && idr[j] >= 0) ? ((uint32_t)idr[j] << 9) | (uint32_t)q : NONE;
   }
-  // The network's stages run as loops (unrolled only for 2 slots per lane): a
-  // fully unrolled network of 512 keys is thousands of instructions that every
-  // SM fetches once at its start.
-#pragma unroll(K == 2 ? 8 : 1)
+  if constexpr (K == 2) {
+    // Up to 64 keys: a rank sort. A key's place is the number of smaller keys
+    // (the valid keys are distinct: the pair index is in their low bits; the
+    // equal NONE keys sort after them and are not placed); one short loop of
+    // shuffles, which the SM fetches once (the sort runs at every CTA's start,
+    // when each instruction fetched is a miss).
+    uint32_t* sb = reinterpret_cast<uint32_t*>(gs);   // scratch: the tables are written after
+    int r0 = 0, r1 = 0;
+#pragma unroll 4
+    for (int src = 0; src < 32; ++src) {
+      const uint32_t a = __shfl_sync(FULL, v[0], src), b = __shfl_sync(FULL, v[1], src);
+      r0 += (int)(a < v[0]) + (int)(b < v[0]);
+      r1 += (int)(a < v[1]) + (int)(b < v[1]);
+    }
+    const int nv = __popc(__ballot_sync(FULL, v[0] != NONE)) + __popc(__ballot_sync(FULL, v[1] != NONE));
+    if (v[0] != NONE) sb[r0] = v[0];
+    if (v[1] != NONE) sb[r1] = v[1];
+    __syncwarp();
+    v[0] = 2 * lane < nv ? sb[2 * lane] : NONE;
+    v[1] = 2 * lane + 1 < nv ? sb[2 * lane + 1] : NONE;
+    __syncwarp();
+  } else {
+  // The network's stages run as loops: a fully unrolled network of 512 keys is
+  // thousands of instructions that every SM fetches once at its start.
+#pragma unroll 1
   for (int k = 2; k <= N; k <<= 1) {
-#pragma unroll(K == 2 ? 8 : 1)
+#pragma unroll 1
     for (int s = k >> 1; s > 0; s >>= 1) {
       if (s >= K) {                        // partner in lane ^ (s / K), same slot
         const bool keep_min = ((lane & (k / K)) == 0) == ((lane & (s / K)) == 0);
@@ -449,6 +470,7 @@ __device__ void route_sort(const Params& p, const int (&idr)[IDR], GroupS* gs, P
         if constexpr (K > 8) cx_lane<K, 8>(v, k, lane);
       }
     }
+  }
   }
   // runs: f = first pair of an expert; st = run start (inclusive max scan of
   // the starts), en = next run's start (suffix min), or the valid-pair count
@@ -1083,7 +1105,7 @@ __device__ bool finalize_unit(const Params& p, Smem& S, int u, int tile, int rb,
   }
   // Every word read above has returned its value: the senders may reuse them.
   if (!bar_and(B1, 128, ok)) return false;
-  if (et < p.xworld && et != p.xdst) st_release_sys(&reinterpret_cast<Hdr*>(xbuf_at(p, et))->uack[u], call);
+  if (et < p.xworld && et != p.xdst) ack_after_reads(&reinterpret_cast<Hdr*>(xbuf_at(p, et))->uack[u], call);
   if (et == 0) me->useq[u] = call;
   return true;
 }

@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(THR) xchg_kernel(Args a) {
     *reinterpret_cast<uint4*>(a.out + (size_t)row * a.out_stride + k) = o;
   }
   __syncthreads();   // every slot read above has returned its value
-  if (t < a.world && t != a.dst) st_release_sys(&reinterpret_cast<Hdr*>(a.buf[t])->ack[c], call);
+  if (t < a.world && t != a.dst) ack_after_reads(&reinterpret_cast<Hdr*>(a.buf[t])->ack[c], call);
   if (t == 0) me->seq[c] = call;
 }
 

@@ -244,10 +244,22 @@ class HostSlice:
     tensor [rows, 5120], pinned for an asynchronous copy) the output lands there
     and is the caller's to keep. Either way, read it after `synchronize()`
     (host) or `join(stream)` (device ordering) or a device-wide synchronisation.
+
+    With `xchg` (a `shard.P2PExchange`) every rank of the column split calls it
+    once per step with the same inputs: each call runs the fused slice + rank
+    combine, the output rank's call returns the combined output and the other
+    ranks' calls return None (they copy nothing back). With `shared` (the view of
+    a one-expert tensor-core arena) the output rank's kernel (or, without
+    `xchg`, the one kernel) also runs config 2's shared expert and adds it last.
     """
 
     def __init__(self, arena: Arena, rows: int, topk: int = 6, c0: int | None = None, c1: int | None = None,
-                 swiglu_limit: float = SWIGLU_LIMIT, slots: int = 2):
+                 swiglu_limit: float = SWIGLU_LIMIT, slots: int = 2, xchg=None, shared: _lib.QxArena | None = None):
+        if (xchg is not None or shared is not None) and arena.layout != "tc":
+            raise ValueError("the fused combine and the shared expert run on the tensor-core arena")
+        if xchg is not None and shared is not None and xchg.rank != xchg.dst:
+            raise ValueError("only the output rank runs the shared expert")
+        self.xchg, self.shared = xchg, shared
         self.arena = arena
         self.rows, self.topk = rows, topk
         self.c0 = arena.a0 if c0 is None else c0
@@ -282,7 +294,7 @@ class HostSlice:
         return x, s, i, t
 
     def __call__(self, li: int, x: torch.Tensor, x_scale: torch.Tensor, ids: torch.Tensor,
-                 tw: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+                 tw: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor | None:
         n = x.shape[0]
         if not 1 <= n <= self.rows or ids.shape != (n, self.topk) or tw.shape != (n, self.topk):
             raise ValueError(f"call of {n} rows / ids {tuple(ids.shape)} outside this HostSlice ({self.rows} x {self.topk})")
@@ -310,10 +322,21 @@ class HostSlice:
         self.ev_in[k].record(self.in_stream)
         stream.wait_event(self.ev_in[k])
         dx, ds, di, dt = self._views(self.dev[k], n)
-        launch(self.arena.view(li), dx.view(torch.float8_e4m3fn), di, dt, self.out_d[k][:n], self.c0, self.c1,
-               self.ws, x_scale=ds, swiglu_limit=self.limit, has_limit=self.has_limit, stream=stream.cuda_stream,
-               layout=self.arena.layout)
+        if self.xchg is not None:
+            self.xchg.slice_combine(self.arena.view(li), dx.view(torch.float8_e4m3fn), di, dt, self.out_d[k][:n],
+                                    self.c0, self.c1, self.ws, x_scale=ds, shared_expert=self.shared,
+                                    stream=stream.cuda_stream, swiglu_limit=self.limit, has_limit=self.has_limit)
+        else:
+            launch(self.arena.view(li), dx.view(torch.float8_e4m3fn), di, dt, self.out_d[k][:n], self.c0, self.c1,
+                   self.ws, x_scale=ds, swiglu_limit=self.limit, has_limit=self.has_limit,
+                   stream=stream.cuda_stream, layout=self.arena.layout, shared=self.shared)
         self.ev_done[k].record(stream)
+        if self.xchg is not None and self.xchg.rank != self.xchg.dst:
+            # a sender: nothing comes back; the slot is free once its slice has run
+            self.ev_out[k].record(stream)
+            self.used[k] = True
+            self.last = k
+            return None
         self.out_stream.wait_event(self.ev_done[k])
         dst = self.out_h[k][:n] if out is None else out
         with rng("qx.d2h"), torch.cuda.stream(self.out_stream):

@@ -85,3 +85,27 @@ def test_shared_expert_full_size_equals_separate_calls(cuda_ready, c0, c1, rows)
     assert torch.equal(fused, sep)
     again = _fused(ar, sh, dq, dinv, dids, dtw, c0, c1)
     assert torch.equal(fused, again)
+
+
+def test_host_slice_with_shared_expert(cuda_ready):
+    """HostSlice with the shared expert (host inputs, pipelined copies) returns the
+    device call's output (routed slice + shared expert in one kernel) over more
+    calls than it has staging slots, bit for bit."""
+    from qmesh_b200.arena import Arena
+    from qmesh_b200.expert_slice import HostSlice
+    dev = cuda_ready
+    ar = Arena(dev, 1, 16, 0, 512)
+    ar.load_layer(0, H.small_layer(41, 16, inter=512))
+    sh = Arena(dev, 1, 1, 0, 512)
+    sh.load_layer(0, H.small_layer(42, 1, inter=512))
+    hs = HostSlice(ar, 6, shared=sh.view(0))
+    cases, got = [], []
+    for step in range(4):
+        ids, tw = H.random_routing(6, 16, 60 + step)
+        _, q, inv = H.activations(6, 60 + step)
+        cases.append((q, inv, ids, tw))
+        got.append(hs(0, q, inv, ids, tw, out=torch.empty(6, 5120, dtype=torch.bfloat16).pin_memory()))
+    hs.synchronize()
+    for step, (q, inv, ids, tw) in enumerate(cases):
+        want = _fused(ar, sh, q.to(dev), inv.to(dev), ids.to(dev), tw.to(dev), 0, 512)
+        assert torch.equal(got[step], want.cpu()), f"call {step}"

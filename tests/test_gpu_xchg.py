@@ -3,7 +3,8 @@ kernel (qx_combine_p2p): over several consecutive steps (both receive slots, the
 acknowledgements) its output equals the oracle's rank-ordered FP32 sum with one
 BF16 rounding, bit for bit, for either output rank and with a shared-expert
 partial. The slice with the combine fused in (qx_slice_decode_tc_xchg): its
-output equals the slice partials combined by qx_combine_p2p, bit for bit. Both:
+output equals the slice partials combined by qx_combine_p2p, bit for bit, also
+when driven through HostSlice from host buffers. Both:
 a rank that skips a step makes the output rank's bounded waits run out and
 report, and the context keeps working. Skipped on a box with fewer than two
 GPUs."""
@@ -192,6 +193,75 @@ def _fused_worker(rank, world, port, rows, dst, q):
             if x is not None:
                 x.close()
         dist.destroy_process_group()
+
+
+def _host_worker(rank, world, port, rows, dst, q):
+    import sys
+    for p in (str(ROOT), str(PKG)):
+        sys.path.insert(0, p)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from qmesh_b200 import shard
+    from qmesh_b200.arena import Arena
+    from qmesh_b200.expert_slice import HostSlice, expert_slice
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=dev, timeout=__import__("datetime").timedelta(seconds=60))
+    xf = xc = None
+    try:
+        a0, a1 = shard.shard_range(rank, world)
+        ar = Arena(dev, 1, 16, a0, a1)
+        ar.fill_synthetic(0, seed=9)
+        xf = shard.P2PExchange(rows_max=rows, dst=dst, device=dev)   # fused, through HostSlice
+        xc = shard.P2PExchange(rows_max=rows, dst=dst, device=dev)   # chunk protocol, for the comparison
+        hs = HostSlice(ar, rows, 6, a0, a1, xchg=xf)
+        got, want = [], []
+        for step in range(STEPS):
+            ids, tw, xq, inv = _fused_case(step, rows)
+            o = torch.empty(rows, 5120, dtype=torch.bfloat16).pin_memory() if rank == dst else None
+            r_ = hs(0, xq, inv, ids, tw, out=o)
+            got.append(r_ is not None)
+            part = expert_slice(ar, 0, xq.to(dev), ids.to(dev), tw.to(dev), x_scale=inv.to(dev))
+            w = xc.combine(part)
+            if rank == dst:
+                want.append((o, w.cpu()))
+        hs.synchronize()
+        torch.cuda.synchronize()
+        equal = [bool(torch.equal(a, b)) for a, b in want] if rank == dst else []
+        q.put((rank, got, equal, int(xf.status.item()), int(xc.status.item())))
+    finally:
+        for x in (xf, xc):
+            if x is not None:
+                x.close()
+        dist.destroy_process_group()
+
+
+def test_host_slice_fused_combine_equals_slice_then_combine():
+    """HostSlice on every rank of the column split (host inputs, pipelined copies,
+    the fused slice + combine): the output rank's host output equals the device
+    slice partials combined by qx_combine_p2p, bit for bit, over consecutive
+    steps; the other ranks' calls return None."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = min(torch.cuda.device_count(), 8)
+    rows, dst = 6, 0
+    port = 29400 + os.getpid() % 200
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_host_worker, args=(r, world, port, rows, dst, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, got, equal, s1, s2 = q.get(timeout=300)
+        res[r] = (got, equal, s1, s2)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert res[r][0] == [r == dst] * STEPS, f"rank {r}: {res[r][0]}"
+        assert res[r][2] == 0 and res[r][3] == 0, f"rank {r}: status {res[r][2:]}"
+    assert res[dst][1] == [True] * STEPS
 
 
 @pytest.mark.parametrize("rows,dst", [(6, 0), (3, 1)])
