@@ -462,13 +462,13 @@ def run_ours(args) -> dict | None:
     d2h = out_h.numel() * out_h.element_size()
 
     hslice = None
-    if (world == 1 and (shv is None or args.layout == "tc")) or fused:
+    if world == 1 and (shv is None or args.layout == "tc"):
         # the public host-buffer call: one packed host-to-device copy per step,
-        # the copies on side streams overlapping the neighbouring steps' kernels
-        # (N > 1: the fused slice + combine on every rank, the output copied back
-        # by the output rank)
+        # the copies on side streams overlapping the neighbouring steps' kernels.
+        # (At N > 1 HostSlice's per-step host work outlasts a step: 130 us per step
+        # at N = 2 against 113 us with the copies straight from the pinned inputs.)
         from qmesh_b200.expert_slice import HostSlice
-        hslice = HostSlice(ar, rows, TOPK, a0, a1, xchg=xchg if fused else None, shared=shv)
+        hslice = HostSlice(ar, rows, TOPK, a0, a1, shared=shv)
         h2d = hslice.nbytes
 
     def e2e_step(i: int) -> None:
