@@ -662,7 +662,7 @@ def run_prefill(args) -> dict | None:
     from qmesh_b200.arena import Arena
     from qmesh_b200.combine import combine_ordered
     from qmesh_b200.expert_slice import alloc_prefill_workspace, launch_prefill
-    from qmesh_b200.shard import combine_across_ranks, shard_range
+    from qmesh_b200.shard import combine_across_ranks, combine_rows_across_ranks, row_bounds, shard_range
     from qmesh_b200.synth import make_activation, routing
     build.build()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -674,6 +674,10 @@ def run_prefill(args) -> dict | None:
         dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
     T, E = args.tokens, args.experts
     a0, a1 = shard_range(rank, world)
+    if args.columns:
+        if world > 1:
+            raise SystemExit("--columns times one rank's shard on one GPU (N = 1)")
+        a0, a1 = (int(v) for v in args.columns.split(":"))
     width = a1 - a0
     ar = Arena(dev, 1, E, a0, a1, layout="tc")
     ar.fill_synthetic(0, 4)
@@ -685,14 +689,18 @@ def run_prefill(args) -> dict | None:
     ws = alloc_prefill_workspace(T, TOPK, a0, a1, E, dev)
     part = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device=dev)
     out = torch.empty_like(part)
-    gathered = [torch.empty_like(part) for _ in range(world)] if world > 1 else None
     view = ar.view(0)
     stream = torch.cuda.current_stream(dev)
+    # N > 1: the row-split combine (an all-to-all of row blocks, each rank sums its
+    # block of every partial in rank order, the output rank collects the blocks)
+    n_me = (row_bounds(T, world)[rank + 1] - row_bounds(T, world)[rank]) if world > 1 else 0
+    recv = torch.empty(world * n_me, HIDDEN, dtype=torch.bfloat16, device=dev) if world > 1 else None
+    mine = torch.empty(n_me, HIDDEN, dtype=torch.bfloat16, device=dev) if world > 1 else None
 
     def step(x, xs, i_, t_) -> None:
         launch_prefill(view, x, i_, t_, a2, part, a0, a1, ws, x_scale=xs, stream=stream.cuda_stream)
         if world > 1:
-            combine_across_ranks(part, dst=0, out=out, combine=combine_ordered, gathered=gathered)
+            combine_rows_across_ranks(part, dst=0, out=out, combine=combine_ordered, recv=recv, mine=mine)
 
     for _ in range(args.warmup):
         step(dq, dinv, dids, dtw)
@@ -713,6 +721,36 @@ def run_prefill(args) -> dict | None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     us = ms * 1e3 / args.steps
+    parity = None
+    if world > 1:
+        # the timed path's output against the gather combine of the same partials, bit for bit
+        torch.cuda.synchronize()
+        timed = out.clone()
+        launch_prefill(view, dq, dids, dtw, a2, part, a0, a1, ws, x_scale=dinv, stream=stream.cuda_stream)
+        want = combine_across_ranks(part, dst=0, combine=combine_ordered)
+        torch.cuda.synchronize()
+        ok = bool(torch.equal(timed, want)) if rank == 0 else True
+        flag = torch.tensor([1 if ok else 0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        parity = {"checked": True, "bit_exact": bool(flag.item()),
+                  "what": "the row-split combine's output vs the gather combine (qx_combine_ordered of the "
+                          "NCCL-gathered partials) of the same step"}
+        if not flag.item():
+            raise SystemExit(f"prefill parity failed: {parity}")
+    # the slice alone, calls back to back behind a stream spin (per rank at N > 1)
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(2e6 + 1.2e5 * args.steps))
+    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ka.record(stream)
+    for _ in range(args.steps):
+        launch_prefill(view, dq, dids, dtw, a2, part, a0, a1, ws, x_scale=dinv, stream=stream.cuda_stream)
+    kb.record(stream)
+    torch.cuda.synchronize()
+    k_us = ka.elapsed_time(kb) * 1e3 / args.steps
+    rank_step_us = rank_kernel_us = None
+    if world > 1:
+        rank_step_us = [round(v, 1) for v in gather_floats(ms * 1e3 / args.steps, world, dev)]
+        rank_kernel_us = [round(v, 1) for v in gather_floats(k_us, world, dev)]
     # end to end: H2D of the chunk's inputs from pinned memory, D2H of the output
     host = [t_.pin_memory() for t_ in (q, inv, ids, tw)]
     dev_in = [torch.empty_like(t_, device=dev) for t_ in host]
@@ -746,6 +784,7 @@ def run_prefill(args) -> dict | None:
     uniq = len(set(ids.flatten().tolist()))
     alg_bytes = uniq * EXPERT_BYTES * width / INTER + T * HIDDEN + T * HIDDEN * 2
     n_pairs = T * TOPK
+    ka_gbs = alg_bytes / (k_us * 1e-6) / 1e9
     flops = 2.0 * n_pairs * (2 * width * HIDDEN + HIDDEN * width)
     peak, peak_kind = peaks()
     res = None
@@ -756,18 +795,24 @@ def run_prefill(args) -> dict | None:
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
             "dtype": "nvfp4-w/nvfp4-x (W4A4)/fp32-acc",
             "data": "synthetic (seeded NVFP4 weights from N(0,0.02); FP8 activations from N(0,1))",
-            "config": {"workload": "config4-prefill", "experts": E, "hidden": HIDDEN, "intermediate": INTER,
+            "config": {"workload": "config4-prefill" + ("-columns-%d-%d-on-one-gpu" % (a0, a1) if args.columns else ""),
+                       "experts": E, "hidden": HIDDEN, "intermediate": INTER,
                        "tokens": T, "topk": TOPK, "columns_per_rank": width, "unique_experts": uniq,
                        "a2": PREFILL_A2, "l2": f"inputs larger than L2: {alg_bytes / 1e9:.2f} GB of expert weights per step",
                        "parallelism": f"column-split tp{world}",
+                       "exchange": None if world == 1 else "row-split combine: NCCL all-to-all of row blocks, "
+                                   "per-rank ordered FP32 sums (qx_combine_ordered), blocks sent to rank 0",
                        "kernel": "grouped tcgen05 mxf4nvf4 (NVFP4 x NVFP4, TMEM accumulators)"},
             "tokens_per_s": round(T / (us * 1e-6), 1),
             "weight_gbs": round(alg_bytes / (us * 1e-6) / 1e9, 1),
-            "tensor_tflops": round(flops / (us * 1e-6) / 1e12, 2),
-            "roofline": {"bound": "hbm", "achieved": round(alg_bytes / (us * 1e-6) / 1e9, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(alg_bytes / (us * 1e-6) / 1e9 / peak, 4),
-                         "peak_kind": peak_kind, "traffic": None, "kernel_us": round(us, 1),
+            "tensor_tflops": round(flops / (k_us * 1e-6) / 1e12, 2),
+            "roofline": {"bound": "hbm", "achieved": round(ka_gbs, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(ka_gbs / peak, 4),
+                         "peak_kind": peak_kind, "traffic": None, "kernel_us": round(k_us, 1),
+                         "kernel_note": "the slice's six kernels per call, calls back to back",
                          "alg_bytes_per_launch": int(alg_bytes), "flops_per_launch": int(flops)},
+            "parity": parity,
+            "ranks": None if world == 1 else {"step_us": rank_step_us, "slice_kernel_us": rank_kernel_us},
             "e2e": {"value": round(us_e2e, 1), "unit": "us/layer", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps * 6 + (args.steps if world > 1 else 0),

@@ -381,26 +381,43 @@ __global__ void __launch_bounds__(256) pf_place_kernel(Params p) {
 // (K half) 128 + (r % 8) 16, scales in the stage's K-block atoms at
 // npad 256 + kb 512 + (r % 32) 16 + (r / 32) 4 + j.
 __global__ void __launch_bounds__(XQ_THR) pf_xquant_kernel(Params p) {
+  // Where the row's routed pairs go: one lane per pair looks it up (id, place,
+  // group) while the other threads load and quantise, so the chain of dependent
+  // loads is walked once per row, for all pairs at once, not per pair by every thread.
+  __shared__ int64_t dst_off[QX_MAX_TOPK];   // the pair's operand block of stage 0, or -1
+  __shared__ int32_t dst_sbs[QX_MAX_TOPK], dst_r[QX_MAX_TOPK], dst_npad[QX_MAX_TOPK];
   const int t = blockIdx.x;
+  const int b = threadIdx.x;                     // 16-element block
+  if (b < p.topk) {
+    const int q = t * p.topk + b;
+    const long long id = id_of(p, q);
+    int64_t off = -1;
+    if (id >= 0 && id < p.E) {
+      const int pos = p.pos_of[q];
+      const Group& g = p.groups[p.grp_of_pos[pos]];
+      off = g.xq_off;
+      dst_sbs[b] = g.sbs;
+      dst_r[b] = pos - g.pos_off;
+      dst_npad[b] = g.npad;
+    }
+    dst_off[b] = off;
+  }
   const float inv = row_inv(p, t);
   const uint8_t* xr = reinterpret_cast<const uint8_t*>(p.x) + (size_t)t * p.x_stride;
-  const int b = threadIdx.x;                     // 16-element block
   float v[16];
   ingest16(p, xr, b * 16, inv, v);
   uint32_t w[2];
   const uint32_t sb = quant16(v, p.ctl->a1g, w);
   const int s = b >> 5, kb = (b >> 2) & (SK - 1), j = b & 3;
+  __syncthreads();
   for (int k = 0; k < p.topk; ++k) {
-    const int q = t * p.topk + k;
-    const long long id = id_of(p, q);
-    if (id < 0 || id >= p.E) continue;
-    const int pos = p.pos_of[q];
-    const Group& g = p.groups[p.grp_of_pos[pos]];
-    const int r = pos - g.pos_off;
-    uint8_t* st = p.xq + g.xq_off + (size_t)s * g.sbs;
+    const int64_t off = dst_off[k];
+    if (off < 0) continue;
+    const int r = dst_r[k];
+    uint8_t* st = p.xq + off + (size_t)s * dst_sbs[k];
     *reinterpret_cast<uint2*>(st + (r >> 3) * 2048 + kb * 256 + (j >> 1) * 128 + (r & 7) * 16 + (j & 1) * 8) =
         make_uint2(w[0], w[1]);
-    st[g.npad * 256 + kb * 512 + (r & 31) * 16 + (r >> 5) * 4 + j] = (uint8_t)sb;
+    st[dst_npad[k] * 256 + kb * 512 + (r & 31) * 16 + (r >> 5) * 4 + j] = (uint8_t)sb;
   }
 }
 

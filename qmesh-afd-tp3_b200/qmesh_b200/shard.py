@@ -58,6 +58,59 @@ def combine_across_ranks(part: torch.Tensor, group=None, dst: int = 0, shared: t
     return combine(parts, out=out)
 
 
+def row_bounds(rows: int, world: int) -> list[int]:
+    """Row block boundaries of the row-split combine: rank k sums rows [b[k], b[k+1])."""
+    return [k * rows // world for k in range(world + 1)]
+
+
+def combine_rows_across_ranks(part: torch.Tensor, group=None, dst: int = 0, out: torch.Tensor | None = None,
+                              combine: Callable[..., torch.Tensor] | None = None,
+                              recv: torch.Tensor | None = None, mine: torch.Tensor | None = None
+                              ) -> torch.Tensor | None:
+    """The rank-ordered FP32 combine of `combine_across_ranks`, split by rows.
+
+    For partials of many rows (a prefill chunk): an all-to-all hands rank k rows
+    [b[k], b[k+1]) of every rank's partial (`row_bounds`), rank k sums them in
+    rank order with one BF16 rounding, and the output rank `dst` collects the
+    combined row blocks (point-to-point). Every element is the same sum in the
+    same order as in `combine_across_ranks`, so the bytes are identical; each
+    rank moves (N-1)/N of one partial and the output rank receives (N-1)/N of
+    one output, where the gather brings N-1 whole partials to one rank. Needs
+    at least one row per rank. `recv` ([N x rows of this rank's block, 5120])
+    and `mine` ([rows of this rank's block, 5120]) may be passed in to avoid
+    allocating per call. Only `dst` returns the output.
+    """
+    if combine is None:
+        from .combine import combine_ordered as combine
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    rows, hid = part.shape
+    if rows < world:
+        raise ValueError(f"{rows} rows cannot give each of {world} ranks a row block")
+    b = row_bounds(rows, world)
+    n_me = b[rank + 1] - b[rank]
+    if recv is None:
+        recv = torch.empty(world * n_me, hid, dtype=part.dtype, device=part.device)
+    dist.all_to_all_single(recv, part.contiguous(), output_split_sizes=[n_me] * world,
+                           input_split_sizes=[b[k + 1] - b[k] for k in range(world)], group=group)
+    parts = [recv[j * n_me:(j + 1) * n_me] for j in range(world)]
+    if rank == dst:
+        if out is None:
+            out = torch.empty(rows, hid, dtype=part.dtype, device=part.device)
+        target = out[b[rank]:b[rank + 1]]
+    else:
+        target = mine if mine is not None else torch.empty(n_me, hid, dtype=part.dtype, device=part.device)
+    res = combine(parts, out=target)
+    if res is not None and res.data_ptr() != target.data_ptr():
+        target.copy_(res)
+    if rank == dst:
+        ops = [dist.P2POp(dist.irecv, out[b[k]:b[k + 1]], k, group) for k in range(world) if k != dst]
+    else:
+        ops = [dist.P2POp(dist.isend, target, dst, group)]
+    for w in dist.batch_isend_irecv(ops):
+        w.wait()
+    return out if rank == dst else None
+
+
 class P2PExchange:
     """One-shot rank-ordered combine over NVLink peer memory (`qx_combine_p2p`,
     or fused into the slice kernel by `slice_combine`).

@@ -68,6 +68,58 @@ def test_column_split_two_ranks():
     assert torch.equal(torch.from_numpy(res[0][1]), want)
 
 
+def _rows_worker(rank, world, port, rows, q):
+    import sys
+    for p in (str(ROOT), str(PKG)):
+        sys.path.insert(0, p)
+    from oracle import moe
+    from qmesh_b200 import shard
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(300 + rank)
+        part = (torch.randn(rows, 5120, generator=g) * (rank + 1)).to(torch.bfloat16)
+
+        def cpu_combine(parts, out=None):
+            r = moe.combine_ordered([p.float() for p in parts]).to(torch.bfloat16)
+            if out is not None:
+                out.copy_(r)
+                return out
+            return r
+
+        by_rows = shard.combine_rows_across_ranks(part, dst=world - 1, combine=cpu_combine)
+        by_gather = shard.combine_across_ranks(part, dst=world - 1, combine=cpu_combine)
+        q.put((rank, None if by_rows is None else by_rows.float().numpy(),
+               None if by_gather is None else by_gather.float().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,rows", [(2, 7), (3, 10)])
+def test_row_split_combine_equals_gather_combine(world, rows):
+    """The row-split combine (all-to-all of row blocks, per-rank ordered sums, the
+    blocks collected on the output rank) gives the gather combine's bytes, with
+    row counts that do not divide by the rank count."""
+    port = 29100 + os.getpid() % 700 + world
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rows_worker, args=(r, world, port, rows, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, a, b = q.get(timeout=120)
+        res[r] = (a, b)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(world - 1):
+        assert res[r] == (None, None)
+    a, b = res[world - 1]
+    assert a is not None and (a == b).all()
+
+
 def test_shard_range_rules():
     from qmesh_b200 import shard
     assert [shard.shard_range(r, 8) for r in range(8)][-1] == (2016, 2304)
