@@ -841,14 +841,15 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
       fence_proxy_async_global();
       prep_seen = true;
     }
-    uint32_t next;                      // the following item, claimed ahead
+    // The following item: the next of the batch in hand, or claimed from the
+    // queue now. The queue's answer is first used after this item's copies are
+    // issued, so its round trip overlaps them.
+    uint32_t next = 0, claim_k = 0, claimed = 0;
     if (cl_next < cl_end) {
       next = cl_next++;
     } else {
-      const uint32_t k = item >= n1 + n2s ? dclaim : 1u;
-      next = gridDim.x + atomicAdd(&p.ctl->work, k);
-      cl_next = next + 1;
-      cl_end = next + k;
+      claim_k = item >= n1 + n2s ? dclaim : 1u;
+      claimed = atomicAdd(&p.ctl->work, claim_k);
     }
     bool check = m.kind == 2 && seen_a != m.group;
     // gate/up: the pairs' x-term rows, the item's first stage (the per-stage
@@ -901,6 +902,11 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
         ++sc;   // this stage's copies are issued: drain_copies waits for them
         break;
       }
+    }
+    if (claim_k) {
+      next = gridDim.x + claimed;
+      cl_next = next + 1;
+      cl_end = next + claim_k;
     }
     item = next;
   }
