@@ -379,27 +379,31 @@ def run_ours(args) -> dict | None:
             launch(shv, q, sh_ids, sh_tw, sh_out, 0, INTER, ws_s, x_scale=inv, stream=st)
             return sh_out
 
-    def exchange(p: torch.Tensor, shared: torch.Tensor | None = None) -> torch.Tensor | None:
+    def exchange(p: torch.Tensor, shared: torch.Tensor | None = None, o: torch.Tensor | None = None):
+        o = out if o is None else o
         if xchg is not None:
-            return xchg.combine(p, out=out, shared=shared)
-        return combine_across_ranks(p, dst=0, out=out, combine=combine_ordered, gathered=gathered, shared=shared)
+            return xchg.combine(p, out=o, shared=shared)
+        return combine_across_ranks(p, dst=0, out=o, combine=combine_ordered, gathered=gathered, shared=shared)
     out = torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev)
     views = [ar.view(li) for li in range(layers)]
     stream = torch.cuda.current_stream(dev)
 
-    def slice_step(view, q, inv, ids, tw, st) -> None:
+    def slice_step(view, q, inv, ids, tw, st, dst: torch.Tensor | None = None) -> None:
         """One step through the public calls: N = 1 the slice (with the shared
         expert in the same kernel when configured); N > 1 the fused slice +
         combine (the output rank runs the shared expert in its kernel), or the
-        slice, a separate shared-expert call on the output rank and the combine."""
+        slice, a separate shared-expert call on the output rank and the combine.
+        The result goes to `dst` when given (else `part` at N = 1, `out` at N > 1)."""
         if fused:
-            xchg.slice_combine(view, q, ids, tw, out, a0, a1, ws, x_scale=inv, stream=st, shared_expert=shv)
+            xchg.slice_combine(view, q, ids, tw, out if dst is None else dst, a0, a1, ws, x_scale=inv, stream=st,
+                               shared_expert=shv)
             return
         if world == 1:
-            launch(view, q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=st, layout=args.layout, shared=shv)
+            launch(view, q, ids, tw, part if dst is None else dst, a0, a1, ws, x_scale=inv, stream=st,
+                   layout=args.layout, shared=shv)
             return
         launch(view, q, ids, tw, part, a0, a1, ws, x_scale=inv, stream=st, layout=args.layout)
-        exchange(part, sh_call(q, inv, st) if sh_call is not None else None)
+        exchange(part, sh_call(q, inv, st) if sh_call is not None else None, dst)
 
     def step(i: int) -> None:
         q, inv, ids, tw = dq[i % len(dq)]
@@ -456,7 +460,6 @@ def run_ours(args) -> dict | None:
     # ---- end to end through the public call with host buffers ----
     from qmesh_b200.expert_slice import expert_slice
     host = [(q.pin_memory(), inv.pin_memory(), ids.pin_memory(), tw.pin_memory()) for q, inv, ids, tw in draws]
-    dev_in = [torch.empty_like(t, device=dev) for t in host[0]]
     out_h = torch.empty(rows, HIDDEN, dtype=torch.bfloat16).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in host[0])
     d2h = out_h.numel() * out_h.element_size()
@@ -471,16 +474,42 @@ def run_ours(args) -> dict | None:
         hslice = HostSlice(ar, rows, TOPK, a0, a1, shared=shv)
         h2d = hslice.nbytes
 
+    # Without HostSlice: two slots of device inputs and outputs; step i's input
+    # copies run on a copy stream while step i - 1 computes, and its output copy
+    # (output rank) on a third stream while step i + 1 computes.
+    slot_in = [[torch.empty_like(t, device=dev) for t in host[0]] for _ in range(2)]
+    slot_out = [torch.empty(rows, HIDDEN, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    slot_host = [torch.empty(rows, HIDDEN, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    cp_stream, d2h_stream = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    slot_used = [False, False]
+
     def e2e_step(i: int) -> None:
         src = host[i % len(host)]
         if hslice is not None:
             hslice(i % layers, src[0], src[1], src[2], src[3])
             return
-        for d, s in zip(dev_in, src):
-            d.copy_(s, non_blocking=True)
-        slice_step(views[i % layers], dev_in[0], dev_in[1], dev_in[2], dev_in[3], stream.cuda_stream)
+        k = i % 2
+        if slot_used[k]:
+            cp_stream.wait_event(ev_done[k])          # the slot's previous slice has read its inputs
+        with torch.cuda.stream(cp_stream):
+            for d, s in zip(slot_in[k], src):
+                d.copy_(s, non_blocking=True)
+        ev_in[k].record(cp_stream)
+        stream.wait_event(ev_in[k])
+        if slot_used[k] and rank == 0:
+            stream.wait_event(ev_out[k])              # the slot's previous output has been copied out
+        slice_step(views[i % layers], slot_in[k][0], slot_in[k][1], slot_in[k][2], slot_in[k][3],
+                   stream.cuda_stream, dst=slot_out[k])
+        ev_done[k].record(stream)
         if rank == 0:
-            out_h.copy_(out if world > 1 else part, non_blocking=True)
+            d2h_stream.wait_event(ev_done[k])
+            with torch.cuda.stream(d2h_stream):
+                slot_host[k].copy_(slot_out[k], non_blocking=True)
+            ev_out[k].record(d2h_stream)
+        slot_used[k] = True
 
     for i in range(args.warmup):
         e2e_step(i)
@@ -490,10 +519,16 @@ def run_ours(args) -> dict | None:
     device_start(world, dev, stream, ev0)
     if hslice is not None:
         hslice.order_after(stream)   # the first step's input copy starts inside the timed region
+    else:
+        cp_stream.wait_stream(stream)
+        d2h_stream.wait_stream(stream)
     for i in range(args.steps):
         e2e_step(i)
     if hslice is not None:
         hslice.join(stream)   # the last step's output copy runs on the host-slice's copy stream
+    else:
+        stream.wait_stream(d2h_stream)
+        stream.wait_stream(cp_stream)
     ev1.record(stream)
     torch.cuda.synchronize()
     ms_e2e = ev0.elapsed_time(ev1)
@@ -697,10 +732,14 @@ def run_prefill(args) -> dict | None:
     recv = torch.empty(world * n_me, HIDDEN, dtype=torch.bfloat16, device=dev) if world > 1 else None
     mine = torch.empty(n_me, HIDDEN, dtype=torch.bfloat16, device=dev) if world > 1 else None
 
-    def step(x, xs, i_, t_) -> None:
-        launch_prefill(view, x, i_, t_, a2, part, a0, a1, ws, x_scale=xs, stream=stream.cuda_stream)
+    def step(x, xs, i_, t_, dst=None) -> None:
+        """One prefill step; its output (N = 1 the slice, N > 1 the combined) goes
+        to `dst` when given, else to `part` (N = 1) or `out` (N > 1)."""
+        launch_prefill(view, x, i_, t_, a2, part if (world > 1 or dst is None) else dst, a0, a1, ws, x_scale=xs,
+                       stream=stream.cuda_stream)
         if world > 1:
-            combine_rows_across_ranks(part, dst=0, out=out, combine=combine_ordered, recv=recv, mine=mine)
+            combine_rows_across_ranks(part, dst=0, out=out if dst is None else dst, combine=combine_ordered,
+                                      recv=recv, mine=mine)
 
     for _ in range(args.warmup):
         step(dq, dinv, dids, dtw)
@@ -752,27 +791,53 @@ def run_prefill(args) -> dict | None:
         rank_step_us = [round(v, 1) for v in gather_floats(ms * 1e3 / args.steps, world, dev)]
         rank_kernel_us = [round(v, 1) for v in gather_floats(k_us, world, dev)]
     # end to end: H2D of the chunk's inputs from pinned memory, D2H of the output
+    # (two slots of device inputs and outputs: a step's input copies run on a copy
+    # stream while the previous step computes, its output copy on a third stream
+    # while the next one computes)
     host = [t_.pin_memory() for t_ in (q, inv, ids, tw)]
-    dev_in = [torch.empty_like(t_, device=dev) for t_ in host]
-    out_h = torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    slot_in = [[torch.empty_like(t_, device=dev) for t_ in host] for _ in range(2)]
+    slot_out = [torch.empty(T, HIDDEN, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    slot_host = [torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     h2d = sum(t_.numel() * t_.element_size() for t_ in host)
-    d2h = out_h.numel() * out_h.element_size()
+    d2h = slot_host[0].numel() * slot_host[0].element_size()
+    cp_stream, d2h_stream = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    slot_used = [False, False]
 
-    def e2e_step() -> None:
-        for d_, h_ in zip(dev_in, host):
-            d_.copy_(h_, non_blocking=True)
-        step(dev_in[0], dev_in[1], dev_in[2], dev_in[3])
+    def e2e_step(i: int) -> None:
+        k = i % 2
+        if slot_used[k]:
+            cp_stream.wait_event(ev_done[k])
+        with torch.cuda.stream(cp_stream):
+            for d_, h_ in zip(slot_in[k], host):
+                d_.copy_(h_, non_blocking=True)
+        ev_in[k].record(cp_stream)
+        stream.wait_event(ev_in[k])
+        if slot_used[k] and rank == 0:
+            stream.wait_event(ev_out[k])
+        step(slot_in[k][0], slot_in[k][1], slot_in[k][2], slot_in[k][3], dst=slot_out[k])
+        ev_done[k].record(stream)
         if rank == 0:
-            out_h.copy_(out if world > 1 else part, non_blocking=True)
+            d2h_stream.wait_event(ev_done[k])
+            with torch.cuda.stream(d2h_stream):
+                slot_host[k].copy_(slot_out[k], non_blocking=True)
+            ev_out[k].record(d2h_stream)
+        slot_used[k] = True
 
-    for _ in range(args.warmup):
-        e2e_step()
+    for i in range(args.warmup):
+        e2e_step(i)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     device_start(world, dev, stream, ev0)
-    for _ in range(args.steps):
-        e2e_step()
+    cp_stream.wait_stream(stream)
+    d2h_stream.wait_stream(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    stream.wait_stream(d2h_stream)
+    stream.wait_stream(cp_stream)
     ev1.record(stream)
     torch.cuda.synchronize()
     ms_e2e = ev0.elapsed_time(ev1)
