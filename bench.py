@@ -731,6 +731,7 @@ def run_prefill(args) -> dict | None:
     n_me = (row_bounds(T, world)[rank + 1] - row_bounds(T, world)[rank]) if world > 1 else 0
     recv = torch.empty(world * n_me, HIDDEN, dtype=torch.bfloat16, device=dev) if world > 1 else None
     mine = torch.empty(n_me, HIDDEN, dtype=torch.bfloat16, device=dev) if world > 1 else None
+    spare = torch.empty(T, HIDDEN, dtype=torch.bfloat16, device=dev) if world > 1 and rank != 0 else None
 
     def step(x, xs, i_, t_, dst=None) -> None:
         """One prefill step; its output (N = 1 the slice, N > 1 the combined) goes
@@ -739,7 +740,7 @@ def run_prefill(args) -> dict | None:
                        stream=stream.cuda_stream)
         if world > 1:
             combine_rows_across_ranks(part, dst=0, out=out if dst is None else dst, combine=combine_ordered,
-                                      recv=recv, mine=mine)
+                                      recv=recv, mine=mine, spare=spare)
 
     for _ in range(args.warmup):
         step(dq, dinv, dids, dtw)
@@ -866,7 +867,7 @@ def run_prefill(args) -> dict | None:
                        "a2": PREFILL_A2, "l2": f"inputs larger than L2: {alg_bytes / 1e9:.2f} GB of expert weights per step",
                        "parallelism": f"column-split tp{world}",
                        "exchange": None if world == 1 else "row-split combine: NCCL all-to-all of row blocks, "
-                                   "per-rank ordered FP32 sums (qx_combine_ordered), blocks sent to rank 0",
+                                   "per-rank ordered FP32 sums (qx_combine_ordered), blocks all-gathered",
                        "kernel": "grouped tcgen05 mxf4nvf4 (NVFP4 x NVFP4, TMEM accumulators)"},
             "tokens_per_s": round(T / (us * 1e-6), 1),
             "weight_gbs": round(alg_bytes / (us * 1e-6) / 1e9, 1),

@@ -65,14 +65,16 @@ def row_bounds(rows: int, world: int) -> list[int]:
 
 def combine_rows_across_ranks(part: torch.Tensor, group=None, dst: int = 0, out: torch.Tensor | None = None,
                               combine: Callable[..., torch.Tensor] | None = None,
-                              recv: torch.Tensor | None = None, mine: torch.Tensor | None = None
-                              ) -> torch.Tensor | None:
+                              recv: torch.Tensor | None = None, mine: torch.Tensor | None = None,
+                              spare: torch.Tensor | None = None) -> torch.Tensor | None:
     """The rank-ordered FP32 combine of `combine_across_ranks`, split by rows.
 
     For partials of many rows (a prefill chunk): an all-to-all hands rank k rows
     [b[k], b[k+1]) of every rank's partial (`row_bounds`), rank k sums them in
     rank order with one BF16 rounding, and the output rank `dst` collects the
-    combined row blocks (point-to-point). Every element is the same sum in the
+    combined row blocks (an all-gather when the rows divide evenly, the other
+    ranks receiving into `spare` ([rows, 5120]); else point-to-point). Every
+    element is the same sum in the
     same order as in `combine_across_ranks`, so the bytes are identical; each
     rank moves (N-1)/N of one partial and the output rank receives (N-1)/N of
     one output, where the gather brings N-1 whole partials to one rank. Needs
@@ -102,6 +104,13 @@ def combine_rows_across_ranks(part: torch.Tensor, group=None, dst: int = 0, out:
     res = combine(parts, out=target)
     if res is not None and res.data_ptr() != target.data_ptr():
         target.copy_(res)
+    if rows % world == 0:
+        # equal blocks: an all-gather (a collective, at NVLink bandwidth; the other
+        # ranks receive into `spare`) lands them in `out` in rank order
+        if rank != dst and spare is None:
+            spare = torch.empty(rows, hid, dtype=part.dtype, device=part.device)
+        dist.all_gather_into_tensor(out if rank == dst else spare, target, group=group)
+        return out if rank == dst else None
     if rank == dst:
         ops = [dist.P2POp(dist.irecv, out[b[k]:b[k + 1]], k, group) for k in range(world) if k != dst]
     else:

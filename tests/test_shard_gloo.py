@@ -96,11 +96,12 @@ def _rows_worker(rank, world, port, rows, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,rows", [(2, 7), (3, 10)])
+@pytest.mark.parametrize("world,rows", [(2, 7), (3, 10), (2, 8)])
 def test_row_split_combine_equals_gather_combine(world, rows):
     """The row-split combine (all-to-all of row blocks, per-rank ordered sums, the
     blocks collected on the output rank) gives the gather combine's bytes, with
-    row counts that do not divide by the rank count."""
+    row counts that do not divide by the rank count (point-to-point collection)
+    and that do (all-gather collection)."""
     port = 29100 + os.getpid() % 700 + world
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
