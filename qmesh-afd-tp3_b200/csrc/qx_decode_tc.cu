@@ -1097,9 +1097,27 @@ __device__ bool finalize_unit(const Params& p, Smem& S, int u, int tile, int rb,
   if (has) {
     uint8_t* own = xbuf_at(p, p.xrank);
     float s[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int r = 0; r < p.xworld && ok; ++r) {
+    // Every sender's words are requested at once (one round trip for all ranks);
+    // those not yet carrying this call are then polled, in rank order.
+    uint64_t wa[QX_XCHG_MAX_RANKS], wb[QX_XCHG_MAX_RANKS];
+#pragma unroll
+    for (int r = 0; r < QX_XCHG_MAX_RANKS; ++r) {
+      if (r < p.xworld && r != p.xdst) {
+        const uint64_t* w = words_of(own, call, r, p.xrows_max, row, k);
+        wa[r] = ld_relaxed_sys_b64(w);
+        wb[r] = ld_relaxed_sys_b64(w + 1);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < QX_XCHG_MAX_RANKS; ++r) {
+      if (r >= p.xworld || !ok) continue;
       uint2 v = mine;
-      if (r != p.xdst) ok = words_wait(words_of(own, call, r, p.xrows_max, row, k), call, v, status, deadline);
+      if (r != p.xdst) {
+        if ((uint32_t)(wa[r] >> 32) == call && (uint32_t)(wb[r] >> 32) == call)
+          v = make_uint2((uint32_t)wa[r], (uint32_t)wb[r]);
+        else
+          ok = words_wait(words_of(own, call, r, p.xrows_max, row, k), call, v, status, deadline);
+      }
       add4(s, v);
     }
     if (p.xshared) add4(s, *reinterpret_cast<const uint2*>(p.xshared + (size_t)row * p.xshared_stride + k));
