@@ -154,7 +154,11 @@ def make_ingest_fixture(ref: str) -> None:
 
 
 if __name__ == "__main__":
-    _ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    # the reference tree: the first argument that is not an option, else QX_REFERENCE_ROOT
+    _pos = [a for a in sys.argv[1:] if not a.startswith("--")]
+    _ref = _pos[0] if _pos else os.environ.get("QX_REFERENCE_ROOT", "")
+    if not _ref and "--prefill" not in sys.argv:
+        sys.exit("usage: make_golden.py REFERENCE_TREE [--ingest | --prefill] (or set QX_REFERENCE_ROOT)")
     if "--ingest" in sys.argv:
         make_ingest_fixture(_ref)
     elif "--prefill" in sys.argv:
