@@ -760,8 +760,8 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
   uint32_t item = blockIdx.x;         // the first item is static, the rest come from the queue
   uint32_t cl_next = 0, cl_end = 0;   // items claimed and not yet started: [cl_next, cl_end)
   // Routed down items of one or two stages are claimed in batches (of 4 or 2),
-  // so the queue's round trip is paid once per batch; longer items (and the
-  // shared expert's, which come first) one at a time.
+  // so the queue's round trip is paid once per batch, except near the queue's
+  // end; longer items (and the shared expert's, which come first) one at a time.
   const int nst2 = (p.NT + SK - 1) / SK;
   const uint32_t dclaim = nst2 == 1 ? 4u : nst2 == 2 ? 2u : 1u;
   for (;;) {
@@ -848,7 +848,10 @@ __device__ void producer(const Params& p, uint8_t* ring, Smem& S, const GroupS* 
     if (cl_next < cl_end) {
       next = cl_next++;
     } else {
-      claim_k = item >= n1 + n2s ? dclaim : 1u;
+      // batches while more than one batch per CTA is left, then single items,
+      // so the last items spread over the CTAs (a batch would leave up to
+      // dclaim - 1 items of tail on one CTA)
+      claim_k = item >= n1 + n2s && (n1 + n2) - item > dclaim * gridDim.x ? dclaim : 1u;
       claimed = atomicAdd(&p.ctl->work, claim_k);
     }
     bool check = m.kind == 2 && seen_a != m.group;
