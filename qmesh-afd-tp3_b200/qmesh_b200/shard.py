@@ -74,13 +74,13 @@ def combine_rows_across_ranks(part: torch.Tensor, group=None, dst: int = 0, out:
     rank order with one BF16 rounding, and the output rank `dst` collects the
     combined row blocks (an all-gather when the rows divide evenly, the other
     ranks receiving into `spare` ([rows, 5120]); else point-to-point). Every
-    element is the same sum in the
-    same order as in `combine_across_ranks`, so the bytes are identical; each
-    rank moves (N-1)/N of one partial and the output rank receives (N-1)/N of
-    one output, where the gather brings N-1 whole partials to one rank. Needs
-    at least one row per rank. `recv` ([N x rows of this rank's block, 5120])
-    and `mine` ([rows of this rank's block, 5120]) may be passed in to avoid
-    allocating per call. Only `dst` returns the output.
+    element is the same sum in the same order as in `combine_across_ranks`, so
+    the bytes are identical; each rank moves (N-1)/N of one partial and the
+    output rank receives (N-1)/N of one output, where the gather brings N-1
+    whole partials to one rank. Needs at least one row per rank. `recv`
+    ([N x rows of this rank's block, 5120]) and `mine` ([rows of this rank's
+    block, 5120]) may be passed in to avoid allocating per call. Only `dst`
+    returns the output.
     """
     if combine is None:
         from .combine import combine_ordered as combine
