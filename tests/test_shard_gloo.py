@@ -121,6 +121,14 @@ def test_row_split_combine_equals_gather_combine(world, rows):
     assert a is not None and (a == b).all()
 
 
+def test_row_bounds_cover_every_row_once():
+    from qmesh_b200 import shard
+    for rows, world in ((7, 2), (10, 3), (2048, 8), (8, 8)):
+        b = shard.row_bounds(rows, world)
+        assert b[0] == 0 and b[-1] == rows and len(b) == world + 1
+        assert all(b[k + 1] - b[k] in (rows // world, rows // world + 1) for k in range(world))
+
+
 def test_shard_range_rules():
     from qmesh_b200 import shard
     assert [shard.shard_range(r, 8) for r in range(8)][-1] == (2016, 2304)
